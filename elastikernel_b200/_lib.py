@@ -1,0 +1,150 @@
+"""ctypes binding of the C-ABI library ``_ek.so`` (declared in include/elastikernel.h).
+
+This is the only place Python touches native code. There is no CPU fallback:
+if the library is missing, :func:`lib` raises, and every operator that needs
+it fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+EK_OK = 0
+EK_ERR_INVALID = 1
+EK_ERR_CUDA = 2
+EK_ERR_OVERSUB = 3
+EK_ERR_UNSUPPORTED = 4
+EK_ERR_DEVICE = 5
+
+EK_DTYPE_BF16 = 0
+EK_DTYPE_FP16 = 1
+EK_DTYPE_E4M3 = 2
+
+EK_B_KN = 0
+EK_B_NK = 1
+
+EK_STATUS_WAIT_TIMEOUT = 1
+EK_STATUS_BAD_EXPERT = 2
+EK_STATUS_BAD_INDEX = 4
+
+LIB_PATH = Path(__file__).with_name("_ek.so")
+
+_c_int = ctypes.c_int
+_c_vp = ctypes.c_void_p
+_c_size = ctypes.c_size_t
+_c_ip = ctypes.POINTER(ctypes.c_int)
+
+
+class GemmPlan(ctypes.Structure):
+    """Mirror of ``ek_gemm_plan``."""
+
+    _fields_ = [
+        ("bm", _c_int), ("bn", _c_int), ("bk", _c_int),
+        ("tiles_m", _c_int), ("tiles_n", _c_int), ("k_blocks", _c_int),
+        ("num_tiles", _c_int), ("num_dp_tiles", _c_int), ("tail_split", _c_int),
+        ("num_units", _c_int), ("grid", _c_int), ("num_sms", _c_int), ("waves", _c_int),
+        ("wave_efficiency", ctypes.c_double), ("est_us", ctypes.c_double),
+        ("workspace_bytes", _c_size),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "ek_abi_version": (_c_int, []),
+    "ek_last_error": (ctypes.c_char_p, []),
+    "ek_device_status": (_c_int, [_c_int, _c_int, _c_ip]),
+    "ek_device_sm_info": (_c_int, [_c_int, _c_ip, _c_ip, _c_ip, _c_ip, _c_ip]),
+    "ek_gctx_create": (_c_int, [_c_int, _c_ip, _c_int, _c_int, ctypes.POINTER(_c_vp), _c_ip]),
+    "ek_gctx_stream_sm_count": (_c_int, [_c_vp, _c_ip]),
+    "ek_gctx_destroy_all": (_c_int, []),
+    "ek_gctx_fake_driver": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "ek_gemm_plan_make": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                   ctypes.POINTER(GemmPlan)]),
+    "ek_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                         _c_vp, _c_size, _c_vp]),
+    "ek_gemm_fp8": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                             _c_vp, _c_size, _c_vp]),
+    "ek_moe_route": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_moe_max_padded_rows": (ctypes.c_int64, [_c_int, _c_int, _c_int, _c_int]),
+    "ek_moe_permute_scratch_bytes": (_c_size, [_c_int, _c_int, _c_int]),
+    "ek_moe_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int,
+                                _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                _c_int, _c_vp]),
+    "ek_moe_down": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
+                             _c_int, _c_int, _c_int, _c_int, _c_vp]),
+    "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
+    "ek_moe_segment_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                     _c_vp]),
+}
+
+_LIB = None
+_LOCK = threading.Lock()
+
+
+class EKError(RuntimeError):
+    """A C-ABI call returned an error code."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    """Load ``_ek.so`` (once) and declare every exported symbol's signature."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"elastikernel_b200 native library not built ({LIB_PATH}); "
+                    "run `python -m elastikernel_b200.csrc.build`")
+            L = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(L, name, None)
+                if fn is None:
+                    continue
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = L
+    return _LIB
+
+
+def exported_symbols() -> list[str]:
+    """Names declared in the binding table (the header's entry points)."""
+    return list(_SIGNATURES)
+
+
+def last_error() -> str:
+    return lib().ek_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    """Raise for a non-zero status: ValueError for over-subscription (as the
+    reference's green_ctx.py:151-155), RuntimeError otherwise."""
+    if rc == EK_OK:
+        return
+    msg = last_error() or f"error code {rc}"
+    if what:
+        msg = f"{what}: {msg}"
+    if rc == EK_ERR_OVERSUB:
+        raise ValueError(msg)
+    raise EKError(rc, msg)
+
+
+def device_status(dev: int, clear: bool = True) -> int:
+    """Synchronise `dev` and return (and by default clear) the kernels' status word."""
+    v = ctypes.c_int(0)
+    check(lib().ek_device_status(int(dev), 1 if clear else 0, ctypes.byref(v)), "ek_device_status")
+    return v.value
+
+
+def stream_ptr(stream) -> int:
+    """Raw CUstream of a torch stream (0 for the legacy default stream)."""
+    return int(stream.cuda_stream) if stream is not None else 0

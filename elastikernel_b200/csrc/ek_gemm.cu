@@ -1,0 +1,272 @@
+// Dense GEMM entry points: SM-count-aware planning and launch of the
+// persistent tcgen05 kernel (ek_gemm_kernel.cuh).
+//
+// The planner is what replaces the reference's "put NUM_SMS in the Triton
+// autotune key" idea (sm_aware_matmul.py:183-216): for a partition of S SMs it
+// picks the tile width BN and a K-split of the tail wave so that the busiest
+// CTA does as little as possible, using a small analytic cost model of the
+// B200 (tensor rate, per-SM operand feed, HBM). The choice is a deterministic
+// function of (M, N, K, S, dtype); no autotuning runs in the hot path.
+#include <algorithm>
+#include <cmath>
+
+#include "ek_gemm_kernel.cuh"
+#include "ek_internal.h"
+
+namespace ek {
+
+int register_status_reader(int (*fn)(int, int*));
+
+namespace {
+
+int read_status(int clear, int* v) {
+  int rc = check_cuda(cudaMemcpyFromSymbol(v, g_ek_status, sizeof(int)), "read status");
+  if (rc) return rc;
+  if (clear) {
+    int z = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_ek_status, &z, sizeof(int)), "clear status");
+  }
+  return rc;
+}
+const int s_status_reg = register_status_reader(read_status);
+
+// ------------------------------------------------------------ cost model
+struct Machine {
+  double clk_ghz = 1.80;         // SM clock under a dense tensor load
+  double f16_flops_clk = 8192;   // dense bf16/fp16 FLOP per clock per SM
+  double f8_flops_clk = 16384;   // dense e4m3 FLOP per clock per SM
+  double feed_bytes_clk = 100;   // operand bytes per clock per SM (L2 -> SMEM)
+  double hbm_gbs = 6500;         // device HBM bandwidth
+  double hbm_per_sm_gbs = 80;    // bandwidth one SM can draw
+  double launch_us = 2.0;        // fixed launch + prologue cost
+};
+
+struct Candidate {
+  int bn, split, full_waves, tail_tiles;
+  double est_us, eff;
+};
+
+int elem_bytes(int dtype) { return dtype == EK_DTYPE_E4M3 ? 1 : 2; }
+
+Candidate evaluate(int M, int N, int K, int S, int dtype, int bn, int split_force) {
+  Machine mc;
+  const int es = elem_bytes(dtype);
+  const int bk = 128 / es;
+  const int tm = (M + 127) / 128, tn = (N + bn - 1) / bn;
+  const int tiles = tm * tn;
+  const int kb = (K + bk - 1) / bk;
+  const int full = tiles / S;
+  const int R = tiles - full * S;
+  const double flops_clk = dtype == EK_DTYPE_E4M3 ? mc.f8_flops_clk : mc.f16_flops_clk;
+  const double mma_clk = 128.0 * bn * bk * 2.0 / flops_clk;
+  const double feed_clk = (128.0 + bn) * 128.0 / mc.feed_bytes_clk;
+  const double t_kb_us = std::max(mma_clk, feed_clk) / (mc.clk_ghz * 1e3);
+
+  Candidate best{bn, 1, full, R, 1e30, 0};
+  const int max_split = std::min(kb, 16);
+  // A forced split only applies when there is a tail wave to split.
+  if (R == 0) split_force = split_force > 0 ? 1 : 0;
+  for (int s = 1; s <= max_split; ++s) {
+    if (split_force > 0 && s != split_force) continue;
+    if (R == 0 && s > 1) break;
+    if (s > 1 && kb / s < 4) break;  // keep each slice long enough to fill the pipeline
+    const int tail_units = R * s;
+    const int grid = std::min(S, full * S + tail_units);
+    const int tail_waves = (tail_units + S - 1) / S;
+    const int slice_kb = (kb + s - 1) / s;
+    const double busiest_kb = double(full) * kb + double(tail_waves) * slice_kb;
+    double t = busiest_kb * t_kb_us;
+    // epilogue of the last tile is not hidden behind a main loop
+    t += 128.0 * bn * 4 / (mc.feed_bytes_clk * mc.clk_ghz * 1e3);
+    if (s > 1) {
+      // partial tiles: written once, read back once by the reducing slice
+      const double part_bytes = double(R) * s * 128.0 * bn * 4.0 * 2.0;
+      t += part_bytes / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
+    }
+    const double unique = (double(M) * K + double(K) * N) * es + double(M) * N * 2;
+    const double t_hbm = unique / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
+    t = std::max(t, t_hbm) + mc.launch_us;
+    const double eff = (double(tiles) * kb) / (double(grid) * busiest_kb);
+    if (t < best.est_us * 0.999) best = Candidate{bn, s, full, R, t, eff};
+  }
+  return best;
+}
+
+}  // namespace
+
+// Ticket counters of split tiles live in the first kTicketBytes of the
+// workspace. Tail tiles are fewer than the partition's SMs, so the SM count is
+// capped at the number of tickets.
+constexpr size_t kTicketBytes = 4096;
+constexpr int kMaxSms = static_cast<int>(kTicketBytes / 4);
+
+int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split, ek_gemm_plan* out) {
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(EK_ERR_INVALID, "GEMM dims must be positive");
+  if (S <= 0 || S > kMaxSms) return set_error(EK_ERR_INVALID, "num_sms must be in [1, %d], got %d", kMaxSms, S);
+  if (dtype < 0 || dtype > 2) return set_error(EK_ERR_INVALID, "unknown dtype %d", dtype);
+  if (dtype == EK_DTYPE_E4M3 && b_layout != EK_B_NK) return set_error(EK_ERR_UNSUPPORTED, "e4m3 B must be [N,K]");
+  static const int kBNs[4] = {256, 192, 128, 64};
+  Candidate best{0, 1, 0, 0, 1e30, 0};
+  for (int bn : kBNs) {
+    if (force_bn > 0 && bn != force_bn) continue;
+    Candidate c = evaluate(M, N, K, S, dtype, bn, force_split);
+    if (c.est_us < best.est_us * 0.98) best = c;  // prefer wider tiles on near ties
+  }
+  if (best.bn == 0) return set_error(EK_ERR_INVALID, "no tile width matches force_bn=%d force_split=%d", force_bn,
+                                     force_split);
+  const int es = elem_bytes(dtype);
+  ek_gemm_plan p{};
+  p.bm = 128;
+  p.bn = best.bn;
+  p.bk = 128 / es;
+  p.tiles_m = (M + 127) / 128;
+  p.tiles_n = (N + best.bn - 1) / best.bn;
+  p.k_blocks = (K + p.bk - 1) / p.bk;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.tail_split = best.split;
+  p.num_dp_tiles = best.split > 1 ? best.full_waves * S : p.num_tiles;
+  const int tail = p.num_tiles - p.num_dp_tiles;
+  p.num_units = p.num_dp_tiles + tail * best.split;
+  p.grid = std::min(S, p.num_units);
+  p.num_sms = S;
+  p.waves = (p.num_units + p.grid - 1) / p.grid;
+  p.wave_efficiency = best.eff;
+  p.est_us = best.est_us;
+  // Workspace: a fixed ticket region first (so tickets of one shape never land
+  // on another shape's partials in a reused buffer), then the fp32 partials.
+  p.workspace_bytes = best.split > 1 ? kTicketBytes + (size_t)tail * best.split * 128 * best.bn * 4 : 0;
+  *out = p;
+  return EK_OK;
+}
+
+namespace {
+
+template <class Cfg>
+int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& prm, int grid,
+               cudaStream_t stream) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
+  if (!attr_done[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::SMEM_BYTES),
+                        "cudaFuncSetAttribute(smem)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb2, prm);
+  return check_cuda(cudaGetLastError(), "gemm kernel launch");
+}
+
+template <int kElem, bool kBMN, int kEpi>
+int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid,
+              cudaStream_t stream) {
+  switch (bn) {
+    case 64: return launch_cfg<GemmCfg<64, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
+    case 128: return launch_cfg<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
+    case 192: return launch_cfg<GemmCfg<192, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
+    case 256: return launch_cfg<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
+  }
+  return set_error(EK_ERR_UNSUPPORTED, "tile width %d not built", bn);
+}
+
+CUtensorMapDataType tma_dtype(int dtype) {
+  switch (dtype) {
+    case EK_DTYPE_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case EK_DTYPE_FP16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  }
+}
+
+int gemm_common(const void* A, const void* B, void* C, const float* a_scale, const float* b_scale, int M, int N,
+                int K, int dtype, int b_layout, int num_sms, int force_bn, int force_split, void* workspace,
+                size_t ws_bytes, void* stream) {
+  clear_error();
+  if (!A || !B || !C) return set_error(EK_ERR_INVALID, "null operand");
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C))
+    return set_error(EK_ERR_INVALID, "operands must be 16-byte aligned");
+  if (N % 8 != 0 || K % 16 != 0)
+    return set_error(EK_ERR_INVALID, "N must be a multiple of 8 and K of 16 (got N=%d K=%d)", N, K);
+  if (b_layout != EK_B_KN && b_layout != EK_B_NK) return set_error(EK_ERR_INVALID, "bad b_layout");
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  ek_gemm_plan plan;
+  rc = plan_dense(M, N, K, S, dtype, b_layout, force_bn, force_split, &plan);
+  if (rc) return rc;
+  if (plan.workspace_bytes > 0 && (!workspace || ws_bytes < plan.workspace_bytes || !aligned16(workspace)))
+    return set_error(EK_ERR_INVALID, "workspace of %zu bytes required (got %zu)", plan.workspace_bytes, ws_bytes);
+
+  const int es = elem_bytes(dtype);
+  const CUtensorMapDataType tdt = tma_dtype(dtype);
+  CUtensorMap ta, tb;
+  rc = make_tmap_2d(&ta, A, tdt, K, M, (uint64_t)K * es, 128 / es, 128);
+  if (rc) return rc;
+  if (b_layout == EK_B_KN)
+    rc = make_tmap_2d(&tb, B, tdt, N, K, (uint64_t)N * es, 64, 64);  // [K, N]: 64 N x 64 K boxes
+  else
+    rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * es, 128 / es, plan.bn);
+  if (rc) return rc;
+
+  GemmParams prm{};
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.tiles_m = plan.tiles_m;
+  prm.tiles_n = plan.tiles_n;
+  prm.k_blocks = plan.k_blocks;
+  prm.num_dp_tiles = plan.num_dp_tiles;
+  prm.tail_split = plan.tail_split;
+  prm.num_units = plan.num_units;
+  prm.group_m = 8;
+  prm.C = C;
+  prm.ldc = N;
+  prm.a_scale = a_scale;
+  prm.b_scale = b_scale;
+  if (plan.workspace_bytes > 0) {
+    const int tail = plan.num_tiles - plan.num_dp_tiles;
+    prm.ws_counters = static_cast<int*>(workspace);
+    prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+    (void)tail;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == EK_DTYPE_E4M3) return launch_bn<kE4M3, false, kEpiRowColScale>(plan.bn, ta, tb, prm, plan.grid, s);
+  if (dtype == EK_DTYPE_BF16) {
+    if (b_layout == EK_B_KN) return launch_bn<kBF16, true, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+    return launch_bn<kBF16, false, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+  }
+  if (b_layout == EK_B_KN) return launch_bn<kFP16, true, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+  return launch_bn<kFP16, false, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+}
+
+}  // namespace
+}  // namespace ek
+
+using namespace ek;
+
+extern "C" {
+
+int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
+                      ek_gemm_plan* out) {
+  clear_error();
+  if (!out) return set_error(EK_ERR_INVALID, "null plan");
+  return plan_dense(M, N, K, num_sms, dtype, b_layout, force_bn, force_split, out);
+}
+
+int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,
+            int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream) {
+  if (dtype != EK_DTYPE_BF16 && dtype != EK_DTYPE_FP16)
+    return set_error(EK_ERR_INVALID, "ek_gemm takes bf16 or fp16 (got dtype %d)", dtype);
+  return gemm_common(A, B, C, nullptr, nullptr, M, N, K, dtype, b_layout, num_sms, force_bn, force_split, workspace,
+                     ws_bytes, stream);
+}
+
+int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float* w_scale, void* C, int M, int N,
+                int K, int num_sms, int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream) {
+  if (!a_scale || !w_scale) return set_error(EK_ERR_INVALID, "null scales");
+  return gemm_common(A, W, C, a_scale, w_scale, M, N, K, EK_DTYPE_E4M3, EK_B_NK, num_sms, force_bn, force_split,
+                     workspace, ws_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,497 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   warp 0      TMA producer (one lane): A and B tiles into a ring of stages
+//   warp 1      TMEM allocator + MMA issuer (one lane): 128 x BN x K tiles
+//               into one of two TMEM accumulators
+//   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> global
+//
+// The grid is the partition's SM count (or fewer CTAs when there is less
+// work); CTA c runs work units c, c + grid, c + 2*grid, ... A unit is one
+// output tile, or one K-slice of a tile when the schedule splits the tail
+// wave (stream-K style). Split slices write fp32 partials to a caller-owned
+// workspace and the last slice to finish (atomic ticket) sums them in slice
+// order, so results do not depend on arrival order.
+//
+// Three schedules share the main loop:
+//   kSchedDense    dense GEMM, grouped rasterisation, optional tail split
+//   kSchedBlocks   MoE grouped GEMM over the padded expert-sorted rows: row
+//                  block b uses expert block_expert[b]; rows past
+//                  *num_rows_padded are skipped
+//   kSchedSegments the reference's CSR segment GEMM: expert e owns rows
+//                  [offsets[e], offsets[e+1])
+#pragma once
+#include "ek_ptx.cuh"
+
+namespace ek {
+
+enum Elem : int { kBF16 = 0, kFP16 = 1, kE4M3 = 2 };
+enum Epi : int { kEpiStore = 0, kEpiRowColScale = 1, kEpiSwiGLU = 2, kEpiWeightedScatter = 3 };
+enum Sched : int { kSchedDense = 0, kSchedBlocks = 1, kSchedSegments = 2 };
+
+template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int kElem = kElem_;
+  static constexpr bool kBMN = kBMN_;  // B stored MN-major ([K, N] row-major)
+  static constexpr int kEpi = kEpi_;
+  static constexpr int kSched = kSched_;
+  static constexpr bool kF8 = (kElem == kE4M3);
+  static constexpr int ES = kF8 ? 1 : 2;   // bytes per element
+  static constexpr int BK = 128 / ES;      // one 128-byte swizzle row of K
+  static constexpr int UK = 32 / ES;       // K of one MMA instruction
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BUDGET = 220 * 1024;
+  static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, 128, BN);
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int THREADS = 192;
+  static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(!(kF8 && kBMN), "e4m3 B must be K-major");
+  static_assert(STAGES >= 2, "not enough shared memory for two stages");
+};
+
+struct GemmParams {
+  int M, N, K;            // output rows (upper bound for grouped), output width, reduction
+  int tiles_m, tiles_n, k_blocks;
+  int num_dp_tiles;       // dense: tiles computed whole
+  int tail_split;         // dense: K-split of the remaining tiles
+  int num_units;          // dense / segments: unit count
+  int group_m;            // rasterisation group (tile rows)
+  void* C;                // output
+  int ldc;                // output row stride (elements)
+  const float* a_scale;   // kEpiRowColScale
+  const float* b_scale;
+  // grouped (kSchedBlocks)
+  const int* block_expert;
+  const int* num_rows_ptr;
+  int num_experts;
+  int b_rows_per_expert;  // rows of the flattened weight per expert
+  const int* sorted_slots;
+  const float* slot_weights;
+  int num_slots;          // T * topk (sentinel)
+  // segments (kSchedSegments)
+  const int* seg_offsets;
+  int seg_mblocks;        // row blocks per expert (upper bound)
+  // split-K workspace
+  float* ws_partial;
+  int* ws_counters;
+};
+
+struct Unit {
+  int tm, tn;       // tile coordinates
+  int kb0, kb1;     // K-block range
+  int split, nsplit;
+  int tail_slot;    // index into the split workspace (dense tail tiles)
+  int a_row;        // first A row of the tile
+  int row_end;      // rows >= row_end are not stored
+  int b_row;        // first B row (K-major) / first K row offset (MN-major)
+  int b_col;        // first B column (MN-major)
+  bool valid;
+};
+
+__device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
+  const int group_size = group_m * tiles_n;
+  const int g = tile / group_size;
+  const int first_m = g * group_m;
+  const int gm = min(tiles_m - first_m, group_m);
+  const int r = tile - g * group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <class Cfg>
+__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows_runtime) {
+  Unit w;
+  w.valid = true;
+  w.split = 0;
+  w.nsplit = 1;
+  w.tail_slot = -1;
+  w.kb0 = 0;
+  w.kb1 = p.k_blocks;
+  if constexpr (Cfg::kSched == kSchedDense) {
+    int tile = u;
+    if (u >= p.num_dp_tiles) {
+      const int v = u - p.num_dp_tiles;
+      tile = p.num_dp_tiles + v / p.tail_split;
+      w.split = v % p.tail_split;
+      w.nsplit = p.tail_split;
+      w.tail_slot = tile - p.num_dp_tiles;
+      w.kb0 = (int)((long long)w.split * p.k_blocks / w.nsplit);
+      w.kb1 = (int)((long long)(w.split + 1) * p.k_blocks / w.nsplit);
+    }
+    raster(tile, p.tiles_m, p.tiles_n, p.group_m, w.tm, w.tn);
+    w.a_row = w.tm * Cfg::BM;
+    w.row_end = p.M;
+    // K-major B: tile rows are output columns. MN-major B: rows are K, so the
+    // tile starts at K row 0 and column tn*BN.
+    w.b_row = Cfg::kBMN ? 0 : w.tn * Cfg::BN;
+    w.b_col = w.tn * Cfg::BN;
+  } else if constexpr (Cfg::kSched == kSchedBlocks) {
+    const int mblocks = rows_runtime / Cfg::BM;
+    raster(u, mblocks, p.tiles_n, p.group_m, w.tm, w.tn);
+    w.a_row = w.tm * Cfg::BM;
+    w.row_end = rows_runtime;
+    const int e = p.block_expert[w.tm];
+    if (e < 0 || e >= p.num_experts) {
+      w.valid = false;
+      if (e >= p.num_experts) atomicOr(&g_ek_status, kStatusBadExpert);
+    }
+    const int bn_rows = (Cfg::kEpi == kEpiSwiGLU) ? Cfg::BN / 2 : Cfg::BN;
+    w.b_row = e * p.b_rows_per_expert + w.tn * bn_rows;
+    w.b_col = 0;
+  } else {  // kSchedSegments
+    const int per_e = p.seg_mblocks * p.tiles_n;
+    const int e = u / per_e;
+    const int r = u - e * per_e;
+    const int mb = r / p.tiles_n;
+    w.tn = r - mb * p.tiles_n;
+    const int s0 = p.seg_offsets[e];
+    const int s1 = p.seg_offsets[e + 1];
+    w.a_row = s0 + mb * Cfg::BM;
+    w.row_end = min(s1, p.M);
+    w.tm = 0;
+    w.valid = (s1 > s0) && (w.a_row < w.row_end);
+    w.b_row = e * p.N;  // K-row offset of the expert block in the [E*N, K] weight
+    w.b_col = w.tn * Cfg::BN;
+  }
+  return w;
+}
+
+// Runtime unit count (grouped GEMMs read the padded row count from device).
+template <class Cfg>
+__device__ __forceinline__ int unit_count(const GemmParams& p, int& rows_runtime) {
+  if constexpr (Cfg::kSched == kSchedBlocks) {
+    int r = *p.num_rows_ptr;
+    r = max(0, min(r, p.M));
+    rows_runtime = r;
+    return (r / Cfg::BM) * p.tiles_n;
+  } else {
+    rows_runtime = p.M;
+    return p.num_units;
+  }
+}
+
+template <class Cfg>
+__device__ __forceinline__ void store_out_chunk(const GemmParams& p, int row, int col0, const float (&v)[32]) {
+  // 32 consecutive output columns of one row; N is a multiple of 8.
+  if constexpr (Cfg::kEpi == kEpiWeightedScatter || Cfg::kElem == kBF16 || Cfg::kElem == kE4M3 ||
+                Cfg::kEpi == kEpiSwiGLU) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < p.N) {
+        uint4 pk;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[g * 8 + 0], v[g * 8 + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[g * 8 + 2], v[g * 8 + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[g * 8 + 4], v[g * 8 + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[g * 8 + 6], v[g * 8 + 7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(out + g * 8) = pk;
+      }
+    }
+  } else {
+    __half* out = reinterpret_cast<__half*>(p.C) + (size_t)row * p.ldc + col0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < p.N) {
+        uint4 pk;
+        __half2 h0 = __floats2half2_rn(v[g * 8 + 0], v[g * 8 + 1]);
+        __half2 h1 = __floats2half2_rn(v[g * 8 + 2], v[g * 8 + 3]);
+        __half2 h2 = __floats2half2_rn(v[g * 8 + 4], v[g * 8 + 5]);
+        __half2 h3 = __floats2half2_rn(v[g * 8 + 6], v[g * 8 + 7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(out + g * 8) = pk;
+      }
+    }
+  }
+}
+
+// Final epilogue math for 32 accumulator columns [col0, col0+32) of `row`.
+template <class Cfg>
+__device__ __forceinline__ void finish_chunk(const GemmParams& p, int row, int col0, float (&v)[32]) {
+  if constexpr (Cfg::kEpi == kEpiRowColScale) {
+    const float sa = p.a_scale[row];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int c = col0 + j;
+      const float sb = (c < p.N) ? p.b_scale[c] : 0.f;
+      v[j] = v[j] * sa * sb;
+    }
+  }
+  store_out_chunk<Cfg>(p, row, col0, v);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, UK = Cfg::UK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
+  uint64_t* drain_bar = bars + 2 * STAGES + 4;
+  uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem_base + 1);
+  volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem_base + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *s_abort = 0;
+    *s_last = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem_base;
+
+  int rows_rt = 0;
+  const int nunits = unit_count<Cfg>(p, rows_rt);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      if constexpr (Cfg::kEpi == kEpiSwiGLU) tma_prefetch_desc(&tmB2);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+        if (!w.valid) continue;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
+          uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
+          tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+          if constexpr (Cfg::kBMN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
+          } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+            tma_load_2d(b_dst + (BN / 2) * 128, &tmB2, &full_bar[stage], kb * BK, w.b_row);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc_i = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+        if (!w.valid) continue;
+        const int buf = acc_i & 1;
+        const uint32_t aphase = (acc_i >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[buf], aphase ^ 1, s_abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, s_abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+            uint64_t bd;
+            if constexpr (Cfg::kBMN)
+              bd = umma_desc_sw128(b0 + k * UK * 128, BK * 128, 1024);
+            else
+              bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
+            umma<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, (kb > w.kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[buf]);
+        ++acc_i;
+      }
+      // Drain: wait until every MMA this thread issued has completed before the
+      // TMEM is released (also on the abort path).
+      umma_commit(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    const int epi_tid = threadIdx.x - 64;
+    int acc_i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+      if (!w.valid) continue;
+      const int buf = acc_i & 1;
+      const uint32_t aphase = (acc_i >> 1) & 1;
+      const bool got = mbar_wait(&tfull_bar[buf], aphase, s_abort);
+      if (named_bar_red_or(1, 128, got ? 0 : 1)) break;  // uniform across the 128 threads
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      const int row = w.a_row + row_in_tile;
+      const bool row_ok = row < w.row_end;
+
+      if constexpr (Cfg::kEpi == kEpiSwiGLU) {
+        // columns [0, BN/2) hold x.w1 (gate input), [BN/2, BN) hold x.w3
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(t_row + c * 32, rg);
+          tmem_ld32(t_row + BN / 2 + c * 32, ru);
+          tmem_ld_wait(rg);
+          reg_dep(ru);
+          if (c == BN / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+          }
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(rg[j])) * __uint_as_float(ru[j]);
+          if (row_ok) store_out_chunk<Cfg>(p, row, w.tn * (BN / 2) + c * 32, v);
+        }
+      } else if constexpr (Cfg::kEpi == kEpiWeightedScatter) {
+        int slot = p.num_slots;
+        if (row_ok) slot = p.sorted_slots[row];
+        const bool keep = row_ok && slot >= 0 && slot < p.num_slots;
+        const float wt = keep ? p.slot_weights[slot] : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
+          tmem_ld_wait(r);
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+          }
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * wt;
+          if (keep) store_out_chunk<Cfg>(p, slot, w.tn * BN + c * 32, v);
+        }
+      } else {
+        const int col_base = (Cfg::kSched == kSchedSegments) ? w.b_col : w.tn * BN;
+        if (w.nsplit == 1) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c * 32, r);
+            tmem_ld_wait(r);
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&tempty_bar[buf]);
+            }
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (row_ok) finish_chunk<Cfg>(p, row, col_base + c * 32, v);
+          }
+        } else {
+          // K-split slice: write the fp32 partial, take a ticket, and let the
+          // last slice reduce all partials in slice order.
+          float* part = p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + w.split) * BM + row_in_tile) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c * 32, r);
+            tmem_ld_wait(r);
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&tempty_bar[buf]);
+            }
+            float4* dst = reinterpret_cast<float4*>(part + c * 32);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              __stcg(dst + g, make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                          __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+          }
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (epi_tid == 0) {
+            const int old = atomicAdd(&p.ws_counters[w.tail_slot], 1);
+            const int last = (old == w.nsplit - 1);
+            if (last) p.ws_counters[w.tail_slot] = 0;  // ready for the next launch
+            *s_last = last;
+          }
+          named_bar_sync(1, 128);
+          if (*s_last) {
+            __threadfence();
+            const float* part0 = p.ws_partial + ((size_t)(w.tail_slot * w.nsplit) * BM + row_in_tile) * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              for (int s = 0; s < w.nsplit; ++s) {
+                const float4* src = reinterpret_cast<const float4*>(part0 + (size_t)s * BM * BN + c * 32);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  const float4 t = __ldcg(src + g);
+                  v[4 * g] += t.x;
+                  v[4 * g + 1] += t.y;
+                  v[4 * g + 2] += t.z;
+                  v[4 * g + 3] += t.w;
+                }
+              }
+              if (row_ok) finish_chunk<Cfg>(p, row, col_base + c * 32, v);
+            }
+          }
+        }
+      }
+      ++acc_i;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace ek

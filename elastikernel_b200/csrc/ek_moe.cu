@@ -1,0 +1,514 @@
+// Fused-MoE stages for sm_100a.
+//
+//   route      softmax + top-k + renormalise, one warp per token
+//              (sm_aware_agent/definition.py:152-153)
+//   permute    count -> scan -> stable scatter of the (token, choice) slots
+//              into an expert-sorted layout padded to 128-row blocks, with the
+//              token rows gathered into that layout on the way
+//   gate_up    grouped tcgen05 GEMM over the padded rows with the SwiGLU
+//              epilogue silu(x.w1) * (x.w3) (definition.py:163-165)
+//   down       grouped tcgen05 GEMM with the routing weight applied in the
+//              epilogue and rows scattered back to their slots (:166-168)
+//   combine    out[t] = sum_j y[t*k + j] in j order (:168)
+//   segment    the reference's CSR segment GEMM (sm_aware_benchmark.py:228-290)
+#include <algorithm>
+#include <cfloat>
+
+#include "ek_gemm_kernel.cuh"
+#include "ek_internal.h"
+
+namespace ek {
+
+int register_status_reader(int (*fn)(int, int*));
+
+namespace {
+
+int read_status(int clear, int* v) {
+  int rc = check_cuda(cudaMemcpyFromSymbol(v, g_ek_status, sizeof(int)), "read status");
+  if (rc) return rc;
+  if (clear) {
+    int z = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_ek_status, &z, sizeof(int)), "clear status");
+  }
+  return rc;
+}
+const int s_status_reg = register_status_reader(read_status);
+
+constexpr int kRouteMaxE = 256;   // logits per token held in registers: 8 per lane
+constexpr int kRouteMaxK = 8;
+constexpr int kPermChunk = 1024;  // slots per permutation CTA
+constexpr int kPermMaxE = 1024;
+
+// ------------------------------------------------------------------ routing
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                                    int* __restrict__ ids, float* __restrict__ wts) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* row = logits + (size_t)t * E;
+  float v[kRouteMaxE / 32];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kRouteMaxE / 32; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? row[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRouteMaxE / 32; ++i)
+    if (lane + 32 * i < E) s += expf(v[i] - mx);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+
+  // Selection on the logits (softmax is monotone): largest first, ties to the
+  // lower expert id.
+  uint32_t taken = 0;
+  float p[kRouteMaxK];
+  int sel[kRouteMaxK];
+  float psum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kRouteMaxK; ++j) {
+    if (j >= k) break;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kRouteMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !(taken & (1u << i)) && (v[i] > bv || (v[i] == bv && e < bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    sel[j] = bi;
+    p[j] = expf(bv - mx) / s;
+    psum += p[j];
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < kRouteMaxK; ++j) {
+      if (j >= k) break;
+      ids[(size_t)t * k + j] = sel[j];
+      wts[(size_t)t * k + j] = p[j] / psum;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ permutation
+__global__ void __launch_bounds__(kPermChunk) permute_count_kernel(const int* __restrict__ ids, int n_slots, int E,
+                                                                   int* __restrict__ chunk_counts) {
+  extern __shared__ int cnt[];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int s = blockIdx.x * kPermChunk + threadIdx.x;
+  if (s < n_slots) {
+    const int e = ids[s];
+    if (e >= 0 && e < E)
+      atomicAdd(&cnt[e], 1);
+    else
+      atomicOr(&g_ek_status, kStatusBadIndex);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x) chunk_counts[(size_t)blockIdx.x * E + i] = cnt[i];
+}
+
+__global__ void __launch_bounds__(kPermChunk)
+    permute_scatter_kernel(const int* __restrict__ ids, int n_slots, int E, int topk, int block_m,
+                           const int* __restrict__ chunk_counts, int n_chunks, int* __restrict__ sorted_slots,
+                           int* __restrict__ block_expert, int* __restrict__ num_rows_padded,
+                           int* __restrict__ expert_counts, int max_rows, const uint8_t* __restrict__ x,
+                           int row_bytes, uint8_t* __restrict__ x_perm) {
+  extern __shared__ int sm[];
+  int* s_tot = sm;              // [E] slots per expert (all chunks)
+  int* s_before = sm + E;       // [E] slots per expert in earlier chunks
+  int* s_start = sm + 2 * E;    // [E] first padded row of each expert
+  int* s_wcnt = sm + 3 * E;     // [32][E] per-warp counts of this chunk
+  int* s_dest = s_wcnt + 32 * E;  // [kPermChunk] destination row per thread
+  __shared__ int s_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  for (int e = tid; e < E; e += blockDim.x) {
+    int tot = 0, before = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int v = chunk_counts[(size_t)c * E + e];
+      tot += v;
+      if (c < (int)blockIdx.x) before += v;
+    }
+    s_tot[e] = tot;
+    s_before[e] = before;
+  }
+  for (int i = tid; i < 32 * E; i += blockDim.x) s_wcnt[i] = 0;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      s_start[e] = acc;
+      acc += (s_tot[e] + block_m - 1) / block_m * block_m;
+    }
+    s_total = acc;
+  }
+  __syncthreads();
+
+  if (blockIdx.x == 0) {
+    const int total = s_total;
+    for (int e = tid; e < E; e += blockDim.x) expert_counts[e] = s_tot[e];
+    if (tid == 0) *num_rows_padded = total;
+    // sentinel in each expert's padding rows and past the used rows
+    for (int e = warp; e < E; e += blockDim.x / 32) {
+      const int padded = (s_tot[e] + block_m - 1) / block_m * block_m;
+      for (int r = s_start[e] + s_tot[e] + lane; r < s_start[e] + padded; r += 32) sorted_slots[r] = n_slots;
+    }
+    for (int r = total + tid; r < max_rows; r += blockDim.x) sorted_slots[r] = n_slots;
+    const int nblocks = max_rows / block_m;
+    for (int b = tid; b < nblocks; b += blockDim.x) {
+      const int r = b * block_m;
+      int ex = -1;
+      if (r < total) {
+        int lo = 0, hi = E - 1;  // last expert with start <= r
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_start[mid] <= r) lo = mid; else hi = mid - 1;
+        }
+        ex = lo;
+      }
+      block_expert[b] = ex;
+    }
+  }
+
+  // stable rank of each slot inside this chunk: warp-level match, then the
+  // counts of earlier warps
+  const int s = blockIdx.x * kPermChunk + tid;
+  int e = (s < n_slots) ? ids[s] : -1;
+  const bool valid = (e >= 0 && e < E);
+  if (!valid) e = -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank_w = __popc(peers & ((1u << lane) - 1u));
+  if (valid && (__ffs(peers) - 1) == lane) s_wcnt[warp * E + e] = __popc(peers);
+  __syncthreads();
+  int dest = -1;
+  if (valid) {
+    int pre = 0;
+    for (int w = 0; w < warp; ++w) pre += s_wcnt[w * E + e];
+    dest = s_start[e] + s_before[e] + pre + rank_w;
+    sorted_slots[dest] = s;
+  }
+  s_dest[tid] = dest;
+  if (x == nullptr) return;
+  __syncthreads();
+  // gather the token rows of this chunk into their padded rows
+  const int nvec = row_bytes / 16;
+  for (int i = warp; i < kPermChunk; i += blockDim.x / 32) {
+    const int d = s_dest[i];
+    if (d < 0) continue;
+    const int tok = (blockIdx.x * kPermChunk + i) / topk;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)d * row_bytes);
+    for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
+  }
+}
+
+// ------------------------------------------------------------------ combine
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ out, int T, int k,
+                               int H) {
+  const int chunks = H / 8;
+  const long long total = (long long)T * chunks;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(idx / chunks);
+    const int c = (int)(idx - (long long)t * chunks) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + ((size_t)t * k + j) * H + c));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = o;
+  }
+}
+
+// ------------------------------------------------------------------ grouped GEMM launch
+template <class Cfg>
+int launch_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& prm,
+                   int grid, cudaStream_t stream) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
+  if (!attr_done[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::SMEM_BYTES),
+                        "cudaFuncSetAttribute(smem)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  if (grid <= 0) return EK_OK;
+  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb2, prm);
+  return check_cuda(cudaGetLastError(), "grouped gemm launch");
+}
+
+// Tile width for a grouped GEMM: balance the units of the expected number of
+// row blocks over the partition, weighing each unit by its operand bytes.
+int grouped_bn(int est_mblocks, int out_cols, int K, int S, bool swiglu) {
+  static const int kBNs[4] = {256, 192, 128, 64};
+  int best = 256;
+  double best_cost = 1e300;
+  for (int bn : kBNs) {
+    const int cols = swiglu ? bn / 2 : bn;
+    const long long tiles_n = (out_cols + cols - 1) / cols;
+    const long long units = (long long)est_mblocks * tiles_n;
+    const long long per_cta = (units + S - 1) / S;
+    // clocks per unit: operand feed (bf16 A + B tiles at ~100 B/clk/SM) vs
+    // tensor work (8192 FLOP/clk/SM); the busiest CTA sets the time
+    const double feed_clk = (128.0 + bn) * K * 2.0 / 100.0;
+    const double mma_clk = 128.0 * bn * K * 2.0 / 8192.0;
+    const double cost = per_cta * std::max(feed_clk, mma_clk);
+    if (cost < best_cost * 0.98) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+}  // namespace ek
+
+using namespace ek;
+
+extern "C" {
+
+int ek_moe_route(const float* logits, int T, int E, int topk, int* topk_ids, float* topk_weights, void* stream) {
+  clear_error();
+  if (T < 0 || E < 1 || E > kRouteMaxE || topk < 1 || topk > kRouteMaxK || topk > E)
+    return set_error(EK_ERR_INVALID, "route: need 1 <= E <= %d and 1 <= k <= min(%d, E) (E=%d k=%d)", kRouteMaxE,
+                     kRouteMaxK, E, topk);
+  if (T == 0) return EK_OK;
+  if (!logits || !topk_ids || !topk_weights) return set_error(EK_ERR_INVALID, "route: null pointer");
+  const int threads = 256;
+  const long long blocks = ((long long)T * 32 + threads - 1) / threads;
+  route_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(logits, T, E, topk, topk_ids,
+                                                                                   topk_weights);
+  return check_cuda(cudaGetLastError(), "route launch");
+}
+
+int64_t ek_moe_max_padded_rows(int T, int topk, int E, int block_m) {
+  if (T < 0 || topk < 1 || E < 1 || block_m < 1) return -1;
+  const int64_t n = (int64_t)T * topk + (int64_t)E * (block_m - 1);
+  return (n + block_m - 1) / block_m * block_m;
+}
+
+size_t ek_moe_permute_scratch_bytes(int T, int topk, int E) {
+  if (T < 0 || topk < 1 || E < 1) return 0;
+  const size_t chunks = ((size_t)T * topk + kPermChunk - 1) / kPermChunk;
+  return std::max<size_t>(chunks, 1) * E * sizeof(int);
+}
+
+int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int* sorted_slots, int* block_expert,
+                   int* num_rows_padded, int* expert_counts, const void* x, int H, int elem_bytes, void* x_perm,
+                   void* scratch, void* stream) {
+  clear_error();
+  if (T < 0 || topk < 1 || E < 1 || E > kPermMaxE || block_m < 1)
+    return set_error(EK_ERR_INVALID, "permute: bad sizes (T=%d k=%d E=%d block_m=%d)", T, topk, E, block_m);
+  if (!topk_ids || !sorted_slots || !block_expert || !num_rows_padded || !expert_counts || !scratch)
+    return set_error(EK_ERR_INVALID, "permute: null pointer");
+  const int row_bytes = H * elem_bytes;
+  if (x) {
+    if (!x_perm || H <= 0 || elem_bytes <= 0 || row_bytes % 16 != 0 || !aligned16(x) || !aligned16(x_perm))
+      return set_error(EK_ERR_INVALID, "permute: gathered rows must be 16-byte multiples on 16-byte aligned buffers");
+  }
+  const long long n_slots = (long long)T * topk;
+  if (n_slots > (1ll << 30)) return set_error(EK_ERR_INVALID, "permute: too many slots");
+  const int64_t max_rows = ek_moe_max_padded_rows(T, topk, E, block_m);
+  const int n_chunks = (int)std::max<long long>((n_slots + kPermChunk - 1) / kPermChunk, 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* chunk_counts = static_cast<int*>(scratch);
+  permute_count_kernel<<<n_chunks, kPermChunk, E * sizeof(int), s>>>(topk_ids, (int)n_slots, E, chunk_counts);
+  int rc = check_cuda(cudaGetLastError(), "permute count launch");
+  if (rc) return rc;
+  const size_t smem = (size_t)(3 * E + 32 * E + kPermChunk) * sizeof(int);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    rc = check_cuda(cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)((3 * kPermMaxE + 32 * kPermMaxE + kPermChunk) * sizeof(int))),
+                    "cudaFuncSetAttribute(permute)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  permute_scatter_kernel<<<n_chunks, kPermChunk, smem, s>>>(
+      topk_ids, (int)n_slots, E, topk, block_m, chunk_counts, n_chunks, sorted_slots, block_expert, num_rows_padded,
+      expert_counts, (int)max_rows, static_cast<const uint8_t*>(x), row_bytes, static_cast<uint8_t*>(x_perm));
+  return check_cuda(cudaGetLastError(), "permute scatter launch");
+}
+
+int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
+                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_sms,
+                   int force_bn, void* stream) {
+  clear_error();
+  if (!x_perm || !w1 || !w3 || !block_expert || !num_rows_padded || !act)
+    return set_error(EK_ERR_INVALID, "gate_up: null pointer");
+  if (max_rows % 128 != 0 || E < 1 || H % 16 != 0 || I % 8 != 0 || H <= 0 || I <= 0)
+    return set_error(EK_ERR_INVALID, "gate_up: max_rows %% 128, H %% 16 and I %% 8 must be 0");
+  if (!aligned16(x_perm) || !aligned16(w1) || !aligned16(w3) || !aligned16(act))
+    return set_error(EK_ERR_INVALID, "gate_up: buffers must be 16-byte aligned");
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  const int mblocks = max_rows / 128;
+  const int bn = force_bn > 0 ? force_bn : grouped_bn(mblocks, I, H, S, true);
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
+  CUtensorMap ta, tb, tb2;
+  if ((rc = make_tmap_2d(&ta, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, max_rows, (uint64_t)H * 2, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&tb, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, bn / 2)))
+    return rc;
+  if ((rc = make_tmap_2d(&tb2, w3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, bn / 2)))
+    return rc;
+  GemmParams p{};
+  p.M = max_rows;
+  p.N = I;
+  p.K = H;
+  p.tiles_n = (I + bn / 2 - 1) / (bn / 2);
+  p.tiles_m = mblocks;
+  p.k_blocks = (H + 63) / 64;
+  p.group_m = 8;
+  p.C = act;
+  p.ldc = I;
+  p.block_expert = block_expert;
+  p.num_rows_ptr = num_rows_padded;
+  p.num_experts = E;
+  p.b_rows_per_expert = I;
+  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 64: return launch_grouped<GemmCfg<64, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
+    case 128: return launch_grouped<GemmCfg<128, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
+    case 192: return launch_grouped<GemmCfg<192, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
+    default: return launch_grouped<GemmCfg<256, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
+  }
+}
+
+int ek_moe_down(const void* act, const void* w2, const int* block_expert, const int* num_rows_padded,
+                const int* sorted_slots, const float* topk_weights, void* y, int max_rows, int E, int H, int I, int T,
+                int topk, int num_sms, int force_bn, void* stream) {
+  clear_error();
+  if (!act || !w2 || !block_expert || !num_rows_padded || !sorted_slots || !topk_weights || !y)
+    return set_error(EK_ERR_INVALID, "down: null pointer");
+  if (max_rows % 128 != 0 || E < 1 || I % 16 != 0 || H % 8 != 0 || H <= 0 || I <= 0 || T < 0 || topk < 1)
+    return set_error(EK_ERR_INVALID, "down: max_rows %% 128, I %% 16 and H %% 8 must be 0");
+  if (!aligned16(act) || !aligned16(w2) || !aligned16(y))
+    return set_error(EK_ERR_INVALID, "down: buffers must be 16-byte aligned");
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  const int mblocks = max_rows / 128;
+  const int bn = force_bn > 0 ? force_bn : grouped_bn(mblocks, H, I, S, false);
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, max_rows, (uint64_t)I * 2, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, (uint64_t)E * H, (uint64_t)I * 2, 64, bn)))
+    return rc;
+  GemmParams p{};
+  p.M = max_rows;
+  p.N = H;
+  p.K = I;
+  p.tiles_n = (H + bn - 1) / bn;
+  p.tiles_m = mblocks;
+  p.k_blocks = (I + 63) / 64;
+  p.group_m = 8;
+  p.C = y;
+  p.ldc = H;
+  p.block_expert = block_expert;
+  p.num_rows_ptr = num_rows_padded;
+  p.num_experts = E;
+  p.b_rows_per_expert = H;
+  p.sorted_slots = sorted_slots;
+  p.slot_weights = topk_weights;
+  p.num_slots = T * topk;
+  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 64: return launch_grouped<GemmCfg<64, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
+    case 128: return launch_grouped<GemmCfg<128, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
+    case 192: return launch_grouped<GemmCfg<192, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
+    default: return launch_grouped<GemmCfg<256, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
+  }
+}
+
+int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream) {
+  clear_error();
+  if (T < 0 || topk < 1 || H % 8 != 0) return set_error(EK_ERR_INVALID, "combine: H must be a multiple of 8");
+  if (T == 0) return EK_OK;
+  if (!y || !out || !aligned16(y) || !aligned16(out)) return set_error(EK_ERR_INVALID, "combine: bad pointers");
+  const long long work = (long long)T * (H / 8);
+  const int threads = 256;
+  const int blocks = (int)std::min<long long>((work + threads - 1) / threads, 148LL * 16);
+  combine_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(out), T, topk, H);
+  return check_cuda(cudaGetLastError(), "combine launch");
+}
+
+int ek_moe_segment_gemm(const void* hs, const void* weights, const int* offsets, void* out, int M, int N, int K,
+                        int E, int dtype, int num_sms, void* stream) {
+  clear_error();
+  if (!hs || !weights || !offsets || !out) return set_error(EK_ERR_INVALID, "segment: null pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || E < 1 || N % 8 != 0 || K % 16 != 0)
+    return set_error(EK_ERR_INVALID, "segment: N %% 8 and K %% 16 must be 0");
+  if (N > K) return set_error(EK_ERR_UNSUPPORTED, "segment: the reference addressing needs N <= K");
+  if (dtype != EK_DTYPE_BF16 && dtype != EK_DTYPE_FP16) return set_error(EK_ERR_INVALID, "segment: bf16/fp16 only");
+  if (!aligned16(hs) || !aligned16(weights) || !aligned16(out))
+    return set_error(EK_ERR_INVALID, "segment: buffers must be 16-byte aligned");
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  const CUtensorMapDataType tdt =
+      dtype == EK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  constexpr int BN = 128;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, hs, tdt, K, M, (uint64_t)K * 2, 64, 128))) return rc;
+  // weights as the [E*N, K] matrix; expert e's block is rows e*N .. e*N+K-1,
+  // columns 0..N-1, read MN-major in 64 x 64 boxes.
+  if ((rc = make_tmap_2d(&tb, weights, tdt, K, (uint64_t)E * N, (uint64_t)K * 2, 64, 64))) return rc;
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.k_blocks = (K + 63) / 64;
+  p.seg_offsets = offsets;
+  p.seg_mblocks = (M + 127) / 128;
+  p.num_units = E * p.seg_mblocks * p.tiles_n;
+  p.group_m = 1;
+  p.C = out;
+  p.ldc = N;
+  const int grid = std::min(S, p.num_units);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == EK_DTYPE_BF16)
+    return launch_grouped<GemmCfg<BN, kBF16, true, kEpiStore, kSchedSegments>>(ta, tb, tb, p, grid, s);
+  return launch_grouped<GemmCfg<BN, kFP16, true, kEpiStore, kSchedSegments>>(ta, tb, tb, p, grid, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,200 @@
+/*
+ * elastikernel B200 C-ABI.
+ *
+ * Plain C entry points over the sm_100a kernels and the green-context shim.
+ * Pointers are device pointers unless named host_*; every compute entry point
+ * is asynchronous on the CUstream / cudaStream_t passed as `stream` (NULL = the
+ * legacy default stream). All functions return EK_OK (0) or an EK_ERR_* code;
+ * ek_last_error() gives the message of the last failure on the calling thread.
+ *
+ * num_sms: size of the SM partition the launch runs in. A value <= 0 means
+ * "look the stream up in the green-context registry", falling back to the
+ * device's full SM count for streams the registry does not know.
+ *
+ * Reference interfaces (Ther-LF/elastikernel) that each group replaces are
+ * cited per declaration as file:line.
+ */
+#ifndef ELASTIKERNEL_H_
+#define ELASTIKERNEL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EK_OK 0
+#define EK_ERR_INVALID 1      /* bad argument (shape, alignment, pointer)   */
+#define EK_ERR_CUDA 2         /* CUDA runtime / driver call failed           */
+#define EK_ERR_OVERSUB 3      /* SM request exceeds what the device has      */
+#define EK_ERR_UNSUPPORTED 4  /* configuration not supported by the kernels */
+#define EK_ERR_DEVICE 5       /* a kernel reported a fault in the status word */
+
+/* Element types for the GEMM entry points. */
+#define EK_DTYPE_BF16 0
+#define EK_DTYPE_FP16 1
+#define EK_DTYPE_E4M3 2
+
+/* Layout of the B operand of a dense GEMM. */
+#define EK_B_KN 0 /* B is [K, N] row-major (the reference's b: b.stride(0) == N) */
+#define EK_B_NK 1 /* B is [N, K] row-major (weight layout, K contiguous)        */
+
+/* ------------------------------------------------------------------ misc */
+
+/* Version of this ABI (major * 100 + minor). */
+int ek_abi_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+const char* ek_last_error(void);
+
+/* Synchronise device `dev`, read the kernels' status word into *status_out and
+ * clear it when `clear` != 0. Non-zero status means a kernel hit a bounded-wait
+ * timeout or an out-of-range index (see the EK_STATUS_* bits). */
+int ek_device_status(int dev, int clear, int* status_out);
+#define EK_STATUS_WAIT_TIMEOUT 1
+#define EK_STATUS_BAD_EXPERT 2
+#define EK_STATUS_BAD_INDEX 4
+
+/* --------------------------------------------------- green-context partitions
+ * Replaces green_ctx.py (get_sm_alignment :46, get_total_sm_count :65,
+ * _split_and_create_gc :84, _remaining_to_resource :110,
+ * create_sm_partition :139, create_disjoint_partitions :169).
+ */
+
+/* Device facts: total SMs, (min SMs, alignment) of a green-context split by
+ * compute capability (7.x -> (2,2), 8.x -> (4,2), >= 9 -> (8,8), as
+ * green_ctx.py:46-62), and the compute capability itself. */
+int ek_device_sm_info(int dev, int* total_sms, int* min_sms, int* alignment, int* cc_major, int* cc_minor);
+
+/* Create n partitions on device `dev` with (already rounded) SM counts
+ * counts[0..n). disjoint != 0 chain-splits each partition off the remainder of
+ * the previous split (green_ctx.py:169-235); disjoint == 0 splits every
+ * partition from the full device, so partitions may overlap
+ * (green_ctx.py:139-166). On success streams_out[i] receives a non-blocking
+ * CUstream bound to partition i and actual_out[i] its real SM count, read from
+ * the split result. Raises EK_ERR_OVERSUB when the counts do not fit. The
+ * green contexts are owned by the library until ek_gctx_destroy_all(). */
+int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** streams_out, int* actual_out);
+
+/* SM count registered for `stream` (0 if the stream is not a partition). */
+int ek_gctx_stream_sm_count(void* stream, int* sm_count_out);
+
+/* Destroy every stream and green context created so far. */
+int ek_gctx_destroy_all(void);
+
+/* Test hook: replace the CUDA driver with an in-library simulation of a device
+ * with `total_sms` SMs split in units of `granularity`; the call numbered
+ * `fail_call` (0-based, -1 = never) returns driver error `fail_code`.
+ * enable == 0 restores the real driver. Used by host-only tests. */
+int ek_gctx_fake_driver(int enable, int total_sms, int granularity, int fail_call, int fail_code);
+
+/* -------------------------------------------------------------------- GEMM
+ * Replaces the Triton matmul_vanilla / matmul_sm_aware kernels and their
+ * wrappers call_vanilla / call_sm_aware (sm_aware_matmul.py:148-234;
+ * duplicate in sm_aware_benchmark.py:59-137), and the GEMM operator
+ * run(A, B, C, M, N, K, NUM_SMS) (sm_aware_agent/definition.py:63-65).
+ */
+
+/* Tile schedule chosen for a GEMM of this shape on a partition of num_sms SMs. */
+typedef struct ek_gemm_plan {
+  int bm, bn, bk;          /* tile shape (bk in elements)                        */
+  int tiles_m, tiles_n;    /* output tiles along M and N                         */
+  int k_blocks;            /* bk-wide steps along K                              */
+  int num_tiles;           /* tiles_m * tiles_n                                  */
+  int num_dp_tiles;        /* tiles computed whole by one CTA                    */
+  int tail_split;          /* K-split factor of the remaining tiles (1 = none)   */
+  int num_units;           /* schedulable work units                             */
+  int grid;                /* CTAs launched (<= num_sms)                         */
+  int num_sms;             /* partition size the plan was made for              */
+  int waves;               /* ceil(num_units / grid)                             */
+  double wave_efficiency;  /* useful K-steps / (grid * K-steps of busiest CTA)   */
+  double est_us;           /* model estimate of the kernel time                  */
+  size_t workspace_bytes;  /* scratch the schedule needs (split partials)        */
+} ek_gemm_plan;
+
+/* Plan a GEMM C[M,N] = A[M,K] * B on num_sms SMs (num_sms > 0 required here).
+ * force_bn / force_split > 0 pin the tile width / tail split (0 = choose). */
+int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
+                      ek_gemm_plan* out);
+
+/* C[M,N] = A[M,K] @ B, fp32 accumulate, C in the input dtype (bf16 / fp16).
+ * A row-major [M,K]; B per b_layout. K and N must be multiples of 8; all
+ * pointers 16-byte aligned. workspace: ws_bytes of device memory holding
+ * plan.workspace_bytes bytes, zero-filled before its first use; the kernel
+ * leaves it zero-filled again (its split counters), so it can be reused by
+ * later calls on the same stream. */
+int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,
+            int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
+
+/* FP8 e4m3 GEMM with per-row activation scales and per-output-channel weight
+ * scales: C[M,N] = (A[M,K] * a_scale[M]) @ (W[N,K] * w_scale[N])^T, bf16 C.
+ * No counterpart kernel in the reference (it has no FP8 path). */
+int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float* w_scale, void* C, int M, int N,
+                int K, int num_sms, int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
+
+/* --------------------------------------------------------------------- MoE
+ * Replaces the fused-MoE operator run(hidden_states, gate_logits, w1, w2, w3,
+ * out, M, K, N, NUM_EXPERTS, TOP_K, NUM_SMS) (sm_aware_agent/definition.py:
+ * 149-170) as four stages, and the segment kernels fused_moe_vanilla /
+ * fused_moe_sm_aware with call_moe_vanilla / call_moe_sm_aware
+ * (sm_aware_benchmark.py:228-391).
+ */
+
+/* Routing (definition.py:152-153): p = softmax(logits[t, :E]) in fp32,
+ * top-k by probability (ties -> lower expert id first), weights renormalised
+ * to sum 1. Writes topk_ids[T, k] (int32) and topk_weights[T, k] (fp32). */
+int ek_moe_route(const float* logits, int T, int E, int topk, int* topk_ids, float* topk_weights, void* stream);
+
+/* Rows of the padded, expert-sorted layout for T tokens, top-k, E experts and
+ * block_m-row blocks: T*k + E*(block_m-1), rounded up to block_m. */
+int64_t ek_moe_max_padded_rows(int T, int topk, int E, int block_m);
+
+/* moe_align_block_size-style permutation. Flattened slots s = t*k + j are
+ * stably sorted by expert id; each expert's run is padded to a multiple of
+ * block_m with the sentinel T*k. Outputs:
+ *   sorted_slots[max_padded_rows]  slot of each padded row (sentinel = T*k)
+ *   block_expert[max_padded_rows / block_m]  expert of each row block (-1 past the end)
+ *   num_rows_padded[1]             padded rows in use
+ *   expert_counts[E]               slots routed to each expert
+ * If x != NULL (x is [T, H], element size elem_bytes) the rows are also
+ * gathered: x_perm[r] = x[sorted_slots[r] / k], zero rows for padding.
+ * scratch: ek_moe_permute_scratch_bytes(T, topk, E) bytes of device memory
+ * (no initial contents required). */
+size_t ek_moe_permute_scratch_bytes(int T, int topk, int E);
+int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int* sorted_slots,
+                   int* block_expert, int* num_rows_padded, int* expert_counts, const void* x, int H,
+                   int elem_bytes, void* x_perm, void* scratch, void* stream);
+
+/* Grouped gate/up GEMM with fused SiLU-and-multiply over the padded rows:
+ *   act[r, n] = silu(x_perm[r] . w1[e, n]) * (x_perm[r] . w3[e, n]),
+ * e = block_expert[r / 128], for r < *num_rows_padded; w1, w3 are [E, I, H]
+ * bf16; act is [max_rows, I] bf16. */
+int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
+                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_sms,
+                   int force_bn, void* stream);
+
+/* Grouped down projection with the top-k weight fused into the epilogue:
+ *   y[s] = topk_weight[s] * (act[r] @ w2[e]^T),  s = sorted_slots[r] < T*k,
+ * w2 is [E, H, I] bf16, y is [T*k, H] bf16. */
+int ek_moe_down(const void* act, const void* w2, const int* block_expert, const int* num_rows_padded,
+                const int* sorted_slots, const float* topk_weights, void* y, int max_rows, int E, int H, int I,
+                int T, int topk, int num_sms, int force_bn, void* stream);
+
+/* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
+int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);
+
+/* Segment GEMM with the reference kernel's semantics
+ * (sm_aware_benchmark.py:228-290): for each expert e with rows
+ * [offsets[e], offsets[e+1]) of hs[M, K]:
+ *   out[rows] = hs[rows] @ Wblk_e,   Wblk_e = weights + e*N*K viewed as [K, N],
+ * i.e. the expert's [N, K] block read as a row-major [K, N] matrix.
+ * fp16 / bf16 in and out (dtype), fp32 accumulate. */
+int ek_moe_segment_gemm(const void* hs, const void* weights, const int* offsets, void* out, int M, int N, int K,
+                        int E, int dtype, int num_sms, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ELASTIKERNEL_H_ */

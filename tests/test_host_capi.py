@@ -1,0 +1,172 @@
+"""Host-only checks of the C-ABI library (no GPU needed).
+
+* the in-tree library loads and exports every entry point include/elastikernel.h declares;
+* the green-context shim's host logic against the in-library fake driver:
+  rounding/over-subscription errors (green_ctx.py:148-155, 197-207), chain
+  splitting of disjoint partitions (green_ctx.py:209-235), driver errors mapped
+  to "CUDA driver error: ..." (green_ctx.py:32-43), the stream registry;
+* the GEMM planner's invariants (the SM-count-aware tile scheduler).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from elastikernel_b200 import _lib
+from elastikernel_b200._lib import check, lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "elastikernel.h"
+
+
+def header_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(ek_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_loads_and_exports_header_symbols():
+    L = lib()
+    syms = header_symbols()
+    assert len(syms) >= 19
+    missing = [s for s in syms if getattr(L, s, None) is None]
+    assert not missing, f"symbols declared in the header but not exported: {missing}"
+    assert set(syms) <= set(_lib.exported_symbols()), "binding table lacks header symbols"
+    assert L.ek_abi_version() == 100
+
+
+@pytest.fixture()
+def fake():
+    L = lib()
+    check(L.ek_gctx_destroy_all())
+    check(L.ek_gctx_fake_driver(1, 148, 8, -1, 0))
+    yield L
+    check(L.ek_gctx_destroy_all())
+    check(L.ek_gctx_fake_driver(0, 0, 0, -1, 0))
+
+
+def _create(L, counts, disjoint):
+    n = len(counts)
+    streams = (ctypes.c_void_p * n)()
+    actual = (ctypes.c_int * n)()
+    rc = L.ek_gctx_create(0, (ctypes.c_int * n)(*counts), n, int(disjoint), streams, actual)
+    return rc, list(streams), list(actual)
+
+
+def test_fake_sm_info(fake):
+    vals = [ctypes.c_int() for _ in range(5)]
+    check(fake.ek_device_sm_info(0, *[ctypes.byref(v) for v in vals]))
+    assert [v.value for v in vals] == [148, 8, 8, 10, 0]
+
+
+def test_disjoint_chain_split(fake):
+    rc, streams, actual = _create(fake, [32, 112], True)
+    assert rc == 0 and actual == [32, 112]
+    assert len(set(streams)) == 2 and all(streams)
+    for s, a in zip(streams, actual):
+        v = ctypes.c_int()
+        check(fake.ek_gctx_stream_sm_count(ctypes.c_void_p(s), ctypes.byref(v)))
+        assert v.value == a
+
+
+def test_split_granularity_reports_actual(fake):
+    # the driver rounds 20 up to its granularity; the shim reports the real count
+    rc, _, actual = _create(fake, [20], False)
+    assert rc == 0 and actual == [24]
+
+
+def test_disjoint_oversubscription(fake):
+    rc, _, _ = _create(fake, [80, 72], True)
+    assert rc == _lib.EK_ERR_OVERSUB
+    assert "exceeds device total" in _lib.last_error()
+
+
+def test_overlapping_partitions_each_from_full_device(fake):
+    rc, _, actual = _create(fake, [136], False)
+    assert rc == 0
+    rc, _, actual2 = _create(fake, [136], False)
+    assert rc == 0 and actual == actual2 == [136]
+
+
+def test_driver_error_is_reported(fake):
+    check(fake.ek_gctx_destroy_all())
+    check(fake.ek_gctx_fake_driver(0, 0, 0, -1, 0))
+    # fail the 4th driver call (DeviceGet, GetDevResource, Split, GenerateDesc)
+    check(fake.ek_gctx_fake_driver(1, 148, 8, 3, 2))  # 2 = CUDA_ERROR_OUT_OF_MEMORY
+    rc, _, _ = _create(fake, [16], False)
+    assert rc == _lib.EK_ERR_CUDA
+    assert _lib.last_error().startswith("CUDA driver error: CUDA_ERROR_OUT_OF_MEMORY")
+    with pytest.raises(RuntimeError, match="CUDA driver error"):
+        check(rc)
+
+
+def test_invalid_counts(fake):
+    rc, _, _ = _create(fake, [0], False)
+    assert rc == _lib.EK_ERR_INVALID
+    rc, _, _ = _create(fake, [200], False)
+    assert rc == _lib.EK_ERR_OVERSUB
+    with pytest.raises(ValueError):
+        check(rc)
+
+
+def test_python_rounding_and_errors(fake, monkeypatch):
+    """green_ctx.create_* round up to the alignment and raise ValueError like the reference."""
+    import torch
+
+    from elastikernel_b200 import green_ctx
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    made = []
+
+    class FakeStream:
+        def __init__(self, ptr, device=None):
+            self.cuda_stream = ptr
+            made.append(ptr)
+
+    monkeypatch.setattr(torch.cuda, "ExternalStream", FakeStream)
+    dev = torch.device("cuda", 0)
+    assert green_ctx.get_sm_alignment(dev) == (8, 8)
+    assert green_ctx.get_total_sm_count(dev) == 148
+    s, n = green_ctx.create_sm_partition(dev, 13)
+    assert n == 16 and green_ctx.stream_sm_count(s) == 16
+    with pytest.raises(ValueError, match="rounded to 152"):
+        green_ctx.create_sm_partition(dev, 148)
+    # 116 rounds up to 120 and 32 + 120 > 148: the reference raises here too
+    with pytest.raises(ValueError, match=r"\[32, 120\]"):
+        green_ctx.create_disjoint_partitions(dev, [32, 116])
+    parts = green_ctx.create_disjoint_partitions(dev, [32, 112])
+    assert [p[1] for p in parts] == [32, 112]
+    with pytest.raises(ValueError, match="exceeds device total"):
+        green_ctx.create_disjoint_partitions(dev, [80, 72])
+    assert green_ctx.create_disjoint_partitions(dev, []) == []
+
+
+@pytest.mark.parametrize("S", [16, 32, 64, 96, 132, 148])
+@pytest.mark.parametrize("M", [1, 128, 256, 512, 1024, 2048, 4096, 8192])
+def test_planner_invariants(S, M):
+    from elastikernel_b200 import _ops
+
+    N = K = 4096
+    p = _ops.plan(M, N, K, S)
+    assert p["bn"] in (64, 128, 192, 256)
+    assert p["tiles_m"] == -(-M // 128) and p["tiles_n"] == -(-N // p["bn"])
+    assert p["num_units"] == p["num_dp_tiles"] + (p["num_tiles"] - p["num_dp_tiles"]) * p["tail_split"]
+    assert 1 <= p["grid"] <= S
+    assert 0 < p["wave_efficiency"] <= 1.0
+    if p["tail_split"] > 1:
+        assert p["workspace_bytes"] > 0
+        assert p["k_blocks"] // p["tail_split"] >= 4
+    else:
+        assert p["workspace_bytes"] == 0
+    # the plan is a deterministic function of its inputs
+    assert _ops.plan(M, N, K, S) == p
+
+
+def test_planner_beats_reference_tiles_at_148():
+    """At 4096^3 on 148 SMs the reference's best tile (128x256, 4 waves) is
+    86.5% efficient; the split tail wave brings the busiest CTA within 2% of ideal."""
+    from elastikernel_b200 import _ops
+
+    p = _ops.plan(4096, 4096, 4096, 148)
+    assert p["wave_efficiency"] > 0.98
