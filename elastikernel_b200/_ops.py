@@ -136,3 +136,158 @@ def _stream_sms(dev: torch.device, stream: int) -> int:
     if v.value > 0:
         return v.value
     return torch.cuda.get_device_properties(dev).multi_processor_count
+
+
+# ---------------------------------------------------------------------- MoE
+BLOCK_M = 128
+
+
+def moe_route(gate_logits: torch.Tensor, topk: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Softmax top-k routing (definition.py:152-153): int32 ids [T,k] and fp32
+    renormalised weights [T,k]. Ties go to the lower expert id."""
+    dev = _require_cuda(gate_logits)
+    if gate_logits.dtype != torch.float32 or gate_logits.dim() != 2:
+        raise RuntimeError("gate_logits must be a 2-D float32 tensor")
+    _contig("gate_logits", gate_logits)
+    T, E = gate_logits.shape
+    ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_route(gate_logits.data_ptr(), T, E, int(topk), ids.data_ptr(), wts.data_ptr(),
+                                 current_stream_handle(dev)), "ek_moe_route")
+    return ids, wts
+
+
+def moe_permute(topk_ids: torch.Tensor, num_experts: int, x: torch.Tensor | None = None,
+                block_m: int = BLOCK_M) -> dict:
+    """Expert-sorted, block-padded layout of the (token, choice) slots, with the
+    token rows of `x` gathered into it when given."""
+    dev = _require_cuda(topk_ids, x)
+    if topk_ids.dtype != torch.int32 or topk_ids.dim() != 2:
+        raise RuntimeError("topk_ids must be a 2-D int32 tensor")
+    _contig("topk_ids", topk_ids)
+    T, k = topk_ids.shape
+    E = int(num_experts)
+    max_rows = int(lib().ek_moe_max_padded_rows(T, k, E, block_m))
+    sorted_slots = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    block_expert = torch.empty(max_rows // block_m, dtype=torch.int32, device=dev)
+    num_rows = torch.empty(1, dtype=torch.int32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    x_perm = None
+    H = 0
+    es = 0
+    if x is not None:
+        _contig("x", x)
+        if x.dim() != 2 or x.shape[0] != T:
+            raise RuntimeError("x must be [T, H]")
+        H = x.shape[1]
+        es = x.element_size()
+        x_perm = torch.empty((max_rows, H), dtype=x.dtype, device=dev)
+    scratch = torch.empty(int(lib().ek_moe_permute_scratch_bytes(T, k, E)), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_permute(topk_ids.data_ptr(), T, k, E, block_m, sorted_slots.data_ptr(),
+                                   block_expert.data_ptr(), num_rows.data_ptr(), counts.data_ptr(), _ptr(x), H, es,
+                                   _ptr(x_perm), scratch.data_ptr(), current_stream_handle(dev)), "ek_moe_permute")
+    return {"sorted_slots": sorted_slots, "block_expert": block_expert, "num_rows_padded": num_rows,
+            "expert_counts": counts, "x_perm": x_perm, "max_rows": max_rows, "T": T, "topk": k, "E": E,
+            "block_m": block_m}
+
+
+def _check_bf16(name: str, t: torch.Tensor) -> None:
+    if t.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name} must be bfloat16")
+    _contig(name, t)
+
+
+def moe_gate_up(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: int | None = None,
+                force_bn: int = 0) -> torch.Tensor:
+    """act[r] = silu(x_perm[r] . w1[e]) * (x_perm[r] . w3[e]) over the padded rows."""
+    x_perm = perm["x_perm"]
+    dev = _require_cuda(x_perm, w1, w3)
+    for n, t in (("x_perm", x_perm), ("w1", w1), ("w3", w3)):
+        _check_bf16(n, t)
+    E, I, H = w1.shape
+    if w3.shape != w1.shape or x_perm.shape[1] != H or E != perm["E"]:
+        raise RuntimeError("gate_up: shape mismatch")
+    max_rows = perm["max_rows"]
+    act = torch.empty((max_rows, I), dtype=torch.bfloat16, device=dev)
+    stream = current_stream_handle(dev)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_gate_up(x_perm.data_ptr(), w1.data_ptr(), w3.data_ptr(), perm["block_expert"].data_ptr(),
+                                   perm["num_rows_padded"].data_ptr(), act.data_ptr(), max_rows, E, H, I,
+                                   int(num_sms or 0), int(force_bn), stream), "ek_moe_gate_up")
+    return act
+
+
+def moe_down(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
+             num_sms: int | None = None, force_bn: int = 0) -> torch.Tensor:
+    """y[s] = topk_weight[s] * (act[r] @ w2[e]^T) for the slot s of each used row r."""
+    dev = _require_cuda(act, w2, topk_weights)
+    _check_bf16("act", act)
+    _check_bf16("w2", w2)
+    _contig("topk_weights", topk_weights)
+    if topk_weights.dtype != torch.float32:
+        raise RuntimeError("topk_weights must be float32")
+    E, H, I = w2.shape
+    T, k = perm["T"], perm["topk"]
+    if act.shape[1] != I or E != perm["E"] or topk_weights.numel() != T * k:
+        raise RuntimeError("down: shape mismatch")
+    y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_down(act.data_ptr(), w2.data_ptr(), perm["block_expert"].data_ptr(),
+                                perm["num_rows_padded"].data_ptr(), perm["sorted_slots"].data_ptr(),
+                                topk_weights.data_ptr(), y.data_ptr(), perm["max_rows"], E, H, I, T, k,
+                                int(num_sms or 0), int(force_bn), current_stream_handle(dev)), "ek_moe_down")
+    return y
+
+
+def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = sum_j y[t*k + j] (fp32 sum in j order), bf16."""
+    dev = _require_cuda(y, out)
+    _check_bf16("y", y)
+    H = y.shape[1]
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    else:
+        _check_bf16("out", out)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_combine(y.data_ptr(), out.data_ptr(), int(T), int(topk), H, current_stream_handle(dev)),
+              "ek_moe_combine")
+    return out
+
+
+def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+              w3: torch.Tensor, topk: int, out: torch.Tensor | None = None, num_sms: int | None = None) -> torch.Tensor:
+    """The whole MoE layer: route -> permute(+gather) -> gate/up SwiGLU -> down(+weight) -> combine."""
+    _require_cuda(hidden_states, gate_logits, w1, w2, w3, out)
+    _check_bf16("hidden_states", hidden_states)
+    T = hidden_states.shape[0]
+    if T == 0:
+        return out if out is not None else torch.empty_like(hidden_states)
+    ids, wts = moe_route(gate_logits, topk)
+    perm = moe_permute(ids, w1.shape[0], x=hidden_states)
+    act = moe_gate_up(perm, w1, w3, num_sms=num_sms)
+    y = moe_down(perm, act, w2, wts, num_sms=num_sms)
+    return moe_combine(y, T, topk, out=out)
+
+
+def moe_segment_gemm(hidden_states: torch.Tensor, weights: torch.Tensor, expert_offsets: torch.Tensor,
+                     num_experts: int, N: int, K: int, num_sms: int | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reference segment GEMM semantics (sm_aware_benchmark.py:228-290)."""
+    dev = _require_cuda(hidden_states, weights, expert_offsets, out)
+    if hidden_states.dtype not in _DTYPES or weights.dtype != hidden_states.dtype:
+        raise RuntimeError("segment GEMM takes bf16/fp16 operands of one dtype")
+    for n, t in (("hidden_states", hidden_states), ("weights", weights), ("expert_offsets", expert_offsets)):
+        _contig(n, t)
+    if expert_offsets.dtype != torch.int32 or expert_offsets.numel() != num_experts + 1:
+        raise RuntimeError("expert_offsets must be int32 [num_experts + 1]")
+    M = hidden_states.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=hidden_states.dtype, device=dev)
+    with torch.cuda.device(dev):
+        check(lib().ek_moe_segment_gemm(hidden_states.data_ptr(), weights.data_ptr(), expert_offsets.data_ptr(),
+                                        out.data_ptr(), M, int(N), int(K), int(num_experts),
+                                        _DTYPES[hidden_states.dtype], int(num_sms or 0),
+                                        current_stream_handle(dev)), "ek_moe_segment_gemm")
+    return out

@@ -1,0 +1,159 @@
+"""Fused-MoE parity on the GPU (C-ABI kernels vs the CPU oracle).
+
+* routing indices and the permutation are compared bit-exactly;
+* routing weights: |w - w_ref| <= 1e-6 (fp32 softmax, different exp rounding);
+* MoE outputs: max|out - ref| / max|ref| <= 1e-2 against the oracle's fp32
+  computation on the same bf16 inputs (the spec's bf16 tolerance);
+* the segment GEMM (reference kernel semantics) against the oracle and the
+  golden output of the reference Triton kernel.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gemm as og
+from oracle import moe as om
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+TOL = 1e-2
+
+
+@pytest.mark.parametrize("T,E,k", [(4096, 8, 2), (1, 8, 2), (512, 256, 8), (333, 16, 4), (64, 64, 6)])
+def test_route_matches_oracle(cuda_dev, T, E, k):
+    from elastikernel_b200 import _ops
+
+    g = torch.Generator().manual_seed(T + E + k)
+    logits = torch.randn((T, E), generator=g)
+    ids, w = _ops.moe_route(logits.to(cuda_dev), k)
+    rids, rw = om.route_ref(logits.numpy(), k)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rids)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, atol=1e-6, rtol=0)
+
+
+def test_route_golden_and_ties(cuda_dev):
+    from elastikernel_b200 import _ops
+
+    z = np.load(GOLD / "routing.npz")
+    for name in ("mixtral", "dsv3", "small"):
+        ids, w = _ops.moe_route(torch.from_numpy(z[f"{name}_logits"]).to(cuda_dev), int(z[f"{name}_k"]))
+        np.testing.assert_array_equal(ids.cpu().numpy(), z[f"{name}_ids"])
+        np.testing.assert_allclose(w.cpu().numpy(), z[f"{name}_weights"], atol=1e-6, rtol=0)
+    ties = torch.zeros((4, 40))
+    ties[1, [3, 35]] = 1.0
+    ties[2, :] = -float("inf")
+    ties[2, [7, 39]] = 0.0
+    ids, w = _ops.moe_route(ties.to(cuda_dev), 2)
+    rids, rw = om.route_ref(ties.numpy(), 2)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rids)
+    np.testing.assert_array_equal(rids, [[0, 1], [3, 35], [7, 39], [0, 1]])
+
+
+@pytest.mark.parametrize("T,E,k", [(4096, 8, 2), (1, 8, 2), (3000, 256, 8), (17, 4, 4), (2500, 64, 3)])
+def test_permute_bit_exact(cuda_dev, T, E, k):
+    from elastikernel_b200 import _ops
+
+    g = torch.Generator().manual_seed(T * 7 + E)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    H = 64
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    perm = _ops.moe_permute(ids.to(cuda_dev), E, x=x.to(cuda_dev))
+    ref = om.permute_ref(ids.numpy(), E, 128)
+    n = ref["num_rows_padded"]
+    assert int(perm["num_rows_padded"].item()) == n
+    np.testing.assert_array_equal(perm["sorted_slots"].cpu().numpy(), ref["sorted_slots"])
+    np.testing.assert_array_equal(perm["block_expert"].cpu().numpy(), ref["block_expert"])
+    np.testing.assert_array_equal(perm["expert_counts"].cpu().numpy(), ref["expert_counts"])
+    slots = ref["sorted_slots"][:n]
+    used = slots < T * k
+    got = perm["x_perm"][:n].cpu()[torch.from_numpy(used)]
+    want = x[torch.from_numpy(slots[used] // k).long()]
+    assert torch.equal(got, want)
+
+
+def _moe_inputs(T, H, I, E, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=g)
+    w1 = (torch.randn((E, I, H), generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn((E, H, I), generator=g) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn((E, I, H), generator=g) * 0.02).to(torch.bfloat16)
+    return x, logits, w1, w2, w3
+
+
+@pytest.mark.parametrize("T,H,I,E,k", [(1, 512, 1024, 8, 2), (16, 512, 1024, 8, 2), (300, 256, 512, 8, 2),
+                                       (64, 256, 384, 16, 4), (200, 128, 256, 32, 8)])
+def test_fused_moe_small(cuda_dev, T, H, I, E, k):
+    from elastikernel_b200 import _ops
+
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=T + I)
+    out = _ops.fused_moe(*(t.to(cuda_dev) for t in (x, logits, w1, w2, w3)), topk=k)
+    torch.cuda.synchronize()
+    ref = om.moe_ref(x, logits, w1, w2, w3, k)
+    err = og.max_rel_err(out, ref)
+    assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("T", [1, 16, 128])
+def test_fused_moe_mixtral_shapes(cuda_dev, T):
+    """Mixtral expert shapes (H=4096, I=14336, E=8, top-2) at small token counts."""
+    from elastikernel_b200 import _ops
+
+    x, logits, w1, w2, w3 = _moe_inputs(T, 4096, 14336, 8, seed=42 + T)
+    out = _ops.fused_moe(*(t.to(cuda_dev) for t in (x, logits, w1, w2, w3)), topk=2)
+    torch.cuda.synchronize()
+    ref = om.moe_ref(x, logits, w1, w2, w3, 2)
+    err = og.max_rel_err(out, ref)
+    assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("bn", [64, 128, 192, 256])
+def test_grouped_tile_widths(cuda_dev, bn):
+    from elastikernel_b200 import _ops
+
+    T, H, I, E, k = 400, 256, 640, 8, 2
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=bn)
+    d = [t.to(cuda_dev) for t in (x, logits, w1, w2, w3)]
+    ids, wts = _ops.moe_route(d[1], k)
+    perm = _ops.moe_permute(ids, E, x=d[0])
+    act = _ops.moe_gate_up(perm, d[2], d[4], force_bn=bn)
+    y = _ops.moe_down(perm, act, d[3], wts, force_bn=bn)
+    out = _ops.moe_combine(y, T, k)
+    torch.cuda.synchronize()
+    assert og.max_rel_err(out, om.moe_ref(x, logits, w1, w2, w3, k)) <= TOL
+
+
+def test_segment_gemm_golden(cuda_dev):
+    from elastikernel_b200 import _ops
+
+    z = np.load(GOLD / "triton_gemm.npz")
+    hs = torch.from_numpy(z["seg_hs"])
+    w = torch.from_numpy(z["seg_w"])
+    offs = torch.from_numpy(z["seg_offsets"])
+    N, K, E = z["seg_out"].shape[1], hs.shape[1], offs.numel() - 1
+    out = _ops.moe_segment_gemm(hs.to(cuda_dev), w.to(cuda_dev), offs.to(cuda_dev), E, N, K)
+    torch.cuda.synchronize()
+    ref = z["seg_out"].astype(np.float32)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, rtol=1e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_segment_gemm_reference_config(cuda_dev, dtype):
+    """The reference MoE benchmark's shapes (sm_aware_benchmark.py:406-444):
+    tokens 512, N = K = 4096, 8 experts, top-2 fake contiguous routing."""
+    from elastikernel_b200 import _ops
+
+    T, N, K, E, k = 512, 4096, 4096, 8, 2
+    g = torch.Generator().manual_seed(42)
+    hs = torch.randn((T, K), generator=g).to(dtype)
+    w = torch.randn((E * N, K), generator=g).to(dtype)
+    tpe = (T * k) // E
+    offs = torch.tensor([0] + [min((i + 1) * tpe, T) for i in range(E - 1)] + [T], dtype=torch.int32)
+    out = _ops.moe_segment_gemm(hs.to(cuda_dev), w.to(cuda_dev), offs.to(cuda_dev), E, N, K)
+    torch.cuda.synchronize()
+    ref = og.segment_gemm_ref(hs, w, offs, N, K)
+    assert og.max_rel_err(out, ref) <= TOL
