@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark of the SM-aware GEMM + fused-MoE hot path on B200.
+
+Headline (`value`): bf16 GEMM M = N = K = 4096 (the N=K=4096 wave-sweep's
+square point) on the full 148-SM device, TFLOP/s, whole job (sum over ranks;
+ranks are independent replicas, "weak" scaling). One step = one GEMM of
+synthetic N(0,1) inputs (seed 0) resident in HBM; the L2 is flushed (256 MB
+write) before every timed step, outside the timed events.
+
+Also on the same line:
+* e2e       the same metric through the public API (sm_aware_matmul.call_sm_aware)
+            with pinned host buffers: H2D of A and B, the GEMM, D2H of C per step
+* roofline  achieved TFLOP/s of the GEMM kernel vs the measured bf16 peak
+* partitions  4096^3 on green-context partitions of {16,32,64,96,132,148} SMs,
+            % of the SM-scaled peak, plus the M sweep at 148 SMs
+* moe       Mixtral-shaped fused MoE tokens/s at T in {1,16,128,1024,4096}
+* cpu_baseline  the reference's CPU GEMM (torch.matmul on CPU) on a bounded sample
+
+`--impl reference` times the reference's own CPU implementation of the path
+(the oracle restatement of the GEMM operator, torch.matmul on CPU bf16) on the
+host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+M = N = K = 4096
+FLOP = 2.0 * M * N * K
+METRIC = "bf16 GEMM TFLOP/s per green-ctx partition (4096^3, 148-SM full device)"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            pass
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="ek_clocks_", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in self.path.read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                if self.uuid and self.uuid.replace("GPU-", "") not in parts[0]:
+                    continue
+                rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def timed_steps(step_fn, steps: int, flush) -> tuple[float, list]:
+    """Run `steps` steps; each is bracketed by events on the current stream
+    (flush outside them). Returns (mean ms per step, per-step ms)."""
+    evs = []
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step_fn()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in evs]
+    return sum(ms) / len(ms), ms
+
+
+def partition_sweep(dev, peak_tflops: float, steps: int) -> dict:
+    from elastikernel_b200 import sm_aware_matmul as smm
+    from elastikernel_b200.green_ctx import create_sm_partition, full_device_partition, get_total_sm_count
+    from elastikernel_b200.timing import time_on_stream
+
+    total = get_total_sm_count(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {"square_4096": [], "m_sweep_148": []}
+    a = torch.randn((M, K), device=dev, dtype=torch.bfloat16, generator=g)
+    b = torch.randn((K, N), device=dev, dtype=torch.bfloat16, generator=g)
+    for S in [16, 32, 64, 96, 132, 148]:
+        try:
+            stream, actual = full_device_partition(dev) if S >= total else create_sm_partition(dev, S)
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    smm.call_sm_aware(a, b)
+                r = time_on_stream(lambda: smm.call_sm_aware(a, b), stream, reps=max(3, steps // 2))
+            p = smm.tcgen05_schedule(M, N, K, actual)
+            tf = FLOP / (r["mean_ms"] * 1e-3) / 1e12
+            out["square_4096"].append({"sm": S, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
+                                       "tflops": round(tf, 1),
+                                       "pct_scaled_peak": round(100 * tf / (peak_tflops * actual / 148), 1),
+                                       "bn": p["bn"], "split": p["tail_split"],
+                                       "wave_eff": round(p["wave_efficiency"], 3)})
+        except Exception as e:  # report and continue, as the reference benchmark does
+            out["square_4096"].append({"sm": S, "error": str(e)[:200]})
+    for Mi in [128, 256, 512, 1024, 2048, 4096, 8192]:
+        a2 = torch.randn((Mi, K), device=dev, dtype=torch.bfloat16, generator=g)
+        for _ in range(2):
+            smm.call_sm_aware(a2, b)
+        r = time_on_stream(lambda: smm.call_sm_aware(a2, b), reps=max(3, steps // 2))
+        tf = 2.0 * Mi * N * K / (r["mean_ms"] * 1e-3) / 1e12
+        p = smm.tcgen05_schedule(Mi, N, K, total)
+        out["m_sweep_148"].append({"M": Mi, "us": round(r["mean_ms"] * 1e3, 1), "tflops": round(tf, 1),
+                                   "pct_peak": round(100 * tf / peak_tflops, 1), "bn": p["bn"],
+                                   "split": p["tail_split"], "tiles": p["num_tiles"]})
+    return out
+
+
+def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:
+    """Mixtral-shaped fused MoE (E=8, top-2, H=4096, I=14336, bf16) tokens/s."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.green_ctx import create_sm_partition
+    from elastikernel_b200.timing import time_on_stream
+
+    E, k, H, I = 8, 2, 4096, 14336
+    g = torch.Generator(device=dev).manual_seed(42)
+    w1 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn((E, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    res = []
+    half_stream, half_sms = create_sm_partition(dev, 72)
+    for T in [1, 16, 128, 1024, 4096]:
+        x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn((T, E), device=dev, generator=g)
+        for label, stream, sms in (("full", torch.cuda.current_stream(dev), 148), ("half", half_stream, half_sms)):
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    _ops.fused_moe(x, logits, w1, w2, w3, k)
+                r = time_on_stream(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k), stream,
+                                   reps=max(3, steps // 2))
+                ids, _ = _ops.moe_route(logits, k)
+            hit = int(torch.unique(ids).numel())
+            t_s = r["mean_ms"] * 1e-3
+            flop = T * k * 6.0 * H * I
+            wbytes = hit * 3.0 * H * I * 2
+            t_floor = max(flop / (1.6654e15 * sms / 148), wbytes / (hbm_gbs * 1e9))
+            res.append({"T": T, "sms": label, "actual_sm": sms, "us": round(r["mean_ms"] * 1e3, 1),
+                        "tokens_per_s": round(T / t_s, 1), "tflops": round(flop / t_s / 1e12, 1),
+                        "experts_hit": hit, "pct_roofline_time": round(100 * t_floor / t_s, 1)})
+    return {"config": "Mixtral E=8 k=2 H=4096 I=14336 bf16, weights N(0,0.02)", "results": res}
+
+
+def cpu_baseline_sample() -> dict:
+    from oracle import cpu_baseline
+
+    threads = cpu_baseline.set_threads()
+    r = cpu_baseline.time_gemm(M, N, K, reps=3, budget_s=20.0)
+    mean_s = statistics.fmean(r["seconds"])
+    return {"value": round(r["flop"] / mean_s / 1e12, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(r['seconds'])} x bf16 torch.matmul {M}x{N}x{K} on CPU (the reference GEMM operator "
+                      f"body), mean {mean_s * 1e3:.0f} ms"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference's own CPU implementation of the path: torch.matmul on CPU
+    bf16 tensors (oracle restatement of definition.py:63-65), all host threads."""
+    if rank != 0:
+        return
+    from oracle import cpu_baseline
+
+    threads = cpu_baseline.set_threads()
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn((M, K), generator=g).to(torch.bfloat16)
+    b = torch.randn((K, N), generator=g).to(torch.bfloat16)
+    for _ in range(args.warmup):
+        cpu_baseline.gemm_cpu(a, b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_baseline.gemm_cpu(a, b)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = FLOP / dt / 1e12
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 0",
+            "config": {"workload": "bf16 GEMM 4096x4096x4096, torch.matmul on host CPU", "M": M, "N": N, "K": K},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} x bf16 torch.matmul {M}x{N}x{K} on CPU"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip the partition sweep, MoE and CPU legs")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local_rank = dist_env()
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from elastikernel_b200 import _lib, sm_aware_matmul as smm
+    from elastikernel_b200.timing import flush_l2
+
+    peaks, peak_kind = load_peaks()
+    peak_tf = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randn((M, K), device=dev, dtype=torch.bfloat16, generator=g)
+    b = torch.randn((K, N), device=dev, dtype=torch.bfloat16, generator=g)
+    plan = smm.tcgen05_schedule(M, N, K, torch.cuda.get_device_properties(dev).multi_processor_count)
+    for _ in range(args.warmup):
+        smm.call_sm_aware(a, b)
+    flush_l2(dev)
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- device-resident timed region
+    sampler = ClockSampler(dev)
+    with sampler:
+        barrier(world)
+        torch.cuda.synchronize()
+        ms, per = timed_steps(lambda: smm.call_sm_aware(a, b), args.steps, lambda: flush_l2(dev))
+        torch.cuda.synchronize()
+        barrier(world)
+        # ------------------------------------------------------------ end-to-end (host buffers)
+        a_h = a.cpu().pin_memory()
+        b_h = b.cpu().pin_memory()
+        c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+        a_d = torch.empty_like(a)
+        b_d = torch.empty_like(b)
+
+        def e2e_step():
+            a_d.copy_(a_h, non_blocking=True)
+            b_d.copy_(b_h, non_blocking=True)
+            c = smm.call_sm_aware(a_d, b_d)
+            c_h.copy_(c, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms, _ = timed_steps(e2e_step, args.steps, None)
+        barrier(world)
+    clocks = sampler.summary()
+    status = _lib.device_status(local_rank)
+
+    ms_max = max_over_ranks(ms, world)
+    e2e_max = max_over_ranks(e2e_ms, world)
+    value = world * FLOP / (ms_max * 1e-3) / 1e12
+    e2e_value = world * FLOP / (e2e_max * 1e-3) / 1e12
+    achieved = FLOP / (ms * 1e-3) / 1e12
+
+    traffic = None
+    tfile = REPO / "profiles" / "gemm_bf16_4096_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    extras = {}
+    if not args.no_extras:
+        extras["partitions"] = partition_sweep(dev, peak_tf, args.steps)
+        extras["moe"] = moe_bench(dev, args.steps, hbm)
+        if rank == 0 and world == 1:
+            extras["cpu_baseline"] = cpu_baseline_sample()
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 0",
+        "config": {"workload": "bf16 GEMM 4096x4096x4096 on the full 148-SM device (N=K=4096 wave sweep, "
+                               "square point); replicas per GPU", "M": M, "N": N, "K": K,
+                   "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) before every timed step",
+                   "schedule": {k: plan[k] for k in ("bn", "tail_split", "num_units", "grid",
+                                                      "wave_efficiency")}},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": 2 * M * K * 2,
+                "d2h_bytes_per_step": M * N * 2,
+                "path": "sm_aware_matmul.call_sm_aware with pinned host A, B -> device -> host C"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": UNIT,
+                     "frac": round(achieved / peak_tf, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if "cpu_baseline" in extras:
+        line["cpu_baseline"] = extras.pop("cpu_baseline")
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
