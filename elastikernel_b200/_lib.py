@@ -68,6 +68,9 @@ _SIGNATURES = {
                          _c_vp, _c_size, _c_vp]),
     "ek_gemm_fp8": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                              _c_vp, _c_size, _c_vp]),
+    "ek_gemm_noalloc": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                 _c_int, _c_vp]),
+    "ek_gemm_noalloc_max_scratch_bytes": (_c_size, []),
     "ek_moe_route": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_max_padded_rows": (ctypes.c_int64, [_c_int, _c_int, _c_int, _c_int]),
     "ek_moe_permute_scratch_bytes": (_c_size, [_c_int, _c_int, _c_int]),

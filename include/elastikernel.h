@@ -133,6 +133,21 @@ int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtyp
 int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float* w_scale, void* C, int M, int N,
                 int K, int num_sms, int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
 
+/* GEMM for callers that cannot allocate device memory. No counterpart in the
+ * reference. Same arguments and result as ek_gemm, minus the workspace: the
+ * scratch for split K-slices comes from a fixed 32 MiB device array inside
+ * the library (ek_gemm_noalloc_max_scratch_bytes()), held by every GPU that
+ * loads it until exit. Intended for hosts that own all device memory (a
+ * serving engine with its own pool that lends plugins no allocator) and for
+ * paths that must not call cudaMalloc/cudaFree because those can synchronise
+ * the device. Schedules needing more scratch fail with EK_ERR_UNSUPPORTED.
+ * All calls on a device share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller. The first call on a device looks up
+ * the array's address; make it before any stream capture on that device. */
+int ek_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,
+                    int force_bn, int force_split, void* stream);
+size_t ek_gemm_noalloc_max_scratch_bytes(void);
+
 /* --------------------------------------------------------------------- MoE
  * Replaces the fused-MoE operator run(hidden_states, gate_logits, w1, w2, w3,
  * out, M, K, N, NUM_EXPERTS, TOP_K, NUM_SMS) (sm_aware_agent/definition.py:
