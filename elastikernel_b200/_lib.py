@@ -40,7 +40,7 @@ class GemmPlan(ctypes.Structure):
     """Mirror of ``ek_gemm_plan``."""
 
     _fields_ = [
-        ("bm", _c_int), ("bn", _c_int), ("bk", _c_int),
+        ("bm", _c_int), ("bn", _c_int), ("bk", _c_int), ("cta_pair", _c_int),
         ("tiles_m", _c_int), ("tiles_n", _c_int), ("k_blocks", _c_int),
         ("num_tiles", _c_int), ("num_dp_tiles", _c_int), ("tail_split", _c_int),
         ("num_units", _c_int), ("grid", _c_int), ("num_sms", _c_int), ("waves", _c_int),

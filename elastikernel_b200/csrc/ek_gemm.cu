@@ -3,7 +3,8 @@
 //
 // The planner is what replaces the reference's "put NUM_SMS in the Triton
 // autotune key" idea (sm_aware_matmul.py:183-216): for a partition of S SMs it
-// picks the tile width BN and a K-split of the tail wave so that the busiest
+// picks the MMA mode (one CTA per 128 x BN tile, or a CTA pair per 256 x BN
+// tile), the tile width BN and a K-split of the tail wave so that the busiest
 // CTA does as little as possible, using a small analytic cost model of the
 // B200 (tensor rate, per-SM operand feed, HBM). The choice is a deterministic
 // function of (M, N, K, S, dtype); no autotuning runs in the hot path.
@@ -35,34 +36,40 @@ struct Machine {
   double clk_ghz = 1.80;         // SM clock under a dense tensor load
   double f16_flops_clk = 8192;   // dense bf16/fp16 FLOP per clock per SM
   double f8_flops_clk = 16384;   // dense e4m3 FLOP per clock per SM
-  double feed_bytes_clk = 100;   // operand bytes per clock per SM (L2 -> SMEM)
+  double feed_bytes_clk = 64;    // operand bytes per clock one SM sustains from L2 with all SMs loading
   double hbm_gbs = 6500;         // device HBM bandwidth
   double hbm_per_sm_gbs = 80;    // bandwidth one SM can draw
+  double part_gbs_per_sm = 200;  // split partials: written and read back through L2
   double launch_us = 2.0;        // fixed launch + prologue cost
 };
 
 struct Candidate {
-  int bn, split, full_waves, tail_tiles;
+  int pair, bn, split, full_waves, tail_tiles;
   double est_us, eff;
 };
 
 int elem_bytes(int dtype) { return dtype == EK_DTYPE_E4M3 ? 1 : 2; }
 
-Candidate evaluate(int M, int N, int K, int S, int dtype, int bn, int split_force) {
+Candidate evaluate(int M, int N, int K, int S, int dtype, int pair, int bn, int split_force) {
   Machine mc;
   const int es = elem_bytes(dtype);
   const int bk = 128 / es;
-  const int tm = (M + 127) / 128, tn = (N + bn - 1) / bn;
+  const int ctas = pair ? 2 : 1;
+  const int tile_m = 128 * ctas;
+  const int slots = S / ctas;  // concurrent tiles
+  const int tm = (M + tile_m - 1) / tile_m, tn = (N + bn - 1) / bn;
   const int tiles = tm * tn;
   const int kb = (K + bk - 1) / bk;
-  const int full = tiles / S;
-  const int R = tiles - full * S;
+  Candidate best{pair, bn, 1, 0, 0, 1e30, 0};
+  if (slots < 1) return best;
+  const int full = tiles / slots;
+  const int R = tiles - full * slots;
   const double flops_clk = dtype == EK_DTYPE_E4M3 ? mc.f8_flops_clk : mc.f16_flops_clk;
+  // per SM and K step: its share of the MMA and the operand bytes it streams
   const double mma_clk = 128.0 * bn * bk * 2.0 / flops_clk;
-  const double feed_clk = (128.0 + bn) * 128.0 / mc.feed_bytes_clk;
+  const double feed_clk = (128.0 + double(bn) / ctas) * 128.0 / mc.feed_bytes_clk;
   const double t_kb_us = std::max(mma_clk, feed_clk) / (mc.clk_ghz * 1e3);
 
-  Candidate best{bn, 1, full, R, 1e30, 0};
   const int max_split = std::min(kb, 16);
   // A forced split only applies when there is a tail wave to split.
   if (R == 0) split_force = split_force > 0 ? 1 : 0;
@@ -71,70 +78,73 @@ Candidate evaluate(int M, int N, int K, int S, int dtype, int bn, int split_forc
     if (R == 0 && s > 1) break;
     if (s > 1 && kb / s < 4) break;  // keep each slice long enough to fill the pipeline
     const int tail_units = R * s;
-    const int grid = std::min(S, full * S + tail_units);
-    const int tail_waves = (tail_units + S - 1) / S;
+    const int grid_tiles = std::min(slots, full * slots + tail_units);
+    const int tail_waves = (tail_units + slots - 1) / slots;
     const int slice_kb = (kb + s - 1) / s;
     const double busiest_kb = double(full) * kb + double(tail_waves) * slice_kb;
     double t = busiest_kb * t_kb_us;
     // epilogue of the last tile is not hidden behind a main loop
     t += 128.0 * bn * 4 / (mc.feed_bytes_clk * mc.clk_ghz * 1e3);
+    const int grid = grid_tiles * ctas;
     if (s > 1) {
       // partial tiles: written once, read back once by the reducing slice
-      const double part_bytes = double(R) * s * 128.0 * bn * 4.0 * 2.0;
-      t += part_bytes / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
+      const double part_bytes = double(R) * s * tile_m * bn * 4.0 * 2.0;
+      t += part_bytes / (std::max(1, grid) * mc.part_gbs_per_sm * 1e3);
     }
     const double unique = (double(M) * K + double(K) * N) * es + double(M) * N * 2;
     const double t_hbm = unique / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
     t = std::max(t, t_hbm) + mc.launch_us;
-    const double eff = (double(tiles) * kb) / (double(grid) * busiest_kb);
-    if (t < best.est_us * 0.999) best = Candidate{bn, s, full, R, t, eff};
+    const double eff = (double(tiles) * kb) / (double(grid_tiles) * busiest_kb);
+    if (t < best.est_us * 0.999) best = Candidate{pair, bn, s, full, R, t, eff};
   }
   return best;
 }
 
 }  // namespace
 
-// Ticket counters of split tiles live in the first kTicketBytes of the
-// workspace. Tail tiles are fewer than the partition's SMs, so the SM count is
-// capped at the number of tickets.
-constexpr size_t kTicketBytes = 4096;
-constexpr int kMaxSms = static_cast<int>(kTicketBytes / 4);
-
 int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split, ek_gemm_plan* out) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(EK_ERR_INVALID, "GEMM dims must be positive");
-  if (S <= 0 || S > kMaxSms) return set_error(EK_ERR_INVALID, "num_sms must be in [1, %d], got %d", kMaxSms, S);
+  if (S <= 0 || S > kGemmMaxSms)
+    return set_error(EK_ERR_INVALID, "num_sms must be in [1, %d], got %d", kGemmMaxSms, S);
   if (dtype < 0 || dtype > 2) return set_error(EK_ERR_INVALID, "unknown dtype %d", dtype);
   if (dtype == EK_DTYPE_E4M3 && b_layout != EK_B_NK) return set_error(EK_ERR_UNSUPPORTED, "e4m3 B must be [N,K]");
-  static const int kBNs[4] = {256, 192, 128, 64};
-  Candidate best{0, 1, 0, 0, 1e30, 0};
-  for (int bn : kBNs) {
-    if (force_bn > 0 && bn != force_bn) continue;
-    Candidate c = evaluate(M, N, K, S, dtype, bn, force_split);
-    if (c.est_us < best.est_us * 0.98) best = c;  // prefer wider tiles on near ties
+  struct Mode {
+    int pair, bn;
+  };
+  // pair modes first: on a near tie the 2-SM tile streams fewer bytes per SM
+  static const Mode kModes[] = {{1, 256}, {1, 128}, {0, 256}, {0, 192}, {0, 128}, {0, 64}};
+  Candidate best{0, 0, 1, 0, 0, 1e30, 0};
+  for (const Mode& m : kModes) {
+    // force_bn > 0: one CTA per 128 x force_bn tile; < 0: a CTA pair per 256 x -force_bn tile
+    if (force_bn > 0 && (m.pair || m.bn != force_bn)) continue;
+    if (force_bn < 0 && (!m.pair || m.bn != -force_bn)) continue;
+    if (m.pair && S < 2) continue;
+    Candidate c = evaluate(M, N, K, S, dtype, m.pair, m.bn, force_split);
+    if (c.est_us < best.est_us * 0.98) best = c;
   }
-  if (best.bn == 0) return set_error(EK_ERR_INVALID, "no tile width matches force_bn=%d force_split=%d", force_bn,
-                                     force_split);
+  if (best.bn == 0)
+    return set_error(EK_ERR_INVALID, "no tile width matches force_bn=%d force_split=%d", force_bn, force_split);
   const int es = elem_bytes(dtype);
+  const int ctas = best.pair ? 2 : 1;
   ek_gemm_plan p{};
-  p.bm = 128;
+  p.bm = 128 * ctas;
   p.bn = best.bn;
   p.bk = 128 / es;
-  p.tiles_m = (M + 127) / 128;
+  p.cta_pair = best.pair;
+  p.tiles_m = (M + p.bm - 1) / p.bm;
   p.tiles_n = (N + best.bn - 1) / best.bn;
   p.k_blocks = (K + p.bk - 1) / p.bk;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.tail_split = best.split;
-  p.num_dp_tiles = best.split > 1 ? best.full_waves * S : p.num_tiles;
+  p.num_dp_tiles = best.split > 1 ? best.full_waves * (S / ctas) : p.num_tiles;
   const int tail = p.num_tiles - p.num_dp_tiles;
   p.num_units = p.num_dp_tiles + tail * best.split;
-  p.grid = std::min(S, p.num_units);
+  p.grid = std::min(S / ctas, p.num_units) * ctas;
   p.num_sms = S;
-  p.waves = (p.num_units + p.grid - 1) / p.grid;
+  p.waves = (p.num_units + p.grid / ctas - 1) / (p.grid / ctas);
   p.wave_efficiency = best.eff;
   p.est_us = best.est_us;
-  // Workspace: a fixed ticket region first (so tickets of one shape never land
-  // on another shape's partials in a reused buffer), then the fp32 partials.
-  p.workspace_bytes = best.split > 1 ? kTicketBytes + (size_t)tail * best.split * 128 * best.bn * 4 : 0;
+  p.workspace_bytes = best.split > 1 ? kGemmTicketBytes + (size_t)tail * best.split * p.bm * best.bn * 4 : 0;
   *out = p;
   return EK_OK;
 }
@@ -142,8 +152,7 @@ int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn
 namespace {
 
 template <class Cfg>
-int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& prm, int grid,
-               cudaStream_t stream) {
+int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid, cudaStream_t stream) {
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -155,20 +164,43 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
     if (rc) return rc;
     attr_done[dev] = true;
   }
-  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb2, prm);
-  return check_cuda(cudaGetLastError(), "gemm kernel launch");
+  if constexpr (Cfg::kPair) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<Cfg>, ta, tb, tb, prm), "gemm pair launch");
+  } else {
+    gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb, prm);
+    return check_cuda(cudaGetLastError(), "gemm kernel launch");
+  }
 }
 
 template <int kElem, bool kBMN, int kEpi>
-int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid,
-              cudaStream_t stream) {
-  switch (bn) {
-    case 64: return launch_cfg<GemmCfg<64, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
-    case 128: return launch_cfg<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
-    case 192: return launch_cfg<GemmCfg<192, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
-    case 256: return launch_cfg<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, tb, prm, grid, stream);
+int launch_mode(int pair, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid,
+                cudaStream_t stream) {
+  if (pair) {
+    switch (bn) {
+      case 128: return launch_cfg<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense, true>>(ta, tb, prm, grid, stream);
+      case 256: return launch_cfg<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense, true>>(ta, tb, prm, grid, stream);
+    }
+  } else {
+    switch (bn) {
+      case 64: return launch_cfg<GemmCfg<64, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, stream);
+      case 128: return launch_cfg<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, stream);
+      case 192: return launch_cfg<GemmCfg<192, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, stream);
+      case 256: return launch_cfg<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, stream);
+    }
   }
-  return set_error(EK_ERR_UNSUPPORTED, "tile width %d not built", bn);
+  return set_error(EK_ERR_UNSUPPORTED, "tile mode pair=%d bn=%d not built", pair, bn);
 }
 
 CUtensorMapDataType tma_dtype(int dtype) {
@@ -197,16 +229,25 @@ int gemm_common(const void* A, const void* B, void* C, const float* a_scale, con
   if (rc) return rc;
   if (plan.workspace_bytes > 0 && (!workspace || ws_bytes < plan.workspace_bytes || !aligned16(workspace)))
     return set_error(EK_ERR_INVALID, "workspace of %zu bytes required (got %zu)", plan.workspace_bytes, ws_bytes);
+  return launch_dense(plan, A, B, C, a_scale, b_scale, M, N, K, dtype, b_layout, workspace,
+                      static_cast<cudaStream_t>(stream));
+}
 
+}  // namespace
+
+int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C, const float* a_scale,
+                 const float* b_scale, int M, int N, int K, int dtype, int b_layout, void* workspace,
+                 cudaStream_t s) {
   const int es = elem_bytes(dtype);
   const CUtensorMapDataType tdt = tma_dtype(dtype);
+  const int bn_cta = plan.bn / (plan.cta_pair ? 2 : 1);
   CUtensorMap ta, tb;
-  rc = make_tmap_2d(&ta, A, tdt, K, M, (uint64_t)K * es, 128 / es, 128);
+  int rc = make_tmap_2d(&ta, A, tdt, K, M, (uint64_t)K * es, 128 / es, 128);
   if (rc) return rc;
   if (b_layout == EK_B_KN)
     rc = make_tmap_2d(&tb, B, tdt, N, K, (uint64_t)N * es, 64, 64);  // [K, N]: 64 N x 64 K boxes
   else
-    rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * es, 128 / es, plan.bn);
+    rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * es, 128 / es, bn_cta);
   if (rc) return rc;
 
   GemmParams prm{};
@@ -225,22 +266,19 @@ int gemm_common(const void* A, const void* B, void* C, const float* a_scale, con
   prm.a_scale = a_scale;
   prm.b_scale = b_scale;
   if (plan.workspace_bytes > 0) {
-    const int tail = plan.num_tiles - plan.num_dp_tiles;
     prm.ws_counters = static_cast<int*>(workspace);
-    prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
-    (void)tail;
+    prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kGemmTicketBytes);
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == EK_DTYPE_E4M3) return launch_bn<kE4M3, false, kEpiRowColScale>(plan.bn, ta, tb, prm, plan.grid, s);
+  if (dtype == EK_DTYPE_E4M3)
+    return launch_mode<kE4M3, false, kEpiRowColScale>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
   if (dtype == EK_DTYPE_BF16) {
-    if (b_layout == EK_B_KN) return launch_bn<kBF16, true, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
-    return launch_bn<kBF16, false, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+    if (b_layout == EK_B_KN) return launch_mode<kBF16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
+    return launch_mode<kBF16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
   }
-  if (b_layout == EK_B_KN) return launch_bn<kFP16, true, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
-  return launch_bn<kFP16, false, kEpiStore>(plan.bn, ta, tb, prm, plan.grid, s);
+  if (b_layout == EK_B_KN) return launch_mode<kFP16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
+  return launch_mode<kFP16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
 }
 
-}  // namespace
 }  // namespace ek
 
 using namespace ek;

@@ -5,12 +5,22 @@
 //               into one of two TMEM accumulators
 //   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> global
 //
+// Two MMA modes:
+//   single  one CTA computes a 128 x BN tile (tcgen05 cta_group::1)
+//   pair    a cluster of two CTAs computes a 256 x BN tile with the 2-SM
+//           MMA (cta_group::2): each CTA loads its own 128 rows of A and its
+//           own BN/2 rows (or columns) of B, the leader (cluster rank 0)
+//           issues the MMAs, and each CTA's TMEM receives its 128 rows. Per
+//           SM this streams 32 KB per 64-wide K step instead of 48 KB, which
+//           is what lets a full 148-SM device keep the tensor pipe fed. The
+//           loads carry no multicast: every CTA reads only its own half.
+//
 // The grid is the partition's SM count (or fewer CTAs when there is less
-// work); CTA c runs work units c, c + grid, c + 2*grid, ... A unit is one
+// work); CTA (or pair) c runs work units c, c + n, c + 2n, ... A unit is one
 // output tile, or one K-slice of a tile when the schedule splits the tail
-// wave (stream-K style). Split slices write fp32 partials to a caller-owned
-// workspace and the last slice to finish (atomic ticket) sums them in slice
-// order, so results do not depend on arrival order.
+// wave. Split slices write fp32 partials to a caller-owned workspace in a
+// thread-major layout (coalesced) and the last slice to finish (atomic
+// ticket) sums them in slice order, so results do not depend on arrival order.
 //
 // Three schedules share the main loop:
 //   kSchedDense    dense GEMM, grouped rasterisation, optional tail split
@@ -28,10 +38,14 @@ enum Elem : int { kBF16 = 0, kFP16 = 1, kE4M3 = 2 };
 enum Epi : int { kEpiStore = 0, kEpiRowColScale = 1, kEpiSwiGLU = 2, kEpiWeightedScatter = 3 };
 enum Sched : int { kSchedDense = 0, kSchedBlocks = 1, kSchedSegments = 2 };
 
-template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_>
+template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false>
 struct GemmCfg {
-  static constexpr int BM = 128;
-  static constexpr int BN = BN_;
+  static constexpr bool kPair = kPair_;
+  static constexpr int CTAS = kPair ? 2 : 1;
+  static constexpr int BM = 128;                 // rows per CTA
+  static constexpr int TILE_M = BM * CTAS;       // rows per work unit
+  static constexpr int BN = BN_;                 // columns per work unit
+  static constexpr int BN_CTA = BN / CTAS;       // B rows (K-major) / columns (MN-major) loaded per CTA
   static constexpr int kElem = kElem_;
   static constexpr bool kBMN = kBMN_;  // B stored MN-major ([K, N] row-major)
   static constexpr int kEpi = kEpi_;
@@ -41,18 +55,23 @@ struct GemmCfg {
   static constexpr int BK = 128 / ES;      // one 128-byte swizzle row of K
   static constexpr int UK = 32 / ES;       // K of one MMA instruction
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TX_BYTES = STAGE_BYTES * CTAS;  // bytes that complete one stage of the pair
   static constexpr int SMEM_BUDGET = 220 * 1024;
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                  : (2 * BN <= 256) ? 256 : 512;
-  static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, 128, BN);
+  static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int THREADS = 192;
+  static constexpr int EPI_WARPS = 4;
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(!kBMN || BN_CTA % 64 == 0, "MN-major B is loaded in 64-column chunks");
   static_assert(!(kF8 && kBMN), "e4m3 B must be K-major");
+  static_assert(!kPair || (kSched == kSchedDense && (kEpi == kEpiStore || kEpi == kEpiRowColScale)),
+                "the CTA-pair mode serves the dense schedule");
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
 };
 
@@ -88,10 +107,11 @@ struct Unit {
   int kb0, kb1;     // K-block range
   int split, nsplit;
   int tail_slot;    // index into the split workspace (dense tail tiles)
-  int a_row;        // first A row of the tile
+  int a_row;        // first A row of this CTA's part of the tile
   int row_end;      // rows >= row_end are not stored
   int b_row;        // first B row (K-major) / first K row offset (MN-major)
-  int b_col;        // first B column (MN-major)
+  int b_col;        // first B column (MN-major) of this CTA's part
+  int c_col;        // first output column of the tile
   bool valid;
 };
 
@@ -106,7 +126,7 @@ __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int g
 }
 
 template <class Cfg>
-__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows_runtime) {
+__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows_runtime, int rank) {
   Unit w;
   w.valid = true;
   w.split = 0;
@@ -126,12 +146,13 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
       w.kb1 = (int)((long long)(w.split + 1) * p.k_blocks / w.nsplit);
     }
     raster(tile, p.tiles_m, p.tiles_n, p.group_m, w.tm, w.tn);
-    w.a_row = w.tm * Cfg::BM;
+    w.a_row = w.tm * Cfg::TILE_M + rank * Cfg::BM;
     w.row_end = p.M;
     // K-major B: tile rows are output columns. MN-major B: rows are K, so the
     // tile starts at K row 0 and column tn*BN.
-    w.b_row = Cfg::kBMN ? 0 : w.tn * Cfg::BN;
-    w.b_col = w.tn * Cfg::BN;
+    w.b_row = Cfg::kBMN ? 0 : w.tn * Cfg::BN + rank * Cfg::BN_CTA;
+    w.b_col = w.tn * Cfg::BN + rank * Cfg::BN_CTA;
+    w.c_col = w.tn * Cfg::BN;
   } else if constexpr (Cfg::kSched == kSchedBlocks) {
     const int mblocks = rows_runtime / Cfg::BM;
     raster(u, mblocks, p.tiles_n, p.group_m, w.tm, w.tn);
@@ -145,6 +166,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     const int bn_rows = (Cfg::kEpi == kEpiSwiGLU) ? Cfg::BN / 2 : Cfg::BN;
     w.b_row = e * p.b_rows_per_expert + w.tn * bn_rows;
     w.b_col = 0;
+    w.c_col = w.tn * bn_rows;
   } else {  // kSchedSegments
     const int per_e = p.seg_mblocks * p.tiles_n;
     const int e = u / per_e;
@@ -159,6 +181,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     w.valid = (s1 > s0) && (w.a_row < w.row_end);
     w.b_row = e * p.N;  // K-row offset of the expert block in the [E*N, K] weight
     w.b_col = w.tn * Cfg::BN;
+    w.c_col = w.tn * Cfg::BN;
   }
   return w;
 }
@@ -238,6 +261,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, UK = Cfg::UK, STAGES = Cfg::STAGES;
+  constexpr int G = Cfg::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -254,6 +278,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int rank = Cfg::kPair ? (int)cluster_ctarank() : 0;  // position in the CTA pair
+  const bool leader = rank == 0;
+  const int unit0 = Cfg::kPair ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int unit_step = Cfg::kPair ? (int)nclusters_x() : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -262,7 +290,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 128);
+      mbar_init(&tempty_bar[b], Cfg::EPI_WARPS * G);  // one arrival per epilogue warp of the pair
     }
     mbar_init(drain_bar, 1);
     *s_abort = 0;
@@ -270,11 +298,12 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem_base, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc<G>(s_tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish<G>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (Cfg::kPair) cluster_sync();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem_base;
 
@@ -290,24 +319,38 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-        const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+      for (int u = unit0; u < nunits && ok; u += unit_step) {
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
         if (!w.valid) continue;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
-          tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
-          if constexpr (Cfg::kBMN) {
+          if constexpr (Cfg::kPair) {
+            // both CTAs' loads complete on the leader's full barrier
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
+            if constexpr (Cfg::kBMN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
-          } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
-            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
-            tma_load_2d(b_dst + (BN / 2) * 128, &tmB2, &full_bar[stage], kb * BK, w.b_row);
+              for (int j = 0; j < Cfg::BN_CTA / 64; ++j)
+                tma_load_2d_pair(b_dst + j * (BK * 128), &tmB, fb, w.b_col + 64 * j, w.b_row + kb * BK);
+            } else {
+              tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, w.b_row);
+            }
           } else {
-            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+            mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+            if constexpr (Cfg::kBMN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
+            } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+              tma_load_2d(b_dst + (BN / 2) * 128, &tmB2, &full_bar[stage], kb * BK, w.b_row);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+            }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -315,14 +358,14 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader of a pair)
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc_i = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-        const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+      for (int u = unit0; u < nunits && ok; u += unit_step) {
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
         if (!w.valid) continue;
         const int buf = acc_i & 1;
         const uint32_t aphase = (acc_i >> 1) & 1;
@@ -342,20 +385,36 @@ __global__ void __launch_bounds__(192, 1)
               bd = umma_desc_sw128(b0 + k * UK * 128, BK * 128, 1024);
             else
               bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
-            umma<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, (kb > w.kb0 || k > 0) ? 1u : 0u);
+            const uint32_t acc = (kb > w.kb0 || k > 0) ? 1u : 0u;
+            if constexpr (Cfg::kPair)
+              umma_pair<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, acc);
+            else
+              umma<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, acc);
           }
-          umma_commit(&empty_bar[stage]);
+          if constexpr (Cfg::kPair)
+            umma_commit_pair(&empty_bar[stage], 0x3);
+          else
+            umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[buf]);
+        if constexpr (Cfg::kPair)
+          umma_commit_pair(&tfull_bar[buf], 0x3);
+        else
+          umma_commit(&tfull_bar[buf]);
         ++acc_i;
       }
-      // Drain: wait until every MMA this thread issued has completed before the
-      // TMEM is released (also on the abort path).
-      umma_commit(drain_bar);
+      // Drain: every MMA issued so far has completed (in both CTAs' TMEM)
+      // before any TMEM is released, also on the abort path.
+      if constexpr (Cfg::kPair)
+        umma_commit_pair(drain_bar, 0x3);
+      else
+        umma_commit(drain_bar);
       volatile int never = 0;
       mbar_wait(drain_bar, 0, &never);
+    } else if (lane == 0 && Cfg::kPair) {
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never);  // the leader's drain commit also arrives here
     }
     __syncwarp();
   } else {
@@ -363,9 +422,20 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     const int epi_tid = threadIdx.x - 64;
+    const uint32_t tempty_leader0 = Cfg::kPair ? mapa_shared(smem_u32(&tempty_bar[0]), 0) : 0u;
+    auto release_tmem = [&](int buf) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (Cfg::kPair)
+          mbar_arrive_cluster(tempty_leader0 + buf * 8);
+        else
+          mbar_arrive(&tempty_bar[buf]);
+      }
+    };
     int acc_i = 0;
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-      const Unit w = decode_unit<Cfg>(p, u, rows_rt);
+    for (int u = unit0; u < nunits; u += unit_step) {
+      const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
       if (!w.valid) continue;
       const int buf = acc_i & 1;
       const uint32_t aphase = (acc_i >> 1) & 1;
@@ -385,14 +455,11 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(t_row + BN / 2 + c * 32, ru);
           tmem_ld_wait(rg);
           reg_dep(ru);
-          if (c == BN / 64 - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[buf]);
-          }
+          if (c == BN / 64 - 1) release_tmem(buf);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(rg[j])) * __uint_as_float(ru[j]);
-          if (row_ok) store_out_chunk<Cfg>(p, row, w.tn * (BN / 2) + c * 32, v);
+          if (row_ok) store_out_chunk<Cfg>(p, row, w.c_col + c * 32, v);
         }
       } else if constexpr (Cfg::kEpi == kEpiWeightedScatter) {
         int slot = p.num_slots;
@@ -404,80 +471,74 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld32(t_row + c * 32, r);
           tmem_ld_wait(r);
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[buf]);
-          }
+          if (c == BN / 32 - 1) release_tmem(buf);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * wt;
-          if (keep) store_out_chunk<Cfg>(p, slot, w.tn * BN + c * 32, v);
+          if (keep) store_out_chunk<Cfg>(p, slot, w.c_col + c * 32, v);
         }
       } else {
-        const int col_base = (Cfg::kSched == kSchedSegments) ? w.b_col : w.tn * BN;
         if (w.nsplit == 1) {
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(t_row + c * 32, r);
             tmem_ld_wait(r);
-            if (c == BN / 32 - 1) {
-              tc_fence_before();
-              mbar_arrive(&tempty_bar[buf]);
-            }
+            if (c == BN / 32 - 1) release_tmem(buf);
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (row_ok) finish_chunk<Cfg>(p, row, col_base + c * 32, v);
+            if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
           }
         } else {
-          // K-split slice: write the fp32 partial, take a ticket, and let the
+          // K-split slice: write this CTA's fp32 partial (thread-major, so a
+          // warp's float4 stores are contiguous), take a ticket, and let the
           // last slice reduce all partials in slice order.
-          float* part = p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + w.split) * BM + row_in_tile) * BN;
+          constexpr size_t kPart = (size_t)BM * BN;  // floats per CTA part
+          float4* part = reinterpret_cast<float4*>(
+              p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + w.split) * G + rank) * kPart);
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(t_row + c * 32, r);
             tmem_ld_wait(r);
-            if (c == BN / 32 - 1) {
-              tc_fence_before();
-              mbar_arrive(&tempty_bar[buf]);
-            }
-            float4* dst = reinterpret_cast<float4*>(part + c * 32);
+            if (c == BN / 32 - 1) release_tmem(buf);
 #pragma unroll
             for (int g = 0; g < 8; ++g)
-              __stcg(dst + g, make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
-                                          __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+              __stcg(part + (c * 8 + g) * BM + row_in_tile,
+                     make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                 __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
           }
           __threadfence();
           named_bar_sync(1, 128);
+          const int ticket = w.tail_slot * G + rank;
           if (epi_tid == 0) {
-            const int old = atomicAdd(&p.ws_counters[w.tail_slot], 1);
+            const int old = atomicAdd(&p.ws_counters[ticket], 1);
             const int last = (old == w.nsplit - 1);
-            if (last) p.ws_counters[w.tail_slot] = 0;  // ready for the next launch
+            if (last) p.ws_counters[ticket] = 0;  // ready for the next launch
             *s_last = last;
           }
           named_bar_sync(1, 128);
           if (*s_last) {
             __threadfence();
-            const float* part0 = p.ws_partial + ((size_t)(w.tail_slot * w.nsplit) * BM + row_in_tile) * BN;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
               float v[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
               for (int s = 0; s < w.nsplit; ++s) {
-                const float4* src = reinterpret_cast<const float4*>(part0 + (size_t)s * BM * BN + c * 32);
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + s) * G + rank) * kPart);
 #pragma unroll
                 for (int g = 0; g < 8; ++g) {
-                  const float4 t = __ldcg(src + g);
+                  const float4 t = __ldcg(src + (c * 8 + g) * BM + row_in_tile);
                   v[4 * g] += t.x;
                   v[4 * g + 1] += t.y;
                   v[4 * g + 2] += t.z;
                   v[4 * g + 3] += t.w;
                 }
               }
-              if (row_ok) finish_chunk<Cfg>(p, row, col_base + c * 32, v);
+              if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
             }
           }
         }
@@ -488,9 +549,10 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (Cfg::kPair) cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    tmem_dealloc<G>(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

@@ -23,35 +23,21 @@
 //    (cudaGetSymbolAddress, with that device current) and caches it. Make that
 //    first call before any stream capture is under way on the device.
 //  * Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
+//
+// The kernel, schedule and launch are those of ek_gemm (launch_dense), so the
+// two entry points compute identical results for the same inputs.
 #include <mutex>
 
-#include "ek_gemm_kernel.cuh"
 #include "ek_internal.h"
 
 namespace ek {
-
-int register_status_reader(int (*fn)(int, int*));
-int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split, ek_gemm_plan* out);
-
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 32u << 20;  // 32 MiB per device
-constexpr size_t kTicketBytes = 4096;                // same split layout as ek_gemm
 
 // Host code must not use this name as an address: it is a host-side stand-in.
 // Kernels get the device address obtained by cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-
-int read_status(int clear, int* v) {
-  int rc = check_cuda(cudaMemcpyFromSymbol(v, g_ek_status, sizeof(int)), "read status");
-  if (rc) return rc;
-  if (clear) {
-    int z = 0;
-    rc = check_cuda(cudaMemcpyToSymbol(g_ek_status, &z, sizeof(int)), "clear status");
-  }
-  return rc;
-}
-const int s_status_reg = register_status_reader(read_status);
 
 // Device address of g_noalloc_scratch, looked up once per device.
 int scratch_address(void** out) {
@@ -70,34 +56,6 @@ int scratch_address(void** out) {
   }
   *out = addr[dev];
   return EK_OK;
-}
-
-template <class Cfg>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid, cudaStream_t s) {
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
-  if (!attr_done[dev]) {
-    int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg::SMEM_BYTES),
-                        "cudaFuncSetAttribute(smem)");
-    if (rc) return rc;
-    attr_done[dev] = true;
-  }
-  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tb, prm);
-  return check_cuda(cudaGetLastError(), "no-alloc gemm launch");
-}
-
-template <int kElem, bool kBMN>
-int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid, cudaStream_t s) {
-  switch (bn) {
-    case 64: return launch<GemmCfg<64, kElem, kBMN, kEpiStore, kSchedDense>>(ta, tb, prm, grid, s);
-    case 128: return launch<GemmCfg<128, kElem, kBMN, kEpiStore, kSchedDense>>(ta, tb, prm, grid, s);
-    case 192: return launch<GemmCfg<192, kElem, kBMN, kEpiStore, kSchedDense>>(ta, tb, prm, grid, s);
-    case 256: return launch<GemmCfg<256, kElem, kBMN, kEpiStore, kSchedDense>>(ta, tb, prm, grid, s);
-  }
-  return set_error(EK_ERR_UNSUPPORTED, "tile width %d not built", bn);
 }
 
 }  // namespace
@@ -134,43 +92,12 @@ int ek_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K, 
   void* scratch = nullptr;
   if ((rc = scratch_address(&scratch))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-
-  const CUtensorMapDataType tdt =
-      dtype == EK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap ta, tb;
-  if ((rc = make_tmap_2d(&ta, A, tdt, K, M, (uint64_t)K * 2, 64, 128))) return rc;
-  if (b_layout == EK_B_KN)
-    rc = make_tmap_2d(&tb, B, tdt, N, K, (uint64_t)N * 2, 64, 64);
-  else
-    rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * 2, 64, plan.bn);
-  if (rc) return rc;
-
-  GemmParams prm{};
-  prm.M = M;
-  prm.N = N;
-  prm.K = K;
-  prm.tiles_m = plan.tiles_m;
-  prm.tiles_n = plan.tiles_n;
-  prm.k_blocks = plan.k_blocks;
-  prm.num_dp_tiles = plan.num_dp_tiles;
-  prm.tail_split = plan.tail_split;
-  prm.num_units = plan.num_units;
-  prm.group_m = 8;
-  prm.C = C;
-  prm.ldc = N;
   if (plan.workspace_bytes > 0) {
     // the ticket counters must start at zero for every launch
-    rc = check_cuda(cudaMemsetAsync(scratch, 0, kTicketBytes, s), "clear no-alloc tickets");
+    rc = check_cuda(cudaMemsetAsync(scratch, 0, kGemmTicketBytes, s), "clear no-alloc tickets");
     if (rc) return rc;
-    prm.ws_counters = static_cast<int*>(scratch);
-    prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + kTicketBytes);
   }
-  if (dtype == EK_DTYPE_BF16) {
-    if (b_layout == EK_B_KN) return launch_bn<kBF16, true>(plan.bn, ta, tb, prm, plan.grid, s);
-    return launch_bn<kBF16, false>(plan.bn, ta, tb, prm, plan.grid, s);
-  }
-  if (b_layout == EK_B_KN) return launch_bn<kFP16, true>(plan.bn, ta, tb, prm, plan.grid, s);
-  return launch_bn<kFP16, false>(plan.bn, ta, tb, prm, plan.grid, s);
+  return launch_dense(plan, A, B, C, nullptr, nullptr, M, N, K, dtype, b_layout, scratch, s);
 }
 
 }  // extern "C"

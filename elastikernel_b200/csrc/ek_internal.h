@@ -41,4 +41,21 @@ int device_sm_count(int* out);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Split-K workspace layout of the dense GEMM: ticket counters first (a fixed
+// region, so tickets of one shape never land on another shape's partials in
+// a reused buffer), then the fp32 partial tiles.
+constexpr size_t kGemmTicketBytes = 8192;
+constexpr int kGemmMaxSms = 1024;  // tail tiles (< SMs) x 2 CTAs fit the ticket region
+
+// Dense GEMM schedule for a partition of S SMs (ek_gemm_plan_make).
+int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split,
+               ek_gemm_plan* out);
+
+// Launch the dense GEMM kernel for `plan` on `stream`. `workspace` must hold
+// plan.workspace_bytes bytes whose ticket region is zero (unused when the
+// plan does not split). a_scale / b_scale only for e4m3.
+int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C, const float* a_scale,
+                 const float* b_scale, int M, int N, int K, int dtype, int b_layout, void* workspace,
+                 cudaStream_t stream);
+
 }  // namespace ek

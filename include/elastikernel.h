@@ -98,7 +98,8 @@ int ek_gctx_fake_driver(int enable, int total_sms, int granularity, int fail_cal
 
 /* Tile schedule chosen for a GEMM of this shape on a partition of num_sms SMs. */
 typedef struct ek_gemm_plan {
-  int bm, bn, bk;          /* tile shape (bk in elements)                        */
+  int bm, bn, bk;          /* tile shape (bk in elements); bm = 256 for CTA pairs */
+  int cta_pair;            /* 1: 2-SM MMA, two CTAs (a cluster) per tile         */
   int tiles_m, tiles_n;    /* output tiles along M and N                         */
   int k_blocks;            /* bk-wide steps along K                              */
   int num_tiles;           /* tiles_m * tiles_n                                  */
@@ -114,7 +115,9 @@ typedef struct ek_gemm_plan {
 } ek_gemm_plan;
 
 /* Plan a GEMM C[M,N] = A[M,K] * B on num_sms SMs (num_sms > 0 required here).
- * force_bn / force_split > 0 pin the tile width / tail split (0 = choose). */
+ * force_bn pins the tile: > 0 one CTA per 128 x force_bn tile (64/128/192/256),
+ * < 0 a CTA pair per 256 x -force_bn tile (128/256), 0 = choose.
+ * force_split > 0 pins the tail split (0 = choose). */
 int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
                       ek_gemm_plan* out);
 

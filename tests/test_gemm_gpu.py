@@ -55,6 +55,36 @@ def test_gemm_tiles_and_splits(cuda_dev, bn, split):
         assert err <= TOL, f"bn={bn} split={split} sms={sms}: {err:.3e}"
 
 
+@pytest.mark.parametrize("bn", [-128, -256])
+@pytest.mark.parametrize("split", [1, 2, 3])
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+def test_gemm_cta_pair_mode(cuda_dev, bn, split, layout):
+    """2-SM MMA (CTA pair per 256 x |bn| tile), ragged shapes, split tails."""
+    from elastikernel_b200 import _ops
+
+    M, N, K = 1000, 1032, 1536
+    a, b, da, db = _inputs(M, N, K, torch.bfloat16, layout, cuda_dev, seed=-bn + split)
+    ref = gemm_ref(a, b, layout)
+    for sms in (16, 148):
+        p = _ops.plan(M, N, K, sms, torch.bfloat16, layout, bn, split)
+        assert p["cta_pair"] == 1 and p["bm"] == 256
+        c = _ops.gemm(da, db, num_sms=sms, b_layout=layout, force_bn=bn, force_split=split)
+        torch.cuda.synchronize()
+        err = max_rel_err(c, ref)
+        assert err <= TOL, f"pair bn={-bn} split={split} sms={sms} {layout}: {err:.3e}"
+
+
+def test_gemm_pair_vs_single_identical_math(cuda_dev):
+    """Both MMA modes accumulate each output in the same K order: results match closely."""
+    from elastikernel_b200 import _ops
+
+    a, b, da, db = _inputs(2048, 2048, 2048, torch.bfloat16, "kn", cuda_dev, seed=3)
+    c1 = _ops.gemm(da, db, force_bn=256, force_split=1)
+    c2 = _ops.gemm(da, db, force_bn=-256, force_split=1)
+    torch.cuda.synchronize()
+    assert max_rel_err(c1, c2.float().cpu().numpy()) <= 1e-3
+
+
 def test_gemm_fp16_reference_dtype(cuda_dev):
     """The reference benchmarks fp16 (sm_aware_matmul.py:263-264)."""
     from elastikernel_b200 import _ops

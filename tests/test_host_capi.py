@@ -150,7 +150,10 @@ def test_planner_invariants(S, M):
     N = K = 4096
     p = _ops.plan(M, N, K, S)
     assert p["bn"] in (64, 128, 192, 256)
-    assert p["tiles_m"] == -(-M // 128) and p["tiles_n"] == -(-N // p["bn"])
+    assert p["bm"] == (256 if p["cta_pair"] else 128)
+    if p["cta_pair"]:
+        assert p["bn"] in (128, 256) and p["grid"] % 2 == 0
+    assert p["tiles_m"] == -(-M // p["bm"]) and p["tiles_n"] == -(-N // p["bn"])
     assert p["num_units"] == p["num_dp_tiles"] + (p["num_tiles"] - p["num_dp_tiles"]) * p["tail_split"]
     assert 1 <= p["grid"] <= S
     assert 0 < p["wave_efficiency"] <= 1.0
