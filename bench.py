@@ -80,6 +80,10 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            # let nvidia-smi finish its start-up (NVML init) before the timed region
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and self.path.stat().st_size == 0:
+                time.sleep(0.05)
             time.sleep(0.3)
         except Exception:
             self.proc = None
@@ -201,6 +205,36 @@ def partition_sweep(dev, peak_tflops: float, steps: int) -> dict:
     return out
 
 
+def fp8_bench(dev, peak_bf16_tflops: float, steps: int) -> dict:
+    """FP8 e4m3 GEMM 4096 x 14336 x 4096 with per-row / per-channel scales on
+    the full device and a 74-SM request (rounded up to the alignment)."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.green_ctx import create_sm_partition, get_total_sm_count
+    from elastikernel_b200.timing import time_on_stream
+
+    Mf, Nf, Kf = 4096, 14336, 4096
+    flop = 2.0 * Mf * Nf * Kf
+    peak_fp8 = 2.0 * peak_bf16_tflops  # dense e4m3 rate is twice bf16 on B200
+    g = torch.Generator(device=dev).manual_seed(0)
+    aq, a_s = _ops.quant_e4m3(torch.randn((Mf, Kf), device=dev, generator=g))
+    wq, w_s = _ops.quant_e4m3(torch.randn((Nf, Kf), device=dev, generator=g))
+    total = get_total_sm_count(dev)
+    res = []
+    for req in (total, 74):
+        stream, actual = (torch.cuda.current_stream(dev), total) if req >= total else create_sm_partition(dev, req)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                _ops.gemm_fp8(aq, wq, a_s, w_s)
+            r = time_on_stream(lambda: _ops.gemm_fp8(aq, wq, a_s, w_s), stream, reps=max(3, steps // 2))
+        tf = flop / (r["mean_ms"] * 1e-3) / 1e12
+        p = _ops.plan(Mf, Nf, Kf, actual, _ops._FP8, "nk")
+        res.append({"sm_request": req, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
+                    "tflops": round(tf, 1), "pct_scaled_fp8_peak": round(100 * tf / (peak_fp8 * actual / 148), 1),
+                    "bm": p["bm"], "bn": p["bn"], "split": p["tail_split"]})
+    return {"config": "e4m3 4096x14336x4096, per-row A / per-channel W fp32 scales, bf16 out",
+            "fp8_peak_tflops": peak_fp8, "peak_note": "2 x measured bf16 burst", "results": res}
+
+
 def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:
     """Mixtral-shaped fused MoE (E=8, top-2, H=4096, I=14336, bf16) tokens/s."""
     from elastikernel_b200 import _ops
@@ -278,7 +312,7 @@ def run_reference(args, rank: int, world: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the partition sweep, MoE and CPU legs")
@@ -360,6 +394,7 @@ def main() -> None:
     extras = {}
     if not args.no_extras:
         extras["partitions"] = partition_sweep(dev, peak_tf, args.steps)
+        extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
         extras["moe"] = moe_bench(dev, args.steps, hbm)
         if rank == 0 and world == 1:
             extras["cpu_baseline"] = cpu_baseline_sample()
@@ -372,7 +407,8 @@ def main() -> None:
         return
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+        "ms_per_step_median": round(statistics.median(per), 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 0",
         "config": {"workload": "bf16 GEMM 4096x4096x4096 on the full 148-SM device (N=K=4096 wave sweep, "
                                "square point); replicas per GPU", "M": M, "N": N, "K": K,

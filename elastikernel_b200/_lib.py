@@ -64,10 +64,12 @@ _SIGNATURES = {
     "ek_gctx_fake_driver": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "ek_gemm_plan_make": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                    ctypes.POINTER(GemmPlan)]),
+    "ek_gemm_workspace_bytes": (_c_size, [_c_int] * 8),
     "ek_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                          _c_vp, _c_size, _c_vp]),
     "ek_gemm_fp8": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                              _c_vp, _c_size, _c_vp]),
+    "ek_quant_e4m3": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_gemm_noalloc": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _c_vp]),
     "ek_gemm_noalloc_max_scratch_bytes": (_c_size, []),

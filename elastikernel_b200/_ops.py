@@ -88,15 +88,17 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, num_
         return out
     if K == 0:
         return out.zero_()
+    L = lib()
     stream = current_stream_handle(dev)
-    ns = int(num_sms) if num_sms else 0
-    sms = ns if ns > 0 else _stream_sms(dev, stream)
-    p = plan(M, N, K, sms, a.dtype, b_layout, force_bn, force_split)
-    ws = _workspace.get(dev, stream, p["workspace_bytes"])
-    with torch.cuda.device(dev):
-        check(lib().ek_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _DTYPES[a.dtype], bl, sms,
-                            int(force_bn), int(force_split), _ptr(ws), 0 if ws is None else ws.numel(), stream),
-              "ek_gemm")
+    sms = int(num_sms) if num_sms else _stream_sms(dev, stream)
+    dt = _DTYPES[a.dtype]
+    need = L.ek_gemm_workspace_bytes(M, N, K, sms, dt, bl, int(force_bn), int(force_split))
+    if need == _SIZE_MAX:
+        check(_lib.EK_ERR_INVALID, "ek_gemm_workspace_bytes")
+    ws = _workspace.get(dev, stream, need)
+    with _on_device(dev):
+        check(L.ek_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, dt, bl, sms, int(force_bn),
+                        int(force_split), _ptr(ws), 0 if ws is None else ws.numel(), stream), "ek_gemm")
     return out
 
 
@@ -118,15 +120,63 @@ def gemm_fp8(a_q: torch.Tensor, w_q: torch.Tensor, a_scale: torch.Tensor, w_scal
     if out is None:
         out = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
     stream = current_stream_handle(dev)
-    ns = int(num_sms) if num_sms else 0
-    sms = ns if ns > 0 else _stream_sms(dev, stream)
-    p = plan(M, N, K, sms, _FP8, "nk", force_bn, force_split)
-    ws = _workspace.get(dev, stream, p["workspace_bytes"])
-    with torch.cuda.device(dev):
+    sms = int(num_sms) if num_sms else _stream_sms(dev, stream)
+    need = lib().ek_gemm_workspace_bytes(M, N, K, sms, _lib.EK_DTYPE_E4M3, _lib.EK_B_NK, int(force_bn),
+                                         int(force_split))
+    if need == _SIZE_MAX:
+        check(_lib.EK_ERR_INVALID, "ek_gemm_workspace_bytes")
+    ws = _workspace.get(dev, stream, need)
+    with _on_device(dev):
         check(lib().ek_gemm_fp8(a_q.data_ptr(), w_q.data_ptr(), a_scale.data_ptr(), w_scale.data_ptr(),
                                 out.data_ptr(), M, N, K, sms, int(force_bn), int(force_split), _ptr(ws),
                                 0 if ws is None else ws.numel(), stream), "ek_gemm_fp8")
     return out
+
+
+def quant_e4m3(x: torch.Tensor, block: tuple[int, int] = (1, 0)) -> tuple[torch.Tensor, torch.Tensor]:
+    """e4m3 codes and fp32 scales (amax / 448 per block) of a bf16/fp32 [rows, cols] tensor.
+
+    block = (1, 0): one scale per row; (1, 128): per 1 x 128 group;
+    (br, bc): per br x bc block. Scales come back shaped [ceil(rows/br), ceil(cols/bc)]
+    (or [rows] for row-wise)."""
+    dev = _require_cuda(x)
+    if x.dtype not in (torch.bfloat16, torch.float32) or x.dim() != 2:
+        raise RuntimeError("quant_e4m3 takes a 2-D bf16 or fp32 tensor")
+    _contig("x", x)
+    if _FP8 is None:
+        raise RuntimeError("this torch has no float8_e4m3fn")
+    rows, cols = x.shape
+    br, bc = int(block[0]), int(block[1])
+    q = torch.empty((rows, cols), dtype=_FP8, device=dev)
+    if br == 1 and bc <= 0:
+        scales = torch.empty(rows, dtype=torch.float32, device=dev)
+    else:
+        scales = torch.empty((-(-rows // br), -(-cols // bc)), dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        check(lib().ek_quant_e4m3(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols, br, bc,
+                                  q.data_ptr(), scales.data_ptr(), current_stream_handle(dev)), "ek_quant_e4m3")
+    return q, scales
+
+
+_SIZE_MAX = ctypes.c_size_t(-1).value
+_DEV_SMS: dict[int, int] = {}
+
+
+class _NullCtx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NULL = _NullCtx()
+
+
+def _on_device(dev: torch.device):
+    """Make `dev` current for a launch (a no-op when it already is)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    return _NULL if torch.cuda.current_device() == idx else torch.cuda.device(dev)
 
 
 def _stream_sms(dev: torch.device, stream: int) -> int:
@@ -135,7 +185,11 @@ def _stream_sms(dev: torch.device, stream: int) -> int:
     check(lib().ek_gctx_stream_sm_count(ctypes.c_void_p(stream), ctypes.byref(v)), "ek_gctx_stream_sm_count")
     if v.value > 0:
         return v.value
-    return torch.cuda.get_device_properties(dev).multi_processor_count
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    n = _DEV_SMS.get(idx)
+    if n is None:
+        n = _DEV_SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n
 
 
 # ---------------------------------------------------------------------- MoE
@@ -152,7 +206,7 @@ def moe_route(gate_logits: torch.Tensor, topk: int) -> tuple[torch.Tensor, torch
     T, E = gate_logits.shape
     ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
     wts = torch.empty((T, topk), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_route(gate_logits.data_ptr(), T, E, int(topk), ids.data_ptr(), wts.data_ptr(),
                                  current_stream_handle(dev)), "ek_moe_route")
     return ids, wts
@@ -184,7 +238,7 @@ def moe_permute(topk_ids: torch.Tensor, num_experts: int, x: torch.Tensor | None
         es = x.element_size()
         x_perm = torch.empty((max_rows, H), dtype=x.dtype, device=dev)
     scratch = torch.empty(int(lib().ek_moe_permute_scratch_bytes(T, k, E)), dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_permute(topk_ids.data_ptr(), T, k, E, block_m, sorted_slots.data_ptr(),
                                    block_expert.data_ptr(), num_rows.data_ptr(), counts.data_ptr(), _ptr(x), H, es,
                                    _ptr(x_perm), scratch.data_ptr(), current_stream_handle(dev)), "ek_moe_permute")
@@ -212,7 +266,7 @@ def moe_gate_up(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: int | N
     max_rows = perm["max_rows"]
     act = torch.empty((max_rows, I), dtype=torch.bfloat16, device=dev)
     stream = current_stream_handle(dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_gate_up(x_perm.data_ptr(), w1.data_ptr(), w3.data_ptr(), perm["block_expert"].data_ptr(),
                                    perm["num_rows_padded"].data_ptr(), act.data_ptr(), max_rows, E, H, I,
                                    int(num_sms or 0), int(force_bn), stream), "ek_moe_gate_up")
@@ -233,7 +287,7 @@ def moe_down(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torc
     if act.shape[1] != I or E != perm["E"] or topk_weights.numel() != T * k:
         raise RuntimeError("down: shape mismatch")
     y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_down(act.data_ptr(), w2.data_ptr(), perm["block_expert"].data_ptr(),
                                 perm["num_rows_padded"].data_ptr(), perm["sorted_slots"].data_ptr(),
                                 topk_weights.data_ptr(), y.data_ptr(), perm["max_rows"], E, H, I, T, k,
@@ -250,7 +304,7 @@ def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = N
         out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     else:
         _check_bf16("out", out)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_combine(y.data_ptr(), out.data_ptr(), int(T), int(topk), H, current_stream_handle(dev)),
               "ek_moe_combine")
     return out
@@ -285,7 +339,7 @@ def moe_segment_gemm(hidden_states: torch.Tensor, weights: torch.Tensor, expert_
     M = hidden_states.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=hidden_states.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         check(lib().ek_moe_segment_gemm(hidden_states.data_ptr(), weights.data_ptr(), expert_offsets.data_ptr(),
                                         out.data_ptr(), M, int(N), int(K), int(num_experts),
                                         _DTYPES[hidden_states.dtype], int(num_sms or 0),

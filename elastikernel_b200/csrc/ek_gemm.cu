@@ -10,6 +10,7 @@
 // function of (M, N, K, S, dtype); no autotuning runs in the hot path.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "ek_gemm_kernel.cuh"
 #include "ek_internal.h"
@@ -102,7 +103,39 @@ Candidate evaluate(int M, int N, int K, int S, int dtype, int pair, int bn, int 
 
 }  // namespace
 
+static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split,
+                               ek_gemm_plan* out);
+
+// Plans are pure functions of their inputs; a small per-thread cache keeps
+// repeated calls of one shape (the common case) from re-running the model.
 int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split, ek_gemm_plan* out) {
+  struct Entry {
+    int key[8];
+    ek_gemm_plan plan;
+    bool used;
+  };
+  constexpr int kEntries = 32;
+  static thread_local Entry cache[kEntries];
+  static thread_local int next = 0;
+  const int key[8] = {M, N, K, S, dtype, b_layout, force_bn, force_split};
+  for (int i = 0; i < kEntries; ++i) {
+    if (cache[i].used && memcmp(cache[i].key, key, sizeof(key)) == 0) {
+      *out = cache[i].plan;
+      return EK_OK;
+    }
+  }
+  int rc = plan_dense_uncached(M, N, K, S, dtype, b_layout, force_bn, force_split, out);
+  if (rc) return rc;
+  Entry& e = cache[next];
+  next = (next + 1) % kEntries;
+  memcpy(e.key, key, sizeof(key));
+  e.plan = *out;
+  e.used = true;
+  return EK_OK;
+}
+
+static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split,
+                               ek_gemm_plan* out) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(EK_ERR_INVALID, "GEMM dims must be positive");
   if (S <= 0 || S > kGemmMaxSms)
     return set_error(EK_ERR_INVALID, "num_sms must be in [1, %d], got %d", kGemmMaxSms, S);
@@ -290,6 +323,13 @@ int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout,
   clear_error();
   if (!out) return set_error(EK_ERR_INVALID, "null plan");
   return plan_dense(M, N, K, num_sms, dtype, b_layout, force_bn, force_split, out);
+}
+
+size_t ek_gemm_workspace_bytes(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn,
+                               int force_split) {
+  ek_gemm_plan p;
+  if (plan_dense(M, N, K, num_sms, dtype, b_layout, force_bn, force_split, &p) != EK_OK) return (size_t)-1;
+  return p.workspace_bytes;
 }
 
 int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,

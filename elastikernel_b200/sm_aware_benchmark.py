@@ -1,0 +1,198 @@
+"""SM-aware kernel benchmark suite (drop-in for elastikernel/sm_aware_benchmark.py).
+
+Usage:
+    python -m elastikernel_b200.sm_aware_benchmark --gemm
+    python -m elastikernel_b200.sm_aware_benchmark --moe
+    python -m elastikernel_b200.sm_aware_benchmark --all
+
+GEMM: vanilla (planned for the full device) vs SM-aware (planned for the
+partition) tcgen05 GEMM under green-context partitions, with the wave
+analysis of the schedule actually run (sm_aware_benchmark.py:17-181).
+
+MoE: the reference's segment "fused MoE" (grouped GEMM over CSR expert
+segments with its fake contiguous routing, sm_aware_benchmark.py:184-468),
+vanilla vs SM-aware, plus the full fused-MoE layer (routing, permutation,
+SwiGLU gate/up, weighted down-projection, combine) at Mixtral shapes.
+"""
+from __future__ import annotations
+
+import argparse
+
+
+def call_moe_vanilla(hidden_states, weights, expert_offsets, num_experts, N, K):
+    """Segment GEMM with the reference kernel's semantics (sm_aware_benchmark.py:351-370),
+    planned for the full device."""
+    import torch
+
+    from . import _ops
+
+    total = torch.cuda.get_device_properties(hidden_states.device).multi_processor_count
+    return _ops.moe_segment_gemm(hidden_states, weights, expert_offsets, num_experts, N, K, num_sms=total)
+
+
+def call_moe_sm_aware(hidden_states, weights, expert_offsets, num_experts, N, K, num_sms=None):
+    """Segment GEMM planned for `num_sms` SMs (None: the current stream's partition)
+    (sm_aware_benchmark.py:372-391)."""
+    from . import _ops
+
+    return _ops.moe_segment_gemm(hidden_states, weights, expert_offsets, num_experts, N, K, num_sms=num_sms)
+
+
+def _partition(dev, sm_count, total):
+    from .green_ctx import create_sm_partition, full_device_partition
+
+    if sm_count >= total:
+        return full_device_partition(dev)
+    return create_sm_partition(dev, sm_count)
+
+
+def run_gemm_benchmark(sm_levels=None, test_cases=None, rep_ms: float = 30.0) -> list:
+    """Vanilla vs SM-aware GEMM per partition size (sm_aware_benchmark.py:17-181)."""
+    import torch
+
+    from . import sm_aware_matmul as smm
+    from .green_ctx import get_sm_alignment, get_total_sm_count
+    from .timing import time_on_stream
+
+    dev = torch.device("cuda:0")
+    total_sms = get_total_sm_count(dev)
+    min_sm, align = get_sm_alignment(dev)
+    print(f"GEMM Benchmark on {torch.cuda.get_device_name(dev)}")
+    print(f"Total SMs: {total_sms}, alignment: min={min_sm}, align={align}")
+    sm_levels = [s for s in (sm_levels or [16, 32, 48, 64, 96, 132, total_sms]) if s <= total_sms]
+    square_cases = [(1024, 1024, 1024), (2048, 2048, 2048), (4096, 4096, 4096)]
+    m_sweep_cases = [(M, 4096, 4096) for M in [1, 16, 32, 64, 128, 256, 512, 1024, 2048]]
+    results = []
+    for M, N, K in test_cases or (square_cases + m_sweep_cases):
+        print(f"\n{'=' * 80}\nGEMM: M={M}, N={N}, K={K}\n{'=' * 80}")
+        print(f"  {'SM':>4} {'Vanilla(us)':>11} {'Aware(us)':>11} {'Speedup':>8}  {'TFLOP/s':>8}  schedule")
+        torch.manual_seed(0)
+        a = torch.randn((M, K), device=dev, dtype=torch.bfloat16)
+        b = torch.randn((K, N), device=dev, dtype=torch.bfloat16)
+        for sm_count in sm_levels:
+            try:
+                stream, actual = _partition(dev, sm_count, total_sms)
+                with torch.cuda.stream(stream):
+                    for _ in range(3):
+                        smm.call_vanilla(a, b)
+                        smm.call_sm_aware(a, b, actual)
+                    van = time_on_stream(lambda: smm.call_vanilla(a, b), stream, rep_ms=rep_ms)
+                    aw = time_on_stream(lambda: smm.call_sm_aware(a, b, actual), stream, rep_ms=rep_ms)
+                p = smm.tcgen05_schedule(M, N, K, actual)
+                sp = van["mean_ms"] / aw["mean_ms"] if aw["mean_ms"] > 0 else 0.0
+                tf = 2.0 * M * N * K / (aw["mean_ms"] * 1e-3) / 1e12
+                mode = f"{p['bm']}x{p['bn']}{' pair' if p['cta_pair'] else ''} split={p['tail_split']}"
+                print(f"  {sm_count:>4} {van['mean_ms'] * 1e3:>11.1f} {aw['mean_ms'] * 1e3:>11.1f} {sp:>7.2f}x  "
+                      f"{tf:>8.1f}  {mode} eff={p['wave_efficiency'] * 100:.1f}%")
+                results.append({"M": M, "N": N, "K": K, "sm": sm_count, "actual": actual,
+                                "vanilla_us": van["mean_ms"] * 1e3, "aware_us": aw["mean_ms"] * 1e3,
+                                "tflops": tf, "plan": p})
+            except Exception as e:
+                print(f"  {sm_count:>4}  Error: {e}")
+    return results
+
+
+def _fake_offsets(num_tokens, num_experts, top_k, dev):
+    """The reference's uniform fake routing (sm_aware_benchmark.py:438-444)."""
+    import torch
+
+    tpe = (num_tokens * top_k) // num_experts
+    offs = [0] + [min((i + 1) * tpe, num_tokens) for i in range(num_experts)]
+    offs[-1] = num_tokens
+    return torch.tensor(offs, dtype=torch.int32, device=dev)
+
+
+def run_moe_benchmark(sm_levels=None, moe_configs=None, rep_ms: float = 30.0, full_layer: bool = True) -> list:
+    """Segment-GEMM MoE of the reference, vanilla vs SM-aware, per partition
+    size; then the full fused-MoE layer at Mixtral shapes."""
+    import torch
+
+    from . import _ops
+    from .green_ctx import get_sm_alignment, get_total_sm_count
+    from .timing import time_on_stream
+
+    dev = torch.device("cuda:0")
+    total_sms = get_total_sm_count(dev)
+    min_sm, align = get_sm_alignment(dev)
+    print(f"\n{'=' * 80}\nFused MoE Benchmark on {torch.cuda.get_device_name(dev)}")
+    print(f"Total SMs: {total_sms}, alignment: min={min_sm}, align={align}\n{'=' * 80}")
+    sm_levels = [s for s in (sm_levels or [16, 32, 48, 64, total_sms]) if s <= total_sms]
+    moe_configs = moe_configs or [
+        {"num_tokens": 128, "hidden_dim": 4096, "intermediate_dim": 4096, "num_experts": 8, "top_k": 2},
+        {"num_tokens": 512, "hidden_dim": 4096, "intermediate_dim": 4096, "num_experts": 8, "top_k": 2},
+        {"num_tokens": 1024, "hidden_dim": 4096, "intermediate_dim": 4096, "num_experts": 8, "top_k": 2},
+        {"num_tokens": 512, "hidden_dim": 4096, "intermediate_dim": 4096, "num_experts": 16, "top_k": 4},
+    ]
+    results = []
+    for cfg in moe_configs:
+        T, K, N = cfg["num_tokens"], cfg["hidden_dim"], cfg["intermediate_dim"]
+        E, k = cfg["num_experts"], cfg["top_k"]
+        print(f"\n{'=' * 80}\nMoE segment GEMM: tokens={T}, hidden={K}, intermediate={N}, experts={E}, top_k={k}")
+        print(f"  {'SM':>4} {'Vanilla(us)':>11} {'Aware(us)':>11} {'Speedup':>8}")
+        torch.manual_seed(42)
+        hs = torch.randn((T, K), device=dev, dtype=torch.bfloat16)
+        w = torch.randn((E * N, K), device=dev, dtype=torch.bfloat16)
+        offs = _fake_offsets(T, E, k, dev)
+        for sm_count in sm_levels:
+            try:
+                stream, actual = _partition(dev, sm_count, total_sms)
+                with torch.cuda.stream(stream):
+                    for _ in range(3):
+                        call_moe_vanilla(hs, w, offs, E, N, K)
+                        call_moe_sm_aware(hs, w, offs, E, N, K, actual)
+                    van = time_on_stream(lambda: call_moe_vanilla(hs, w, offs, E, N, K), stream, rep_ms=rep_ms)
+                    aw = time_on_stream(lambda: call_moe_sm_aware(hs, w, offs, E, N, K, actual), stream,
+                                        rep_ms=rep_ms)
+                sp = van["mean_ms"] / aw["mean_ms"] if aw["mean_ms"] > 0 else 0.0
+                print(f"  {sm_count:>4} {van['mean_ms'] * 1e3:>11.1f} {aw['mean_ms'] * 1e3:>11.1f} {sp:>7.2f}x")
+                results.append({"kind": "segment", **cfg, "sm": sm_count, "actual": actual,
+                                "vanilla_us": van["mean_ms"] * 1e3, "aware_us": aw["mean_ms"] * 1e3})
+            except Exception as e:
+                print(f"  {sm_count:>4}  Error: {e}")
+    if full_layer:
+        E, k, H, I = 8, 2, 4096, 14336
+        print(f"\n{'=' * 80}\nFused MoE layer (Mixtral: E={E}, top-{k}, H={H}, I={I}, bf16)")
+        print(f"  {'T':>5} {'SM':>4} {'us':>9} {'tokens/s':>12} {'TFLOP/s':>8}")
+        g = torch.Generator(device=dev).manual_seed(42)
+        w1 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w3 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn((E, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        for T in [1, 16, 128, 1024, 4096]:
+            x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+            logits = torch.randn((T, E), device=dev, generator=g)
+            for sm_count in (total_sms, total_sms // 2):
+                try:
+                    stream, actual = _partition(dev, sm_count, total_sms)
+                    with torch.cuda.stream(stream):
+                        for _ in range(2):
+                            _ops.fused_moe(x, logits, w1, w2, w3, k)
+                        r = time_on_stream(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k), stream, rep_ms=rep_ms)
+                    t = r["mean_ms"] * 1e-3
+                    tf = T * k * 6.0 * H * I / t / 1e12
+                    print(f"  {T:>5} {actual:>4} {r['mean_ms'] * 1e3:>9.1f} {T / t:>12.1f} {tf:>8.1f}")
+                    results.append({"kind": "layer", "T": T, "sm": sm_count, "actual": actual,
+                                    "us": r["mean_ms"] * 1e3, "tokens_per_s": T / t, "tflops": tf})
+                except Exception as e:
+                    print(f"  {T:>5} {sm_count:>4}  Error: {e}")
+    return results
+
+
+def main():
+    parser = argparse.ArgumentParser(description="SM-Aware Kernel Benchmark")
+    parser.add_argument("--gemm", action="store_true", help="Benchmark GEMM")
+    parser.add_argument("--moe", action="store_true", help="Benchmark Fused MoE")
+    parser.add_argument("--all", action="store_true", help="Benchmark all operators")
+    args = parser.parse_args()
+    if args.all:
+        run_gemm_benchmark()
+        run_moe_benchmark()
+    elif args.gemm:
+        run_gemm_benchmark()
+    elif args.moe:
+        run_moe_benchmark()
+    else:
+        parser.print_help()
+
+
+if __name__ == "__main__":
+    main()

@@ -121,6 +121,11 @@ typedef struct ek_gemm_plan {
 int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
                       ek_gemm_plan* out);
 
+/* Scratch bytes ek_gemm / ek_gemm_fp8 need for this call (plan.workspace_bytes);
+ * 0 when the schedule does not split. Returns (size_t)-1 on invalid input. */
+size_t ek_gemm_workspace_bytes(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn,
+                               int force_split);
+
 /* C[M,N] = A[M,K] @ B, fp32 accumulate, C in the input dtype (bf16 / fp16).
  * A row-major [M,K]; B per b_layout. K and N must be multiples of 8; all
  * pointers 16-byte aligned. workspace: ws_bytes of device memory holding
@@ -135,6 +140,18 @@ int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtyp
  * No counterpart kernel in the reference (it has no FP8 path). */
 int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float* w_scale, void* C, int M, int N,
                 int K, int num_sms, int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
+
+/* FP8 e4m3 quantisation with fp32 scales. x is [rows, cols] bf16 (x_dtype 0)
+ * or fp32 (x_dtype 3); q is [rows, cols] e4m3 codes. Scales are
+ * amax / 448 per block (1 for an all-zero block) and q = e4m3(x / scale),
+ * round-to-nearest-even, saturating:
+ *   block_rows = 1, block_cols <= 0 : one scale per row, scales[rows]
+ *   block_rows = 1, block_cols = 128: per 1 x 128 group, scales[rows][cols/128]
+ *   otherwise                       : per block_rows x block_cols block,
+ *                                     scales[ceil(rows/br)][ceil(cols/bc)].
+ * No counterpart in the reference (it has no FP8 path). */
+int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, void* q,
+                  float* scales, void* stream);
 
 /* GEMM for callers that cannot allocate device memory. No counterpart in the
  * reference. Same arguments and result as ek_gemm, minus the workspace: the

@@ -1,0 +1,52 @@
+"""FP8 e4m3 quantisation oracle (no reference code: the reference has no FP8
+path; this is the definition the GPU kernels are tested against).
+
+scale = amax(block) / 448 in fp32 (1.0 for an all-zero block);
+q = e4m3(x / scale) with IEEE fp32 division and round-to-nearest-even
+(torch's float8_e4m3fn cast); |x / scale| <= 448 by construction.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+E4M3_MAX = np.float32(448.0)
+
+
+def _f32(x) -> np.ndarray:
+    if isinstance(x, np.ndarray):
+        return x.astype(np.float32)
+    return x.detach().cpu().to(torch.float32).numpy()
+
+
+def _cast(v: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(torch.float8_e4m3fn)
+
+
+def quant_rows(x) -> tuple[torch.Tensor, np.ndarray]:
+    X = _f32(x)
+    amax = np.abs(X).max(axis=1)
+    s = np.where(amax > 0, amax / E4M3_MAX, np.float32(1.0)).astype(np.float32)
+    return _cast(X / s[:, None]), s
+
+
+def quant_blocks(x, br: int, bc: int) -> tuple[torch.Tensor, np.ndarray]:
+    X = _f32(x)
+    R, C = X.shape
+    nbr, nbc = -(-R // br), -(-C // bc)
+    s = np.ones((nbr, nbc), dtype=np.float32)
+    Q = np.empty_like(X)
+    for i in range(nbr):
+        for j in range(nbc):
+            blk = X[i * br:(i + 1) * br, j * bc:(j + 1) * bc]
+            a = np.abs(blk).max()
+            sc = np.float32(a / E4M3_MAX) if a > 0 else np.float32(1.0)
+            s[i, j] = sc
+            Q[i * br:(i + 1) * br, j * bc:(j + 1) * bc] = blk / sc
+    return _cast(Q), s
+
+
+def dequant_blocks(q: torch.Tensor, s: np.ndarray, br: int, bc: int) -> np.ndarray:
+    Q = q.to(torch.float32).numpy()
+    S = np.repeat(np.repeat(s, br, axis=0), bc, axis=1)[:Q.shape[0], :Q.shape[1]]
+    return Q * S
