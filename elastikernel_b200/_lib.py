@@ -79,7 +79,7 @@ _SIGNATURES = {
     "ek_moe_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int,
                                 _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
-                                _c_int, _c_vp]),
+                                _c_int, _c_int, _c_vp]),
     "ek_moe_down": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
                              _c_int, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),

@@ -269,7 +269,8 @@ def moe_gate_up(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: int | N
     with _on_device(dev):
         check(lib().ek_moe_gate_up(x_perm.data_ptr(), w1.data_ptr(), w3.data_ptr(), perm["block_expert"].data_ptr(),
                                    perm["num_rows_padded"].data_ptr(), act.data_ptr(), max_rows, E, H, I,
-                                   int(num_sms or 0), int(force_bn), stream), "ek_moe_gate_up")
+                                   perm["T"] * perm["topk"], int(num_sms or 0), int(force_bn), stream),
+              "ek_moe_gate_up")
     return act
 
 

@@ -125,17 +125,15 @@ __global__ void __launch_bounds__(kPermChunk) permute_count_kernel(const int* __
 }
 
 __global__ void __launch_bounds__(kPermChunk)
-    permute_scatter_kernel(const int* __restrict__ ids, int n_slots, int E, int topk, int block_m,
+    permute_scatter_kernel(const int* __restrict__ ids, int n_slots, int E, int block_m,
                            const int* __restrict__ chunk_counts, int n_chunks, int* __restrict__ sorted_slots,
                            int* __restrict__ block_expert, int* __restrict__ num_rows_padded,
-                           int* __restrict__ expert_counts, int max_rows, const uint8_t* __restrict__ x,
-                           int row_bytes, uint8_t* __restrict__ x_perm) {
+                           int* __restrict__ expert_counts, int max_rows) {
   extern __shared__ int sm[];
   int* s_tot = sm;              // [E] slots per expert (all chunks)
   int* s_before = sm + E;       // [E] slots per expert in earlier chunks
   int* s_start = sm + 2 * E;    // [E] first padded row of each expert
   int* s_wcnt = sm + 3 * E;     // [32][E] per-warp counts of this chunk
-  int* s_dest = s_wcnt + 32 * E;  // [kPermChunk] destination row per thread
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -204,17 +202,25 @@ __global__ void __launch_bounds__(kPermChunk)
     dest = s_start[e] + s_before[e] + pre + rank_w;
     sorted_slots[dest] = s;
   }
-  s_dest[tid] = dest;
-  if (x == nullptr) return;
-  __syncthreads();
-  // gather the token rows of this chunk into their padded rows
+}
+
+// Row gather into the padded layout: x_perm[r] = x[sorted_slots[r] / k] for the
+// used rows; padding rows are left as they are (each GEMM output row depends
+// only on its own input row, and padding rows are never stored). One warp per
+// row, 16-byte vectors, grid-stride over the rows.
+__global__ void __launch_bounds__(256)
+    gather_rows_kernel(const int* __restrict__ sorted_slots, const int* __restrict__ num_rows_padded, int max_rows,
+                       int n_slots, int topk, const uint8_t* __restrict__ x, int row_bytes,
+                       uint8_t* __restrict__ x_perm) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const int rows = min(*num_rows_padded, max_rows);
   const int nvec = row_bytes / 16;
-  for (int i = warp; i < kPermChunk; i += blockDim.x / 32) {
-    const int d = s_dest[i];
-    if (d < 0) continue;
-    const int tok = (blockIdx.x * kPermChunk + i) / topk;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * row_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)d * row_bytes);
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int s = sorted_slots[r];
+    if (s < 0 || s >= n_slots) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(s / topk) * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)r * row_bytes);
     for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
   }
 }
@@ -269,22 +275,36 @@ int launch_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   return check_cuda(cudaGetLastError(), "grouped gemm launch");
 }
 
-// Tile width for a grouped GEMM: balance the units of the expected number of
-// row blocks over the partition, weighing each unit by its operand bytes.
-int grouped_bn(int est_mblocks, int out_cols, int K, int S, bool swiglu) {
+// Expected 128-row blocks of the padded layout for n_slots (token, choice)
+// slots over E experts: every used expert adds at most one partial block.
+int est_mblocks(long long n_slots, int E, int max_mblocks) {
+  const long long est = n_slots <= E ? n_slots : (n_slots + 127) / 128 + std::min<long long>(E, n_slots);
+  return (int)std::max<long long>(1, std::min<long long>(est, max_mblocks));
+}
+
+// Tile width for a grouped GEMM. Each unit streams a B tile of expert weights
+// (from HBM, shared by the row blocks of one expert that run together) and
+// an A tile of gathered rows (L2-resident); the busiest CTA sets the time.
+int grouped_bn(int mblocks, int E, int out_cols, int K, int S, bool swiglu) {
+  constexpr double kClkGhz = 1.8, kMmaFlopClk = 8192.0;
+  constexpr double kL2PerSmGBs = 180.0;  // operand feed one SM sustains from L2
+  constexpr double kL2GBs = 9000.0;      // L2 -> SM bandwidth shared by all active SMs
+  constexpr double kHbmGBs = 6500.0;     // device HBM bandwidth
+  constexpr double kHbmPerSmGBs = 80.0;  // HBM bandwidth one SM's TMA pipeline reaches
   static const int kBNs[4] = {256, 192, 128, 64};
   int best = 256;
   double best_cost = 1e300;
+  const double share = std::max(1.0, std::min(8.0, double(mblocks) / std::max(1, std::min(E, mblocks))));
   for (int bn : kBNs) {
     const int cols = swiglu ? bn / 2 : bn;
     const long long tiles_n = (out_cols + cols - 1) / cols;
-    const long long units = (long long)est_mblocks * tiles_n;
-    const long long per_cta = (units + S - 1) / S;
-    // clocks per unit: operand feed (bf16 A + B tiles at ~100 B/clk/SM) vs
-    // tensor work (8192 FLOP/clk/SM); the busiest CTA sets the time
-    const double feed_clk = (128.0 + bn) * K * 2.0 / 100.0;
-    const double mma_clk = 128.0 * bn * K * 2.0 / 8192.0;
-    const double cost = per_cta * std::max(feed_clk, mma_clk);
+    const long long units = (long long)mblocks * tiles_n;
+    const long long active = std::min<long long>(S, units);
+    const long long waves = (units + S - 1) / S;
+    const double mma_us = 128.0 * bn * K * 2.0 / kMmaFlopClk / (kClkGhz * 1e3);
+    const double l2_us = (128.0 + bn) * K * 2.0 / (std::min(kL2PerSmGBs, kL2GBs / active) * 1e3);
+    const double hbm_us = bn * K * 2.0 / share / (std::min(kHbmPerSmGBs, kHbmGBs / active) * 1e3);
+    const double cost = waves * std::max(mma_us, std::max(l2_us, hbm_us));
     if (cost < best_cost * 0.98) {
       best_cost = cost;
       best = bn;
@@ -348,25 +368,31 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
   permute_count_kernel<<<n_chunks, kPermChunk, E * sizeof(int), s>>>(topk_ids, (int)n_slots, E, chunk_counts);
   int rc = check_cuda(cudaGetLastError(), "permute count launch");
   if (rc) return rc;
-  const size_t smem = (size_t)(3 * E + 32 * E + kPermChunk) * sizeof(int);
+  const size_t smem = (size_t)(3 * E + 32 * E) * sizeof(int);
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     rc = check_cuda(cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)((3 * kPermMaxE + 32 * kPermMaxE + kPermChunk) * sizeof(int))),
+                                         (int)((3 * kPermMaxE + 32 * kPermMaxE) * sizeof(int))),
                     "cudaFuncSetAttribute(permute)");
     if (rc) return rc;
     attr_done[dev] = true;
   }
   permute_scatter_kernel<<<n_chunks, kPermChunk, smem, s>>>(
-      topk_ids, (int)n_slots, E, topk, block_m, chunk_counts, n_chunks, sorted_slots, block_expert, num_rows_padded,
-      expert_counts, (int)max_rows, static_cast<const uint8_t*>(x), row_bytes, static_cast<uint8_t*>(x_perm));
-  return check_cuda(cudaGetLastError(), "permute scatter launch");
+      topk_ids, (int)n_slots, E, block_m, chunk_counts, n_chunks, sorted_slots, block_expert, num_rows_padded,
+      expert_counts, (int)max_rows);
+  rc = check_cuda(cudaGetLastError(), "permute scatter launch");
+  if (rc || x == nullptr) return rc;
+  const int gather_blocks = (int)std::min<long long>((max_rows + 7) / 8, 148LL * 8);
+  gather_rows_kernel<<<std::max(gather_blocks, 1), 256, 0, s>>>(sorted_slots, num_rows_padded, (int)max_rows,
+                                                               (int)n_slots, topk, static_cast<const uint8_t*>(x),
+                                                               row_bytes, static_cast<uint8_t*>(x_perm));
+  return check_cuda(cudaGetLastError(), "row gather launch");
 }
 
 int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
-                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_sms,
+                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_slots, int num_sms,
                    int force_bn, void* stream) {
   clear_error();
   if (!x_perm || !w1 || !w3 || !block_expert || !num_rows_padded || !act)
@@ -379,7 +405,7 @@ int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   const int mblocks = max_rows / 128;
-  const int bn = force_bn > 0 ? force_bn : grouped_bn(mblocks, I, H, S, true);
+  const int bn = force_bn > 0 ? force_bn : grouped_bn(est_mblocks(num_slots, E, mblocks), E, I, H, S, true);
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
   CUtensorMap ta, tb, tb2;
   if ((rc = make_tmap_2d(&ta, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, max_rows, (uint64_t)H * 2, 64, 128))) return rc;
@@ -425,7 +451,8 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   const int mblocks = max_rows / 128;
-  const int bn = force_bn > 0 ? force_bn : grouped_bn(mblocks, H, I, S, false);
+  const int bn = force_bn > 0 ? force_bn
+                              : grouped_bn(est_mblocks((long long)T * topk, E, mblocks), E, H, I, S, false);
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
   CUtensorMap ta, tb;
   if ((rc = make_tmap_2d(&ta, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, max_rows, (uint64_t)I * 2, 64, 128))) return rc;

@@ -177,13 +177,38 @@ def run_moe_benchmark(sm_levels=None, moe_configs=None, rep_ms: float = 30.0, fu
     return results
 
 
+def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None) -> None:
+    """Run the Mixtral-shaped fused-MoE layer at `tokens` tokens a few times
+    (no timing; a fixed launch sequence for profilers)."""
+    import torch
+
+    from . import _ops
+
+    dev = torch.device("cuda:0")
+    E, k, H, I = 8, 2, 4096, 14336
+    g = torch.Generator(device=dev).manual_seed(42)
+    w1 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn((E, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn((tokens, H), device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn((tokens, E), device=dev, generator=g)
+    for _ in range(reps):
+        _ops.fused_moe(x, logits, w1, w2, w3, k, num_sms=num_sms)
+    torch.cuda.synchronize()
+
+
 def main():
     parser = argparse.ArgumentParser(description="SM-Aware Kernel Benchmark")
     parser.add_argument("--gemm", action="store_true", help="Benchmark GEMM")
     parser.add_argument("--moe", action="store_true", help="Benchmark Fused MoE")
     parser.add_argument("--all", action="store_true", help="Benchmark all operators")
+    parser.add_argument("--layer-tokens", type=int, default=0,
+                        help="only run the Mixtral fused-MoE layer at this token count (for profiling)")
+    parser.add_argument("--reps", type=int, default=5)
     args = parser.parse_args()
-    if args.all:
+    if args.layer_tokens > 0:
+        run_layer(args.layer_tokens, args.reps)
+    elif args.all:
         run_gemm_benchmark()
         run_moe_benchmark()
     elif args.gemm:

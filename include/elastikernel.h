@@ -204,10 +204,11 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
 /* Grouped gate/up GEMM with fused SiLU-and-multiply over the padded rows:
  *   act[r, n] = silu(x_perm[r] . w1[e, n]) * (x_perm[r] . w3[e, n]),
  * e = block_expert[r / 128], for r < *num_rows_padded; w1, w3 are [E, I, H]
- * bf16; act is [max_rows, I] bf16. */
+ * bf16; act is [max_rows, I] bf16. num_slots (T * topk) only guides the
+ * choice of tile width. */
 int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
-                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_sms,
-                   int force_bn, void* stream);
+                   const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_slots,
+                   int num_sms, int force_bn, void* stream);
 
 /* Grouped down projection with the top-k weight fused into the epilogue:
  *   y[s] = topk_weight[s] * (act[r] @ w2[e]^T),  s = sorted_slots[r] < T*k,
