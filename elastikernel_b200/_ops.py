@@ -296,6 +296,48 @@ def moe_down(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torc
     return y
 
 
+def moe_gate_up_packed(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: int | None = None,
+                       tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+    """Swapped-operand gate/up over the packed layout (permute with block_m=1)."""
+    x_perm = perm["x_perm"]
+    dev = _require_cuda(x_perm, w1, w3)
+    for n, t in (("x_perm", x_perm), ("w1", w1), ("w3", w3)):
+        _check_bf16(n, t)
+    if perm["block_m"] != 1:
+        raise RuntimeError("the packed GEMMs take the packed layout (moe_permute(..., block_m=1))")
+    E, I, H = w1.shape
+    if w3.shape != w1.shape or x_perm.shape[1] != H or E != perm["E"]:
+        raise RuntimeError("gate_up_packed: shape mismatch")
+    rows = perm["max_rows"]
+    act = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_gate_up_packed(x_perm.data_ptr(), w1.data_ptr(), w3.data_ptr(),
+                                          perm["expert_counts"].data_ptr(), act.data_ptr(), rows, E, H, I,
+                                          int(tok_tile), int(pair), int(num_sms or 0), current_stream_handle(dev)),
+              "ek_moe_gate_up_packed")
+    return act
+
+
+def moe_down_packed(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
+                    num_sms: int | None = None, tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+    """Swapped-operand down projection with the routing weight, scattered to slots."""
+    dev = _require_cuda(act, w2, topk_weights)
+    _check_bf16("act", act)
+    _check_bf16("w2", w2)
+    _contig("topk_weights", topk_weights)
+    E, H, I = w2.shape
+    T, k = perm["T"], perm["topk"]
+    if act.shape[1] != I or E != perm["E"] or topk_weights.numel() != T * k or perm["block_m"] != 1:
+        raise RuntimeError("down_packed: shape mismatch")
+    y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_down_packed(act.data_ptr(), w2.data_ptr(), perm["expert_counts"].data_ptr(),
+                                       perm["sorted_slots"].data_ptr(), topk_weights.data_ptr(), y.data_ptr(),
+                                       perm["max_rows"], E, H, I, T, k, int(tok_tile), int(pair),
+                                       int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_packed")
+    return y
+
+
 def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_j y[t*k + j] (fp32 sum in j order), bf16."""
     dev = _require_cuda(y, out)
@@ -312,17 +354,27 @@ def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = N
 
 
 def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-              w3: torch.Tensor, topk: int, out: torch.Tensor | None = None, num_sms: int | None = None) -> torch.Tensor:
-    """The whole MoE layer: route -> permute(+gather) -> gate/up SwiGLU -> down(+weight) -> combine."""
+              w3: torch.Tensor, topk: int, out: torch.Tensor | None = None, num_sms: int | None = None,
+              layout: str = "packed") -> torch.Tensor:
+    """The whole MoE layer: route -> permute(+gather) -> gate/up SwiGLU -> down(+weight) -> combine.
+
+    layout="packed" (default): expert-major rows without padding and the
+    swapped-operand GEMMs; layout="padded": 128-row padded blocks and the
+    token-major GEMMs."""
     _require_cuda(hidden_states, gate_logits, w1, w2, w3, out)
     _check_bf16("hidden_states", hidden_states)
     T = hidden_states.shape[0]
     if T == 0:
         return out if out is not None else torch.empty_like(hidden_states)
     ids, wts = moe_route(gate_logits, topk)
-    perm = moe_permute(ids, w1.shape[0], x=hidden_states)
-    act = moe_gate_up(perm, w1, w3, num_sms=num_sms)
-    y = moe_down(perm, act, w2, wts, num_sms=num_sms)
+    if layout == "packed" and w1.shape[0] <= 256:
+        perm = moe_permute(ids, w1.shape[0], x=hidden_states, block_m=1)
+        act = moe_gate_up_packed(perm, w1, w3, num_sms=num_sms)
+        y = moe_down_packed(perm, act, w2, wts, num_sms=num_sms)
+    else:
+        perm = moe_permute(ids, w1.shape[0], x=hidden_states)
+        act = moe_gate_up(perm, w1, w3, num_sms=num_sms)
+        y = moe_down(perm, act, w2, wts, num_sms=num_sms)
     return moe_combine(y, T, topk, out=out)
 
 

@@ -22,21 +22,37 @@
 // thread-major layout (coalesced) and the last slice to finish (atomic
 // ticket) sums them in slice order, so results do not depend on arrival order.
 //
-// Three schedules share the main loop:
+// Schedules sharing the main loop:
 //   kSchedDense    dense GEMM, grouped rasterisation, optional tail split
-//   kSchedBlocks   MoE grouped GEMM over the padded expert-sorted rows: row
-//                  block b uses expert block_expert[b]; rows past
-//                  *num_rows_padded are skipped
+//   kSchedBlocks   MoE grouped GEMM over the block-padded expert-sorted rows:
+//                  A = token rows, B = expert weights; row block b uses expert
+//                  block_expert[b]; rows past *num_rows_padded are skipped
 //   kSchedSegments the reference's CSR segment GEMM: expert e owns rows
 //                  [offsets[e], offsets[e+1])
+//   kSchedExperts  MoE grouped GEMM with the operands swapped: A = expert
+//                  weight rows (the 128/256-row MMA side), B = that expert's
+//                  token rows (N = 16..256), over the packed expert-sorted
+//                  rows (no padding). A unit is (expert, feature tile, token
+//                  tile); weight tiles stream from HBM once per token tile, so
+//                  small token counts stay HBM-efficient, and large ones can
+//                  use the CTA pair.
 #pragma once
 #include "ek_ptx.cuh"
 
 namespace ek {
 
 enum Elem : int { kBF16 = 0, kFP16 = 1, kE4M3 = 2 };
-enum Epi : int { kEpiStore = 0, kEpiRowColScale = 1, kEpiSwiGLU = 2, kEpiWeightedScatter = 3 };
-enum Sched : int { kSchedDense = 0, kSchedBlocks = 1, kSchedSegments = 2 };
+enum Epi : int {
+  kEpiStore = 0,
+  kEpiRowColScale = 1,
+  kEpiSwiGLU = 2,
+  kEpiWeightedScatter = 3,
+  kEpiSwiGLUT = 4,    // swapped: TMEM rows = [64 w1 rows | 64 w3 rows], columns = tokens
+  kEpiScatterT = 5,   // swapped: TMEM rows = output features, columns = tokens
+};
+enum Sched : int { kSchedDense = 0, kSchedBlocks = 1, kSchedSegments = 2, kSchedExperts = 3 };
+
+constexpr int kMaxExpertsT = 256;  // experts per launch of the swapped schedule
 
 template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false>
 struct GemmCfg {
@@ -50,6 +66,7 @@ struct GemmCfg {
   static constexpr bool kBMN = kBMN_;  // B stored MN-major ([K, N] row-major)
   static constexpr int kEpi = kEpi_;
   static constexpr int kSched = kSched_;
+  static constexpr bool kSwapped = (kSched == kSchedExperts);
   static constexpr bool kF8 = (kElem == kE4M3);
   static constexpr int ES = kF8 ? 1 : 2;   // bytes per element
   static constexpr int BK = 128 / ES;      // one 128-byte swizzle row of K
@@ -58,20 +75,30 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES * CTAS;  // bytes that complete one stage of the pair
-  static constexpr int SMEM_BUDGET = 220 * 1024;
+  // extra shared memory of the swapped schedule: expert prefixes, per-token
+  // slots / weights, and the gate exchange of the SwiGLU epilogue
+  static constexpr int EXTRA_BYTES =
+      kSwapped ? (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + 64 * 33 * 4 + 127) / 128 * 128 : 0;
+  static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                  : (2 * BN <= 256) ? 256 : 512;
   static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EXTRA_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int THREADS = 192;
   static constexpr int EPI_WARPS = 4;
-  static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static constexpr int CHUNK = BN < 32 ? BN : 32;  // TMEM columns per epilogue load
+  static_assert(kSwapped ? (BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256)
+                         : (BN % 64 == 0 && BN <= 256),
+                "tile width");
+  static_assert(BN_CTA % 8 == 0, "B tiles are whole 8-row swizzle atoms");
   static_assert(!kBMN || BN_CTA % 64 == 0, "MN-major B is loaded in 64-column chunks");
   static_assert(!(kF8 && kBMN), "e4m3 B must be K-major");
-  static_assert(!kPair || (kSched == kSchedDense && (kEpi == kEpiStore || kEpi == kEpiRowColScale)),
-                "the CTA-pair mode serves the dense schedule");
+  static_assert(!kPair || (kSched == kSchedDense && (kEpi == kEpiStore || kEpi == kEpiRowColScale)) ||
+                    (kSwapped && (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT)),
+                "the CTA-pair mode serves the dense and swapped schedules");
+  static_assert(!kSwapped || (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT), "swapped schedule epilogues");
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
 };
 
@@ -97,6 +124,11 @@ struct GemmParams {
   // segments (kSchedSegments)
   const int* seg_offsets;
   int seg_mblocks;        // row blocks per expert (upper bound)
+  // swapped experts (kSchedExperts): rows of expert e are packed at
+  // [start_e, start_e + expert_counts[e]) of the token operand
+  const int* expert_counts;
+  int w_rows_per_expert;  // rows of the flattened weight per expert (I for w1/w3, H for w2)
+  int feat_tiles;         // weight-row tiles per expert
   // split-K workspace
   float* ws_partial;
   int* ws_counters;
@@ -108,11 +140,19 @@ struct Unit {
   int split, nsplit;
   int tail_slot;    // index into the split workspace (dense tail tiles)
   int a_row;        // first A row of this CTA's part of the tile
-  int row_end;      // rows >= row_end are not stored
+  int row_end;      // rows >= row_end are not stored (swapped: token rows)
   int b_row;        // first B row (K-major) / first K row offset (MN-major)
   int b_col;        // first B column (MN-major) of this CTA's part
-  int c_col;        // first output column of the tile
+  int c_col;        // first output column of the tile (swapped: first feature of this CTA)
+  int tok0;         // swapped: token row of TMEM column 0
+  int n_eff;        // MMA N of this unit (swapped: tokens actually present, rounded up)
   bool valid;
+};
+
+// Shared state of the swapped schedule, filled once per CTA.
+struct ExpertTables {
+  int* start;   // [E + 1] first packed row of each expert
+  int* tprefix; // [E + 1] prefix of units per expert
 };
 
 __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
@@ -126,7 +166,8 @@ __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int g
 }
 
 template <class Cfg>
-__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows_runtime, int rank) {
+__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows_runtime, int rank,
+                                            const ExpertTables& xt) {
   Unit w;
   w.valid = true;
   w.split = 0;
@@ -134,6 +175,8 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
   w.tail_slot = -1;
   w.kb0 = 0;
   w.kb1 = p.k_blocks;
+  w.tok0 = 0;
+  w.n_eff = Cfg::BN;
   if constexpr (Cfg::kSched == kSchedDense) {
     int tile = u;
     if (u >= p.num_dp_tiles) {
@@ -167,7 +210,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     w.b_row = e * p.b_rows_per_expert + w.tn * bn_rows;
     w.b_col = 0;
     w.c_col = w.tn * bn_rows;
-  } else {  // kSchedSegments
+  } else if constexpr (Cfg::kSched == kSchedSegments) {
     const int per_e = p.seg_mblocks * p.tiles_n;
     const int e = u / per_e;
     const int r = u - e * per_e;
@@ -182,22 +225,39 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     w.b_row = e * p.N;  // K-row offset of the expert block in the [E*N, K] weight
     w.b_col = w.tn * Cfg::BN;
     w.c_col = w.tn * Cfg::BN;
+  } else {  // kSchedExperts
+    int lo = 0, hi = p.num_experts - 1;  // last expert whose unit prefix is <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (xt.tprefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo;
+    const int r = u - xt.tprefix[e];
+    const int cnt = xt.start[e + 1] - xt.start[e];
+    const int ttiles = (cnt + Cfg::BN - 1) / Cfg::BN;
+    const int j = r % ttiles;  // token tile (fastest: tiles sharing a weight tile run together)
+    const int f = r / ttiles;  // feature tile
+    // the expert's tokens are split evenly over its tiles and the MMA N is
+    // shrunk to the tokens present (a multiple of 16 per CTA of the pair)
+    const int per = (cnt + ttiles - 1) / ttiles;
+    constexpr int kStep = 16 * Cfg::CTAS;
+    w.n_eff = min(Cfg::BN, (per + kStep - 1) / kStep * kStep);
+    w.tm = f;
+    w.tn = j;
+    w.tok0 = xt.start[e] + j * per;
+    w.row_end = xt.start[e] + min((j + 1) * per, cnt);
+    w.b_row = w.tok0 + rank * (w.n_eff / Cfg::CTAS);
+    w.b_col = 0;
+    if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
+      // 64 features per CTA: rows [64 of w1 | 64 of w3]
+      w.c_col = f * 64 * Cfg::CTAS + rank * 64;
+      w.a_row = e * p.w_rows_per_expert + w.c_col;
+    } else {
+      w.c_col = f * Cfg::TILE_M + rank * Cfg::BM;
+      w.a_row = e * p.w_rows_per_expert + w.c_col;
+    }
   }
   return w;
-}
-
-// Runtime unit count (grouped GEMMs read the padded row count from device).
-template <class Cfg>
-__device__ __forceinline__ int unit_count(const GemmParams& p, int& rows_runtime) {
-  if constexpr (Cfg::kSched == kSchedBlocks) {
-    int r = *p.num_rows_ptr;
-    r = max(0, min(r, p.M));
-    rows_runtime = r;
-    return (r / Cfg::BM) * p.tiles_n;
-  } else {
-    rows_runtime = p.M;
-    return p.num_units;
-  }
 }
 
 template <class Cfg>
@@ -256,17 +316,27 @@ __device__ __forceinline__ void finish_chunk(const GemmParams& p, int row, int c
   store_out_chunk<Cfg>(p, row, col0, v);
 }
 
+// CHUNK TMEM columns of this thread's row (32 or 16).
+template <class Cfg>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[32]) {
+  if constexpr (Cfg::CHUNK == 32)
+    tmem_ld32(taddr, r);
+  else
+    tmem_ld16(taddr, r);
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmX, const GemmParams p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, UK = Cfg::UK, STAGES = Cfg::STAGES;
   constexpr int G = Cfg::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* sX = sB + STAGES * Cfg::B_BYTES;  // swapped-schedule tables
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + Cfg::EXTRA_BYTES);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* tfull_bar = bars + 2 * STAGES;
@@ -275,6 +345,10 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem_base + 1);
   volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem_base + 2);
+  ExpertTables xt{reinterpret_cast<int*>(sX), reinterpret_cast<int*>(sX) + (kMaxExpertsT + 1)};
+  int* s_slot = reinterpret_cast<int*>(sX) + 2 * (kMaxExpertsT + 1);  // [BN]
+  float* s_wt = reinterpret_cast<float*>(s_slot + BN);                 // [BN]
+  float* s_xg = s_wt + BN;                                             // [64][33]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -296,6 +370,19 @@ __global__ void __launch_bounds__(192, 1)
     *s_abort = 0;
     *s_last = 0;
     fence_mbar_init();
+    if constexpr (Cfg::kSwapped) {
+      // packed starts and unit prefix per expert (units = feature tiles x token tiles)
+      int acc = 0, units = 0;
+      for (int e = 0; e < p.num_experts; ++e) {
+        const int c = max(0, p.expert_counts[e]);
+        xt.start[e] = acc;
+        xt.tprefix[e] = units;
+        acc += c;
+        units += p.feat_tiles * ((c + BN - 1) / BN);
+      }
+      xt.start[p.num_experts] = acc;
+      xt.tprefix[p.num_experts] = units;
+    }
   }
   if (warp == 1) {
     tmem_alloc<G>(s_tmem_base, Cfg::TMEM_COLS);
@@ -307,20 +394,27 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem_base;
 
-  int rows_rt = 0;
-  const int nunits = unit_count<Cfg>(p, rows_rt);
+  int rows_rt = p.M;
+  int nunits = p.num_units;
+  if constexpr (Cfg::kSched == kSchedBlocks) {
+    int r = *p.num_rows_ptr;
+    rows_rt = max(0, min(r, p.M));
+    nunits = (rows_rt / Cfg::BM) * p.tiles_n;
+  } else if constexpr (Cfg::kSwapped) {
+    nunits = xt.tprefix[p.num_experts];
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      if constexpr (Cfg::kEpi == kEpiSwiGLU) tma_prefetch_desc(&tmB2);
+      if constexpr (Cfg::kEpi == kEpiSwiGLU || Cfg::kEpi == kEpiSwiGLUT) tma_prefetch_desc(&tmX);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int u = unit0; u < nunits && ok; u += unit_step) {
-        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
         if (!w.valid) continue;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) { ok = false; break; }
@@ -330,7 +424,12 @@ __global__ void __launch_bounds__(192, 1)
             // both CTAs' loads complete on the leader's full barrier
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
             const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-            tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
+            if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
+              tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
+              tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * BK, w.a_row);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
+            }
             if constexpr (Cfg::kBMN) {
 #pragma unroll
               for (int j = 0; j < Cfg::BN_CTA / 64; ++j)
@@ -340,14 +439,19 @@ __global__ void __launch_bounds__(192, 1)
             }
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+            if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+              tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * BK, w.a_row);
+            } else {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+            }
             if constexpr (Cfg::kBMN) {
 #pragma unroll
               for (int j = 0; j < BN / 64; ++j)
                 tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
             } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
               tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
-              tma_load_2d(b_dst + (BN / 2) * 128, &tmB2, &full_bar[stage], kb * BK, w.b_row);
+              tma_load_2d(b_dst + (BN / 2) * 128, &tmX, &full_bar[stage], kb * BK, w.b_row);
             } else {
               tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
             }
@@ -365,13 +469,16 @@ __global__ void __launch_bounds__(192, 1)
       int acc_i = 0;
       bool ok = true;
       for (int u = unit0; u < nunits && ok; u += unit_step) {
-        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
+        const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
         if (!w.valid) continue;
         const int buf = acc_i & 1;
         const uint32_t aphase = (acc_i >> 1) & 1;
         if (!mbar_wait(&tempty_bar[buf], aphase ^ 1, s_abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
+        // the swapped schedule sets the MMA N per unit (instruction descriptor bits 17..22)
+        const uint32_t idesc = Cfg::kSwapped ? ((Cfg::IDESC & ~(0x3Fu << 17)) | ((uint32_t)(w.n_eff >> 3) << 17))
+                                             : Cfg::IDESC;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, s_abort)) { ok = false; break; }
           tc_fence_after();
@@ -387,9 +494,9 @@ __global__ void __launch_bounds__(192, 1)
               bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
             const uint32_t acc = (kb > w.kb0 || k > 0) ? 1u : 0u;
             if constexpr (Cfg::kPair)
-              umma_pair<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, acc);
+              umma_pair<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
             else
-              umma<Cfg::kF8>(d_tmem, ad, bd, Cfg::IDESC, acc);
+              umma<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
           }
           if constexpr (Cfg::kPair)
             umma_commit_pair(&empty_bar[stage], 0x3);
@@ -435,10 +542,27 @@ __global__ void __launch_bounds__(192, 1)
     };
     int acc_i = 0;
     for (int u = unit0; u < nunits; u += unit_step) {
-      const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank);
+      const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
       if (!w.valid) continue;
       const int buf = acc_i & 1;
       const uint32_t aphase = (acc_i >> 1) & 1;
+      if constexpr (Cfg::kEpi == kEpiScatterT) {
+        // slot and routing weight of every token column of this unit
+        for (int t = epi_tid; t < BN; t += 128) {
+          const int tr = w.tok0 + t;
+          int slot = -1;
+          float wt = 0.f;
+          if (tr < w.row_end) {
+            slot = p.sorted_slots[tr];
+            if (slot >= 0 && slot < p.num_slots)
+              wt = p.slot_weights[slot];
+            else
+              slot = -1;
+          }
+          s_slot[t] = slot;
+          s_wt[t] = wt;
+        }
+      }
       const bool got = mbar_wait(&tfull_bar[buf], aphase, s_abort);
       if (named_bar_red_or(1, 128, got ? 0 : 1)) break;  // uniform across the 128 threads
       tc_fence_after();
@@ -446,7 +570,62 @@ __global__ void __launch_bounds__(192, 1)
       const int row = w.a_row + row_in_tile;
       const bool row_ok = row < w.row_end;
 
-      if constexpr (Cfg::kEpi == kEpiSwiGLU) {
+      if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
+        // TMEM rows 0..63: x.w1 for 64 features, rows 64..127: x.w3 for the
+        // same features; columns: tokens. Gate rows hand their values over
+        // through shared memory, up rows combine and store.
+        constexpr int CH = Cfg::CHUNK;
+        const bool is_gate = row_in_tile < 64;
+        const int feat = row_in_tile & 63;
+        const int col = w.c_col + feat;
+        const int nch = (w.n_eff + CH - 1) / CH;
+        __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          uint32_t r[32];
+          tmem_ld_chunk<Cfg>(t_row + c * CH, r);
+          tmem_ld_wait(r);
+          if (c == nch - 1) release_tmem(buf);
+          if (is_gate) {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) s_xg[feat * 33 + t] = __uint_as_float(r[t]);
+          }
+          named_bar_sync(1, 128);
+          if (!is_gate && col < p.N) {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) {
+              const int tr = w.tok0 + c * CH + t;
+              if (tr < w.row_end) {
+                const float g = s_xg[feat * 33 + t];
+                outp[(size_t)tr * p.ldc + col] = __float2bfloat16_rn(silu_f(g) * __uint_as_float(r[t]));
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+        }
+      } else if constexpr (Cfg::kEpi == kEpiScatterT) {
+        // TMEM rows: output features; columns: tokens scattered to their slot
+        constexpr int CH = Cfg::CHUNK;
+        const int col = w.c_col + row_in_tile;
+        const int nch = (w.n_eff + CH - 1) / CH;
+        __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          uint32_t r[32];
+          tmem_ld_chunk<Cfg>(t_row + c * CH, r);
+          tmem_ld_wait(r);
+          if (c == nch - 1) release_tmem(buf);
+          if (col < p.N) {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) {
+              const int slot = s_slot[c * CH + t];
+              if (slot >= 0)
+                outp[(size_t)slot * p.ldc + col] = __float2bfloat16_rn(__uint_as_float(r[t]) * s_wt[c * CH + t]);
+            }
+          }
+        }
+        named_bar_sync(1, 128);  // s_slot / s_wt are rewritten for the next unit
+      } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
         // columns [0, BN/2) hold x.w1 (gate input), [BN/2, BN) hold x.w3
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {

@@ -271,8 +271,51 @@ int launch_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     attr_done[dev] = true;
   }
   if (grid <= 0) return EK_OK;
-  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb2, prm);
-  return check_cuda(cudaGetLastError(), "grouped gemm launch");
+  if constexpr (Cfg::kPair) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<Cfg>, ta, tb, tb2, prm), "grouped pair launch");
+  } else {
+    gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tb2, prm);
+    return check_cuda(cudaGetLastError(), "grouped gemm launch");
+  }
+}
+
+// Token tile (N of the swapped MMA) and CTA-pair choice for the packed
+// expert-major GEMMs: the tile covers the average tokens of a used expert.
+void packed_tiles(long long n_slots, int E, int S, int force_tok, int force_pair, int* tok, int* pair) {
+  int t = force_tok;
+  if (t <= 0) {
+    const long long used = std::max<long long>(1, std::min<long long>(E, n_slots));
+    const long long avg = (n_slots + used - 1) / used;
+    t = 16;
+    while (t < avg && t < 256) t *= 2;
+  }
+  *tok = t;
+  *pair = force_pair >= 0 ? force_pair : (t >= 128 && S >= 2 ? 1 : 0);
+}
+
+template <int kEpi, bool kPair>
+int launch_packed_tok(int tok, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx,
+                      const GemmParams& p, int grid, cudaStream_t s) {
+  switch (tok) {
+    case 16: return launch_grouped<GemmCfg<16, kBF16, false, kEpi, kSchedExperts, kPair>>(ta, tb, tx, p, grid, s);
+    case 32: return launch_grouped<GemmCfg<32, kBF16, false, kEpi, kSchedExperts, kPair>>(ta, tb, tx, p, grid, s);
+    case 64: return launch_grouped<GemmCfg<64, kBF16, false, kEpi, kSchedExperts, kPair>>(ta, tb, tx, p, grid, s);
+    case 128: return launch_grouped<GemmCfg<128, kBF16, false, kEpi, kSchedExperts, kPair>>(ta, tb, tx, p, grid, s);
+    case 256: return launch_grouped<GemmCfg<256, kBF16, false, kEpi, kSchedExperts, kPair>>(ta, tb, tx, p, grid, s);
+  }
+  return set_error(EK_ERR_INVALID, "token tile must be 16, 32, 64, 128 or 256 (got %d)", tok);
 }
 
 // Expected 128-row blocks of the padded layout for n_slots (token, choice)
@@ -483,6 +526,87 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
     case 192: return launch_grouped<GemmCfg<192, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
     default: return launch_grouped<GemmCfg<256, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
   }
+}
+
+int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, const int* expert_counts, void* act,
+                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* stream) {
+  clear_error();
+  if (!x_perm || !w1 || !w3 || !expert_counts || !act) return set_error(EK_ERR_INVALID, "gate_up_packed: null pointer");
+  if (rows < 0 || E < 1 || E > kMaxExpertsT || H % 16 != 0 || I % 8 != 0 || H <= 0 || I <= 0)
+    return set_error(EK_ERR_INVALID, "gate_up_packed: need 1 <= E <= %d, H %% 16 == 0, I %% 8 == 0", kMaxExpertsT);
+  if (!aligned16(x_perm) || !aligned16(w1) || !aligned16(w3) || !aligned16(act))
+    return set_error(EK_ERR_INVALID, "gate_up_packed: buffers must be 16-byte aligned");
+  if (rows == 0) return EK_OK;
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  int tok = 0, pr = 0;
+  packed_tiles(rows, E, S, tok_tile, pair, &tok, &pr);
+  const int ctas = pr ? 2 : 1;
+  CUtensorMap ta, tx, tb;
+  if ((rc = make_tmap_2d(&ta, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, 64)))
+    return rc;
+  if ((rc = make_tmap_2d(&tx, w3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, 64)))
+    return rc;
+  if ((rc = make_tmap_2d(&tb, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, rows, (uint64_t)H * 2, 64, tok / ctas)))
+    return rc;
+  GemmParams p{};
+  p.M = rows;
+  p.N = I;
+  p.K = H;
+  p.k_blocks = (H + 63) / 64;
+  p.C = act;
+  p.ldc = I;
+  p.num_experts = E;
+  p.expert_counts = expert_counts;
+  p.w_rows_per_expert = I;
+  p.feat_tiles = (I + 64 * ctas - 1) / (64 * ctas);
+  const int grid = std::max(1, S / ctas) * ctas;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pr) return launch_packed_tok<kEpiSwiGLUT, true>(tok, ta, tb, tx, p, grid, s);
+  return launch_packed_tok<kEpiSwiGLUT, false>(tok, ta, tb, tx, p, grid, s);
+}
+
+int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts, const int* sorted_slots,
+                       const float* topk_weights, void* y, int rows, int E, int H, int I, int T, int topk,
+                       int tok_tile, int pair, int num_sms, void* stream) {
+  clear_error();
+  if (!act || !w2 || !expert_counts || !sorted_slots || !topk_weights || !y)
+    return set_error(EK_ERR_INVALID, "down_packed: null pointer");
+  if (rows < 0 || E < 1 || E > kMaxExpertsT || I % 16 != 0 || H % 8 != 0 || H <= 0 || I <= 0 || T < 0 || topk < 1)
+    return set_error(EK_ERR_INVALID, "down_packed: need 1 <= E <= %d, I %% 16 == 0, H %% 8 == 0", kMaxExpertsT);
+  if (!aligned16(act) || !aligned16(w2) || !aligned16(y))
+    return set_error(EK_ERR_INVALID, "down_packed: buffers must be 16-byte aligned");
+  if (rows == 0) return EK_OK;
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  int tok = 0, pr = 0;
+  packed_tiles(rows, E, S, tok_tile, pair, &tok, &pr);
+  const int ctas = pr ? 2 : 1;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, w2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, (uint64_t)E * H, (uint64_t)I * 2, 64, 128)))
+    return rc;
+  if ((rc = make_tmap_2d(&tb, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, rows, (uint64_t)I * 2, 64, tok / ctas)))
+    return rc;
+  GemmParams p{};
+  p.M = rows;
+  p.N = H;
+  p.K = I;
+  p.k_blocks = (I + 63) / 64;
+  p.C = y;
+  p.ldc = H;
+  p.num_experts = E;
+  p.expert_counts = expert_counts;
+  p.w_rows_per_expert = H;
+  p.feat_tiles = (H + 128 * ctas - 1) / (128 * ctas);
+  p.sorted_slots = sorted_slots;
+  p.slot_weights = topk_weights;
+  p.num_slots = T * topk;
+  const int grid = std::max(1, S / ctas) * ctas;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pr) return launch_packed_tok<kEpiScatterT, true>(tok, ta, tb, ta, p, grid, s);
+  return launch_packed_tok<kEpiScatterT, false>(tok, ta, tb, ta, p, grid, s);
 }
 
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream) {

@@ -177,7 +177,7 @@ def run_moe_benchmark(sm_levels=None, moe_configs=None, rep_ms: float = 30.0, fu
     return results
 
 
-def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None) -> None:
+def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None, layout: str = "packed") -> None:
     """Run the Mixtral-shaped fused-MoE layer at `tokens` tokens a few times
     (no timing; a fixed launch sequence for profilers)."""
     import torch
@@ -193,7 +193,7 @@ def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None) -> None:
     x = torch.randn((tokens, H), device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn((tokens, E), device=dev, generator=g)
     for _ in range(reps):
-        _ops.fused_moe(x, logits, w1, w2, w3, k, num_sms=num_sms)
+        _ops.fused_moe(x, logits, w1, w2, w3, k, num_sms=num_sms, layout=layout)
     torch.cuda.synchronize()
 
 
@@ -205,9 +205,10 @@ def main():
     parser.add_argument("--layer-tokens", type=int, default=0,
                         help="only run the Mixtral fused-MoE layer at this token count (for profiling)")
     parser.add_argument("--reps", type=int, default=5)
+    parser.add_argument("--layout", choices=["packed", "padded"], default="packed")
     args = parser.parse_args()
     if args.layer_tokens > 0:
-        run_layer(args.layer_tokens, args.reps)
+        run_layer(args.layer_tokens, args.reps, layout=args.layout)
     elif args.all:
         run_gemm_benchmark()
         run_moe_benchmark()

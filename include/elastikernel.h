@@ -217,6 +217,21 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
                 const int* sorted_slots, const float* topk_weights, void* y, int max_rows, int E, int H, int I,
                 int T, int topk, int num_sms, int force_bn, void* stream);
 
+/* Packed (expert-major) variants of the two grouped GEMMs, over the layout
+ * ek_moe_permute produces with block_m = 1 (rows of expert e packed at
+ * [start_e, start_e + expert_counts[e]), rows = T * topk, no padding). The
+ * operands are swapped on the tensor cores: expert weight rows form the
+ * 128-row (or 256-row with pair = 1, a 2-SM CTA pair) side and the expert's
+ * tokens the N side, in tiles of tok_tile tokens (16/32/64/128/256). Weight
+ * tiles stream from HBM once per token tile, which keeps small token counts
+ * HBM-efficient. tok_tile = 0 and pair = -1 choose automatically.
+ * Results equal the block-padded variants'. E <= 256. */
+int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, const int* expert_counts, void* act,
+                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* stream);
+int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts, const int* sorted_slots,
+                       const float* topk_weights, void* y, int rows, int E, int H, int I, int T, int topk,
+                       int tok_tile, int pair, int num_sms, void* stream);
+
 /* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);
 

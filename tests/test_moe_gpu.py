@@ -85,17 +85,39 @@ def _moe_inputs(T, H, I, E, seed):
     return x, logits, w1, w2, w3
 
 
+@pytest.mark.parametrize("layout", ["packed", "padded"])
 @pytest.mark.parametrize("T,H,I,E,k", [(1, 512, 1024, 8, 2), (16, 512, 1024, 8, 2), (300, 256, 512, 8, 2),
-                                       (64, 256, 384, 16, 4), (200, 128, 256, 32, 8)])
-def test_fused_moe_small(cuda_dev, T, H, I, E, k):
+                                       (64, 256, 384, 16, 4), (200, 128, 256, 32, 8), (5, 256, 256, 64, 6)])
+def test_fused_moe_small(cuda_dev, T, H, I, E, k, layout):
     from elastikernel_b200 import _ops
 
     x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=T + I)
-    out = _ops.fused_moe(*(t.to(cuda_dev) for t in (x, logits, w1, w2, w3)), topk=k)
+    out = _ops.fused_moe(*(t.to(cuda_dev) for t in (x, logits, w1, w2, w3)), topk=k, layout=layout)
     torch.cuda.synchronize()
     ref = om.moe_ref(x, logits, w1, w2, w3, k)
     err = og.max_rel_err(out, ref)
     assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("tok", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("pair", [0, 1])
+def test_packed_token_tiles(cuda_dev, tok, pair):
+    """Swapped-operand GEMMs for every token tile, single CTA and CTA pair,
+    with ragged per-expert token counts and an unused expert."""
+    from elastikernel_b200 import _ops
+
+    T, H, I, E, k = 700, 256, 384, 8, 2
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=tok + pair)
+    logits[:, 5] = -30.0  # expert 5 receives no tokens
+    d = [t.to(cuda_dev) for t in (x, logits, w1, w2, w3)]
+    ids, wts = _ops.moe_route(d[1], k)
+    perm = _ops.moe_permute(ids, E, x=d[0], block_m=1)
+    act = _ops.moe_gate_up_packed(perm, d[2], d[4], tok_tile=tok, pair=pair)
+    y = _ops.moe_down_packed(perm, act, d[3], wts, tok_tile=tok, pair=pair)
+    out = _ops.moe_combine(y, T, k)
+    torch.cuda.synchronize()
+    assert int(perm["expert_counts"][5].item()) == 0
+    assert og.max_rel_err(out, om.moe_ref(x, logits, w1, w2, w3, k)) <= TOL
 
 
 @pytest.mark.parametrize("T", [1, 16, 128])
