@@ -81,7 +81,7 @@ struct GemmCfg {
       kSwapped ? (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + 64 * 33 * 4 + 127) / 128 * 128 : 0;
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                  : (2 * BN <= 256) ? 256 : 512;
   static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);

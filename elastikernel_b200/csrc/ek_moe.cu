@@ -13,6 +13,7 @@
 //   segment    the reference's CSR segment GEMM (sm_aware_benchmark.py:228-290)
 #include <algorithm>
 #include <cfloat>
+#include <cmath>
 
 #include "ek_gemm_kernel.cuh"
 #include "ek_internal.h"
@@ -292,14 +293,17 @@ int launch_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
 }
 
 // Token tile (N of the swapped MMA) and CTA-pair choice for the packed
-// expert-major GEMMs: the tile covers the average tokens of a used expert.
+// expert-major GEMMs. A weight tile is streamed once per token tile, so the
+// tile should hold the busiest expert's tokens: size it for the mean plus
+// three standard deviations of a uniform routing's per-expert count.
 void packed_tiles(long long n_slots, int E, int S, int force_tok, int force_pair, int* tok, int* pair) {
   int t = force_tok;
   if (t <= 0) {
-    const long long used = std::max<long long>(1, std::min<long long>(E, n_slots));
-    const long long avg = (n_slots + used - 1) / used;
+    const double used = (double)std::max<long long>(1, std::min<long long>(E, n_slots));
+    const double avg = (double)n_slots / used;
+    const double want = avg + 3.0 * std::sqrt(avg) + 1.0;
     t = 16;
-    while (t < avg && t < 256) t *= 2;
+    while (t < want && t < 256) t *= 2;
   }
   *tok = t;
   *pair = force_pair >= 0 ? force_pair : (t >= 128 && S >= 2 ? 1 : 0);
