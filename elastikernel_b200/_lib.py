@@ -85,6 +85,12 @@ _SIGNATURES = {
     "ek_moe_gate_up_packed": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp] + [_c_int] * 7 + [_c_vp]),
     "ek_moe_down_packed": (_c_int, [_c_vp] * 6 + [_c_int] * 9 + [_c_vp]),
     "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
+    "ek_moe_gate_up_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 6 + [_c_vp]),
+    "ek_moe_down_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 8 + [_c_vp]),
+    "ek_moe_gather_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
+    "ek_moe_slot_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),
+    "ek_ep_pack_meta": (_c_int, [_c_vp, _c_int, _c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_moe_combine_rows": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_segment_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                      _c_vp]),
 }

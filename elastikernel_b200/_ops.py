@@ -338,6 +338,74 @@ def moe_down_packed(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weight
     return y
 
 
+def quant_moe_weights_fp8(w1: torch.Tensor, w2: torch.Tensor, w3: torch.Tensor) -> dict:
+    """e4m3 expert weights with 128 x 128 fp32 block scales (DeepSeek style).
+    w1, w3 [E, I, H] and w2 [E, H, I] (bf16 or fp32); I and H multiples of 128."""
+    E, I, H = w1.shape
+    if I % 128 or H % 128:
+        raise RuntimeError("block-scaled FP8 needs I and H multiples of 128")
+    out = {"E": E, "I": I, "H": H}
+    for name, w, rows, cols in (("w1", w1, I, H), ("w3", w3, I, H), ("w2", w2, H, I)):
+        q, s = quant_e4m3(w.reshape(E * rows, cols).contiguous(), block=(128, 128))
+        out[name + "q"] = q.view(E, rows, cols)
+        out[name + "s"] = s
+    return out
+
+
+def moe_gate_up_fp8bs(perm: dict, xq: torch.Tensor, xs: torch.Tensor, qw: dict, num_sms: int | None = None,
+                      tok_tile: int = 0) -> torch.Tensor:
+    """Block-scaled FP8 gate/up (SwiGLU) over the packed layout; bf16 act [rows, I]."""
+    dev = _require_cuda(xq, xs)
+    if perm["block_m"] != 1:
+        raise RuntimeError("the FP8 block-scaled GEMMs take the packed layout (block_m=1)")
+    rows, E, H, I = perm["max_rows"], qw["E"], qw["H"], qw["I"]
+    if xq.shape != (rows, H) or xs.shape != (rows, H // 128):
+        raise RuntimeError("gate_up_fp8bs: activation shape mismatch")
+    act = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_gate_up_fp8bs(xq.data_ptr(), xs.data_ptr(), qw["w1q"].data_ptr(), qw["w3q"].data_ptr(),
+                                         qw["w1s"].data_ptr(), qw["w3s"].data_ptr(), perm["expert_counts"].data_ptr(),
+                                         act.data_ptr(), rows, E, H, I, int(tok_tile), int(num_sms or 0),
+                                         current_stream_handle(dev)), "ek_moe_gate_up_fp8bs")
+    return act
+
+
+def moe_down_fp8bs(perm: dict, aq: torch.Tensor, as_: torch.Tensor, qw: dict, topk_weights: torch.Tensor,
+                   num_sms: int | None = None, tok_tile: int = 0) -> torch.Tensor:
+    """Block-scaled FP8 down projection with the routing weight, scattered to slots (bf16 [T*k, H])."""
+    dev = _require_cuda(aq, as_, topk_weights)
+    rows, E, H, I = perm["max_rows"], qw["E"], qw["H"], qw["I"]
+    T, k = perm["T"], perm["topk"]
+    if aq.shape != (rows, I) or as_.shape != (rows, I // 128) or topk_weights.numel() != T * k:
+        raise RuntimeError("down_fp8bs: shape mismatch")
+    y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_down_fp8bs(aq.data_ptr(), as_.data_ptr(), qw["w2q"].data_ptr(), qw["w2s"].data_ptr(),
+                                      perm["expert_counts"].data_ptr(), perm["sorted_slots"].data_ptr(),
+                                      topk_weights.data_ptr(), y.data_ptr(), rows, E, H, I, T, k, int(tok_tile),
+                                      int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_fp8bs")
+    return y
+
+
+def fused_moe_fp8(hidden_states: torch.Tensor, gate_logits: torch.Tensor, qw: dict, topk: int,
+                  out: torch.Tensor | None = None, num_sms: int | None = None) -> torch.Tensor:
+    """MoE layer with e4m3 block-scaled experts: route -> permute(+gather) ->
+    quantise rows (1 x 128 groups) -> FP8 gate/up SwiGLU -> quantise act ->
+    FP8 down (+weight) -> combine."""
+    _require_cuda(hidden_states, gate_logits, out)
+    _check_bf16("hidden_states", hidden_states)
+    T = hidden_states.shape[0]
+    if T == 0:
+        return out if out is not None else torch.empty_like(hidden_states)
+    ids, wts = moe_route(gate_logits, topk)
+    perm = moe_permute(ids, qw["E"], x=hidden_states, block_m=1)
+    xq, xs = quant_e4m3(perm["x_perm"], block=(1, 128))
+    act = moe_gate_up_fp8bs(perm, xq, xs, qw, num_sms=num_sms)
+    aq, as_ = quant_e4m3(act, block=(1, 128))
+    y = moe_down_fp8bs(perm, aq, as_, qw, wts, num_sms=num_sms)
+    return moe_combine(y, T, topk, out=out)
+
+
 def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_j y[t*k + j] (fp32 sum in j order), bf16."""
     dev = _require_cuda(y, out)

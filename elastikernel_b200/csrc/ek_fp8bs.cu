@@ -1,0 +1,149 @@
+// Entry points of the FP8 block-scaled grouped GEMMs (ek_fp8bs_kernel.cuh).
+#include <algorithm>
+#include <cmath>
+
+#include "ek_fp8bs_kernel.cuh"
+#include "ek_internal.h"
+
+namespace ek {
+
+int register_status_reader(int (*fn)(int, int*));
+
+namespace {
+
+int read_status(int clear, int* v) {
+  int rc = check_cuda(cudaMemcpyFromSymbol(v, g_ek_status, sizeof(int)), "read status");
+  if (rc) return rc;
+  if (clear) {
+    int z = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_ek_status, &z, sizeof(int)), "clear status");
+  }
+  return rc;
+}
+const int s_status_reg = register_status_reader(read_status);
+
+template <class Cfg>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const Fp8BsParams& P, int grid,
+           cudaStream_t s) {
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
+  if (!attr_done[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_fp8bs_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::SMEM_BYTES),
+                        "cudaFuncSetAttribute(fp8bs)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  gemm_fp8bs_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tx, P);
+  return check_cuda(cudaGetLastError(), "fp8 block-scaled launch");
+}
+
+template <int kEpi>
+int launch_tok(int tok, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const Fp8BsParams& P,
+               int grid, cudaStream_t s) {
+  switch (tok) {
+    case 16: return launch<Fp8BsCfg<16, kEpi>>(ta, tb, tx, P, grid, s);
+    case 32: return launch<Fp8BsCfg<32, kEpi>>(ta, tb, tx, P, grid, s);
+    case 64: return launch<Fp8BsCfg<64, kEpi>>(ta, tb, tx, P, grid, s);
+    case 128: return launch<Fp8BsCfg<128, kEpi>>(ta, tb, tx, P, grid, s);
+  }
+  return set_error(EK_ERR_INVALID, "fp8 block-scaled token tile must be 16, 32, 64 or 128 (got %d)", tok);
+}
+
+// Token tile sized for the busiest expert (mean + 3 sigma), at most 128.
+int tok_tile(long long rows, int E, int force) {
+  if (force > 0) return force;
+  const double used = (double)std::max<long long>(1, std::min<long long>(E, rows));
+  const double avg = (double)rows / used;
+  const double want = avg + 3.0 * std::sqrt(avg) + 1.0;
+  int t = 16;
+  while (t < want && t < 128) t *= 2;
+  return t;
+}
+
+}  // namespace
+}  // namespace ek
+
+using namespace ek;
+
+extern "C" {
+
+int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, const void* w3q,
+                         const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
+                         int E, int H, int I, int tok, int num_sms, void* stream) {
+  clear_error();
+  if (!xq || !x_scale || !w1q || !w3q || !w1_scale || !w3_scale || !expert_counts || !act)
+    return set_error(EK_ERR_INVALID, "gate_up_fp8bs: null pointer");
+  if (rows < 0 || E < 1 || E > kMaxExpertsT || H % 128 != 0 || I % 128 != 0 || H <= 0 || I <= 0)
+    return set_error(EK_ERR_INVALID, "gate_up_fp8bs: need 1 <= E <= %d and H, I multiples of 128", kMaxExpertsT);
+  if (!aligned16(xq) || !aligned16(w1q) || !aligned16(w3q) || !aligned16(act))
+    return set_error(EK_ERR_INVALID, "gate_up_fp8bs: buffers must be 16-byte aligned");
+  if (rows == 0) return EK_OK;
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  const int t = tok_tile(rows, E, tok);
+  CUtensorMap ta, tx, tb;
+  if ((rc = make_tmap_2d(&ta, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
+  if ((rc = make_tmap_2d(&tx, w3q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
+  if ((rc = make_tmap_2d(&tb, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, rows, H, 128, t))) return rc;
+  Fp8BsParams P{};
+  P.g.M = rows;
+  P.g.N = I;
+  P.g.K = H;
+  P.g.k_blocks = H / 128;
+  P.g.C = act;
+  P.g.ldc = I;
+  P.g.num_experts = E;
+  P.g.expert_counts = expert_counts;
+  P.g.w_rows_per_expert = I;
+  P.g.feat_tiles = I / 64;
+  P.x_scale = x_scale;
+  P.w_scale = w1_scale;
+  P.w_scale2 = w3_scale;
+  P.ksb = H / 128;
+  return launch_tok<kEpiSwiGLUT>(t, ta, tb, tx, P, S, static_cast<cudaStream_t>(stream));
+}
+
+int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
+                      const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
+                      int E, int H, int I, int T, int topk, int tok, int num_sms, void* stream) {
+  clear_error();
+  if (!aq || !a_scale || !w2q || !w2_scale || !expert_counts || !sorted_slots || !topk_weights || !y)
+    return set_error(EK_ERR_INVALID, "down_fp8bs: null pointer");
+  if (rows < 0 || E < 1 || E > kMaxExpertsT || H % 128 != 0 || I % 128 != 0 || H <= 0 || I <= 0 || T < 0 || topk < 1)
+    return set_error(EK_ERR_INVALID, "down_fp8bs: need 1 <= E <= %d and H, I multiples of 128", kMaxExpertsT);
+  if (!aligned16(aq) || !aligned16(w2q) || !aligned16(y))
+    return set_error(EK_ERR_INVALID, "down_fp8bs: buffers must be 16-byte aligned");
+  if (rows == 0) return EK_OK;
+  int S = 0;
+  int rc = resolve_num_sms(num_sms, stream, &S);
+  if (rc) return rc;
+  const int t = tok_tile(rows, E, tok);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_2d(&ta, w2q, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, (uint64_t)E * H, I, 128, 128))) return rc;
+  if ((rc = make_tmap_2d(&tb, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, rows, I, 128, t))) return rc;
+  Fp8BsParams P{};
+  P.g.M = rows;
+  P.g.N = H;
+  P.g.K = I;
+  P.g.k_blocks = I / 128;
+  P.g.C = y;
+  P.g.ldc = H;
+  P.g.num_experts = E;
+  P.g.expert_counts = expert_counts;
+  P.g.w_rows_per_expert = H;
+  P.g.feat_tiles = H / 128;
+  P.g.sorted_slots = sorted_slots;
+  P.g.slot_weights = topk_weights;
+  P.g.num_slots = T * topk;
+  P.x_scale = a_scale;
+  P.w_scale = w2_scale;
+  P.w_scale2 = w2_scale;
+  P.ksb = I / 128;
+  return launch_tok<kEpiScatterT>(t, ta, tb, ta, P, S, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

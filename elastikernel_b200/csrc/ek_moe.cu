@@ -613,6 +613,20 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
   return launch_packed_tok<kEpiScatterT, false>(tok, ta, tb, ta, p, grid, s);
 }
 
+int ek_moe_gather_rows(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
+                       const void* src, int row_bytes, void* dst, void* stream) {
+  clear_error();
+  if (!sorted_slots || !num_rows_padded || !src || !dst || max_rows < 0 || n_slots < 0 || topk < 1 ||
+      row_bytes <= 0 || row_bytes % 16 != 0 || !aligned16(src) || !aligned16(dst))
+    return set_error(EK_ERR_INVALID, "gather_rows: bad arguments (rows must be 16-byte multiples, aligned)");
+  if (max_rows == 0) return EK_OK;
+  const int blocks = (int)std::min<long long>((max_rows + 7) / 8, 148LL * 8);
+  gather_rows_kernel<<<std::max(blocks, 1), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      sorted_slots, num_rows_padded, max_rows, n_slots, topk, static_cast<const uint8_t*>(src), row_bytes,
+      static_cast<uint8_t*>(dst));
+  return check_cuda(cudaGetLastError(), "gather_rows launch");
+}
+
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream) {
   clear_error();
   if (T < 0 || topk < 1 || H % 8 != 0) return set_error(EK_ERR_INVALID, "combine: H must be a multiple of 8");

@@ -1,0 +1,184 @@
+"""Expert-parallel fused MoE across the GPUs of one node (one process per GPU).
+
+Experts are split contiguously: rank g owns experts [g*Eg, (g+1)*Eg),
+Eg = num_experts / world_size. One forward pass:
+
+1. route locally (softmax top-k, renormalised);
+2. sort the (token, choice) slots by destination rank and gather their rows
+   (ek_moe_permute with the ranks as "experts", block_m = 1), with each row's
+   expert id local to its destination and its routing weight (ek_ep_pack_meta);
+3. exchange the per-rank counts, then the rows and their metadata
+   (all-to-all over NCCL / NVLink);
+4. run the received rows through the local experts (packed expert-major
+   GEMMs), each output row already multiplied by its routing weight;
+5. send the rows back (all-to-all with the splits reversed);
+6. sum every token's k returned rows in choice order (ek_moe_combine_rows).
+
+The reference has no multi-GPU path (its only parallelism is SM partitioning
+inside one GPU); this follows the expert-parallel MoE layout of the hot-path
+spec. The kernel steps go through an ``ops`` object: ``CudaEPOps`` (the
+product, C-ABI kernels) or any object with the same methods (the tests drive
+the same orchestration with a CPU implementation on gloo ranks).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Dispatched:
+    """Per-forward bookkeeping kept between dispatch and combine."""
+
+    T: int
+    topk: int
+    send_counts: list
+    recv_counts: list
+    slot_row: torch.Tensor  # [T*k] row of every slot in send order
+
+
+class CudaEPOps:
+    """Kernel steps of the expert-parallel MoE on the C-ABI kernels."""
+
+    def __init__(self, num_sms: int | None = None):
+        self.num_sms = num_sms
+
+    def route(self, logits, topk):
+        from . import _ops
+
+        return _ops.moe_route(logits, topk)
+
+    def dest_of(self, ids, experts_per_rank):
+        return torch.div(ids, experts_per_rank, rounding_mode="floor").to(torch.int32)
+
+    def permute_by_dest(self, dest, world, x):
+        from . import _ops
+
+        return _ops.moe_permute(dest.contiguous(), world, x=x, block_m=1)
+
+    def pack_meta(self, perm, ids, wts, experts_per_rank):
+        from . import _lib, _ops
+
+        rows = perm["max_rows"]
+        dev = ids.device
+        local_ids = torch.empty(rows, dtype=torch.int32, device=dev)
+        wout = torch.empty(rows, dtype=torch.float32, device=dev)
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_ep_pack_meta(perm["sorted_slots"].data_ptr(), rows, ids.data_ptr(),
+                                                  wts.data_ptr(), ids.numel(), experts_per_rank,
+                                                  local_ids.data_ptr(), wout.data_ptr(),
+                                                  _ops.current_stream_handle(dev)), "ek_ep_pack_meta")
+        return local_ids, wout
+
+    def slot_rows(self, perm):
+        from . import _lib, _ops
+
+        dev = perm["sorted_slots"].device
+        n = perm["T"] * perm["topk"]
+        slot_row = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_moe_slot_rows(perm["sorted_slots"].data_ptr(), perm["num_rows_padded"].data_ptr(),
+                                                   perm["max_rows"], n, slot_row.data_ptr(),
+                                                   _ops.current_stream_handle(dev)), "ek_moe_slot_rows")
+        return slot_row
+
+    def experts(self, x_recv, local_ids, w_recv, w1, w2, w3):
+        """Local experts on the received rows; row r of the result is
+        w_recv[r] * expert(local_ids[r])(x_recv[r])."""
+        from . import _ops
+
+        R = x_recv.shape[0]
+        H = w2.shape[1]
+        if R == 0:
+            return torch.empty((0, H), dtype=torch.bfloat16, device=x_recv.device)
+        E = w1.shape[0]
+        layout = _ops.moe_layout(int(self.num_sms or _ops._stream_sms(x_recv.device, _ops.current_stream_handle(
+            x_recv.device))), E)
+        if layout == "packed":
+            perm = _ops.moe_permute(local_ids.view(R, 1), E, x=x_recv, block_m=1)
+            act = _ops.moe_gate_up_packed(perm, w1, w3, num_sms=self.num_sms)
+            return _ops.moe_down_packed(perm, act, w2, w_recv, num_sms=self.num_sms)
+        perm = _ops.moe_permute(local_ids.view(R, 1), E, x=x_recv)
+        act = _ops.moe_gate_up(perm, w1, w3, num_sms=self.num_sms)
+        return _ops.moe_down(perm, act, w2, w_recv, num_sms=self.num_sms)
+
+    def combine_rows(self, y_back, slot_row, T, topk):
+        from . import _lib, _ops
+
+        dev = y_back.device
+        H = y_back.shape[1]
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_moe_combine_rows(y_back.data_ptr(), slot_row.data_ptr(), out.data_ptr(), T, topk,
+                                                      H, y_back.shape[0], _ops.current_stream_handle(dev)),
+                       "ek_moe_combine_rows")
+        return out
+
+
+class ExpertParallelMoE:
+    """Expert-parallel MoE layer. Each rank holds the weights of its own experts:
+    w1, w3 [Eg, I, H] and w2 [Eg, H, I] (bf16)."""
+
+    def __init__(self, num_experts: int, topk: int, w1, w2, w3, group=None, ops=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % self.world != 0:
+            raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
+        self.num_experts = num_experts
+        self.experts_per_rank = num_experts // self.world
+        if w1.shape[0] != self.experts_per_rank:
+            raise ValueError(f"rank holds {w1.shape[0]} experts, expected {self.experts_per_rank}")
+        self.topk = topk
+        self.w1, self.w2, self.w3 = w1, w2, w3
+        self.ops = ops or CudaEPOps()
+
+    # ---------------------------------------------------------------- phases
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out.copy_(inp)
+            return out
+        dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=self.group)
+        return out
+
+    def dispatch(self, x, gate_logits):
+        """Route, sort by destination and exchange rows + metadata.
+        Returns (x_recv, local_ids_recv, w_recv, Dispatched)."""
+        ops = self.ops
+        T, H = x.shape
+        ids, wts = ops.route(gate_logits, self.topk)
+        dest = ops.dest_of(ids, self.experts_per_rank)
+        perm = ops.permute_by_dest(dest, self.world, x)
+        local_ids, row_w = ops.pack_meta(perm, ids, wts, self.experts_per_rank)
+        counts = perm["expert_counts"].to(torch.int64)
+        recv = torch.empty_like(counts)
+        self._a2a(recv, counts, None, None)
+        send_counts = counts.cpu().tolist()
+        recv_counts = recv.cpu().tolist()
+        R = int(sum(recv_counts))
+        n = T * self.topk
+        x_send = perm["x_perm"][:n]
+        x_recv = torch.empty((R, H), dtype=x.dtype, device=x.device)
+        self._a2a(x_recv, x_send, recv_counts, send_counts)
+        ids_recv = torch.empty(R, dtype=torch.int32, device=x.device)
+        self._a2a(ids_recv, local_ids[:n], recv_counts, send_counts)
+        w_recv = torch.empty(R, dtype=torch.float32, device=x.device)
+        self._a2a(w_recv, row_w[:n], recv_counts, send_counts)
+        slot_row = ops.slot_rows(perm)
+        return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, send_counts, recv_counts, slot_row)
+
+    def combine(self, y_local, d: Dispatched):
+        n = d.T * d.topk
+        y_back = torch.empty((n, y_local.shape[1]), dtype=y_local.dtype, device=y_local.device)
+        self._a2a(y_back, y_local, d.send_counts, d.recv_counts)
+        return self.ops.combine_rows(y_back, d.slot_row, d.T, d.topk)
+
+    def forward(self, x, gate_logits):
+        x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)
+        y_local = self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
+        return self.combine(y_local, d)
+
+    __call__ = forward

@@ -232,6 +232,42 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
                        const float* topk_weights, void* y, int rows, int E, int H, int I, int T, int topk,
                        int tok_tile, int pair, int num_sms, void* stream);
 
+/* FP8 e4m3 packed grouped GEMMs with DeepSeek-style scales: weights with
+ * 128 x 128 fp32 block scales (w*_scale [E*rows/128][K/128]), tokens with
+ * 1 x 128 fp32 group scales (x_scale / a_scale [rows][K/128]); fp32
+ * accumulation with the scales applied per 128-wide K block; bf16 outputs as
+ * ek_moe_gate_up_packed / ek_moe_down_packed. H and I must be multiples of
+ * 128; tok = token tile (16/32/64/128, 0 = choose). No counterpart in the
+ * reference (it has no FP8 path). */
+int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, const void* w3q,
+                         const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
+                         int E, int H, int I, int tok, int num_sms, void* stream);
+int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
+                      const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
+                      int E, int H, int I, int T, int topk, int tok, int num_sms, void* stream);
+
+/* Row gather of the padded/packed layout: dst[r] = src[sorted_slots[r] / topk]
+ * for the used rows r < *num_rows_padded with a valid slot (row_bytes a
+ * multiple of 16). Used to gather rows of a second tensor (e.g. FP8 scales)
+ * with a permutation ek_moe_permute already made. */
+int ek_moe_gather_rows(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
+                       const void* src, int row_bytes, void* dst, void* stream);
+
+/* Expert-parallel helpers (no counterpart in the reference, which has no
+ * multi-GPU path). After a permutation by destination rank:
+ *   ek_moe_slot_rows     slot_row[sorted_slots[r]] = r for the used rows
+ *                        (the row each slot occupies in send order);
+ *   ek_ep_pack_meta      per send row r: local_ids[r] = topk_ids[s] % experts_per_rank,
+ *                        weights_out[r] = topk_weights[s], s = sorted_slots[r];
+ *   ek_moe_combine_rows  out[t] = sum_j y[slot_row[t*k + j]] (fp32, j order), bf16,
+ *                        rows outside [0, n_rows) skipped. */
+int ek_moe_slot_rows(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int* slot_row,
+                     void* stream);
+int ek_ep_pack_meta(const int* sorted_slots, int rows, const int* topk_ids, const float* topk_weights, int n_slots,
+                    int experts_per_rank, int* local_ids, float* weights_out, void* stream);
+int ek_moe_combine_rows(const void* y, const int* slot_row, void* out, int T, int topk, int H, int n_rows,
+                        void* stream);
+
 /* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);
 
