@@ -104,6 +104,40 @@ class CudaEPOps:
         act = _ops.moe_gate_up(perm, w1, w3, num_sms=self.num_sms)
         return _ops.moe_down(perm, act, w2, w_recv, num_sms=self.num_sms)
 
+    # ---------------------------------------------------------------- FP8 dispatch
+    def quant_rows(self, x):
+        from . import _ops
+
+        return _ops.quant_e4m3(x, block=(1, 128))
+
+    def gather_rows(self, perm, src):
+        """Rows of `src` in the permutation's order (e.g. the scales of gathered FP8 rows)."""
+        from . import _lib, _ops
+
+        dev = src.device
+        rows = perm["max_rows"]
+        dst = torch.empty((rows,) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
+        row_bytes = src[0].numel() * src.element_size()
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_moe_gather_rows(perm["sorted_slots"].data_ptr(), perm["num_rows_padded"].data_ptr(),
+                                                     rows, perm["T"] * perm["topk"], perm["topk"], src.data_ptr(),
+                                                     row_bytes, dst.data_ptr(), _ops.current_stream_handle(dev)),
+                       "ek_moe_gather_rows")
+        return dst
+
+    def experts_fp8(self, xq_recv, xs_recv, local_ids, w_recv, qw):
+        """Local block-scaled FP8 experts on received e4m3 rows and their 1 x 128 scales."""
+        from . import _ops
+
+        R = xq_recv.shape[0]
+        if R == 0:
+            return torch.empty((0, qw["H"]), dtype=torch.bfloat16, device=xq_recv.device)
+        perm = _ops.moe_permute(local_ids.view(R, 1), qw["E"], x=xq_recv, block_m=1)
+        xs = self.gather_rows(perm, xs_recv)
+        act = _ops.moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=self.num_sms)
+        aq, as_ = _ops.quant_e4m3(act, block=(1, 128))
+        return _ops.moe_down_fp8bs(perm, aq, as_, qw, w_recv, num_sms=self.num_sms)
+
     def combine_rows(self, y_back, slot_row, T, topk):
         from . import _lib, _ops
 
@@ -119,9 +153,11 @@ class CudaEPOps:
 
 class ExpertParallelMoE:
     """Expert-parallel MoE layer. Each rank holds the weights of its own experts:
-    w1, w3 [Eg, I, H] and w2 [Eg, H, I] (bf16)."""
+    w1, w3 [Eg, I, H] and w2 [Eg, H, I] (bf16), or ``qw`` = their e4m3
+    block-scaled form (_ops.quant_moe_weights_fp8), in which case the rows
+    are dispatched as e4m3 with 1 x 128 scales (half the bytes of bf16)."""
 
-    def __init__(self, num_experts: int, topk: int, w1, w2, w3, group=None, ops=None):
+    def __init__(self, num_experts: int, topk: int, w1=None, w2=None, w3=None, group=None, ops=None, qw=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -129,10 +165,12 @@ class ExpertParallelMoE:
             raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
         self.num_experts = num_experts
         self.experts_per_rank = num_experts // self.world
-        if w1.shape[0] != self.experts_per_rank:
-            raise ValueError(f"rank holds {w1.shape[0]} experts, expected {self.experts_per_rank}")
+        self.fp8 = qw is not None
+        held = qw["E"] if self.fp8 else w1.shape[0]
+        if held != self.experts_per_rank:
+            raise ValueError(f"rank holds {held} experts, expected {self.experts_per_rank}")
         self.topk = topk
-        self.w1, self.w2, self.w3 = w1, w2, w3
+        self.w1, self.w2, self.w3, self.qw = w1, w2, w3, qw
         self.ops = ops or CudaEPOps()
 
     # ---------------------------------------------------------------- phases
@@ -151,6 +189,9 @@ class ExpertParallelMoE:
         T, H = x.shape
         ids, wts = ops.route(gate_logits, self.topk)
         dest = ops.dest_of(ids, self.experts_per_rank)
+        xs = None
+        if self.fp8:
+            x, xs = ops.quant_rows(x)  # e4m3 rows + 1 x 128 scales travel instead of bf16
         perm = ops.permute_by_dest(dest, self.world, x)
         local_ids, row_w = ops.pack_meta(perm, ids, wts, self.experts_per_rank)
         counts = perm["expert_counts"].to(torch.int64)
@@ -162,10 +203,17 @@ class ExpertParallelMoE:
         n = T * self.topk
         x_send = perm["x_perm"][:n]
         x_recv = torch.empty((R, H), dtype=x.dtype, device=x.device)
-        self._a2a(x_recv, x_send, recv_counts, send_counts)
-        ids_recv = torch.empty(R, dtype=torch.int32, device=x.device)
+        if self.fp8:  # byte view: the exchange does not need to know the float8 type
+            self._a2a(x_recv.view(torch.uint8), x_send.view(torch.uint8), recv_counts, send_counts)
+            xs_send = ops.gather_rows(perm, xs)[:n]
+            xs_recv = torch.empty((R, xs.shape[1]), dtype=torch.float32, device=x.device)
+            self._a2a(xs_recv, xs_send, recv_counts, send_counts)
+            x_recv = (x_recv, xs_recv)
+        else:
+            self._a2a(x_recv, x_send, recv_counts, send_counts)
+        ids_recv = torch.empty(R, dtype=torch.int32, device=ids.device)
         self._a2a(ids_recv, local_ids[:n], recv_counts, send_counts)
-        w_recv = torch.empty(R, dtype=torch.float32, device=x.device)
+        w_recv = torch.empty(R, dtype=torch.float32, device=ids.device)
         self._a2a(w_recv, row_w[:n], recv_counts, send_counts)
         slot_row = ops.slot_rows(perm)
         return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, send_counts, recv_counts, slot_row)
@@ -178,7 +226,10 @@ class ExpertParallelMoE:
 
     def forward(self, x, gate_logits):
         x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)
-        y_local = self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
+        if self.fp8:
+            y_local = self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw)
+        else:
+            y_local = self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
         return self.combine(y_local, d)
 
     __call__ = forward
