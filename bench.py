@@ -235,6 +235,68 @@ def fp8_bench(dev, peak_bf16_tflops: float, steps: int) -> dict:
             "fp8_peak_tflops": peak_fp8, "peak_note": "2 x measured bf16 burst", "results": res}
 
 
+def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float) -> dict:
+    """DeepSeek-V3-shaped expert-parallel MoE: 256 experts, top-8 softmax
+    routing, H=7168, I=2048, e4m3 experts with 128 x 128 block scales, 4096
+    tokens per rank, 256/world experts per rank, e4m3 dispatch over NCCL
+    all-to-all. The expert GEMMs run in a 112-SM green-context partition
+    disjoint from a 32-SM one (a 116-SM request rounds up to 120, which with
+    32 exceeds 148)."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.ep_moe import CudaEPOps, ExpertParallelMoE
+    from elastikernel_b200.green_ctx import create_disjoint_partitions, get_total_sm_count
+
+    E, k, H, I, T = 256, 8, 7168, 2048, 4096
+    eg = E // world
+    rank = int(os.environ.get("RANK", 0))
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    parts = {"w1q": [], "w1s": [], "w3q": [], "w3s": [], "w2q": [], "w2s": []}
+    for c0 in range(0, eg, 32):  # quantise in chunks to bound the bf16 staging memory
+        n = min(32, eg - c0)
+        w1 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w3 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn((n, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        q = _ops.quant_moe_weights_fp8(w1, w2, w3)
+        for key in parts:
+            parts[key].append(q[key])
+        del w1, w2, w3, q
+    qw = {"E": eg, "I": I, "H": H}
+    for key, lst in parts.items():
+        qw[key] = torch.cat(lst, dim=0)
+    del parts
+    gx = torch.Generator(device=dev).manual_seed(42 + rank)
+    x = torch.randn((T, H), device=dev, generator=gx).to(torch.bfloat16)
+    logits = torch.randn((T, E), device=dev, generator=gx)
+    total = get_total_sm_count(dev)
+    if total >= 148:
+        (comm_stream, comm_sms), (gemm_stream, gemm_sms) = create_disjoint_partitions(dev, [32, 112])
+    else:
+        gemm_stream, gemm_sms = torch.cuda.current_stream(dev), total
+    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms))
+    with torch.cuda.stream(gemm_stream):
+        for _ in range(2):
+            moe(x, logits)
+        torch.cuda.synchronize()
+        barrier(world)
+        reps = max(3, steps // 10)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            moe(x, logits)
+        e.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+    flop = T * k * 6.0 * H * I
+    tf = flop / (ms * 1e-3) / 1e12
+    peak_fp8 = 2.0 * peak_bf16_tflops
+    return {"config": "DeepSeek-V3-shaped: E=256 top-8 H=7168 I=2048, e4m3 128x128 block scales, 4096 tokens/rank, "
+                      f"{eg} experts/rank, e4m3 dispatch via NCCL all-to-all",
+            "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
+            "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms,
+            "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
+            "host_sync": "per-layer count exchange read on the host (all-to-all split sizes)"}
+
+
 def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:
     """Mixtral-shaped fused MoE (E=8, top-2, H=4096, I=14336, bf16) tokens/s."""
     from elastikernel_b200 import _ops
@@ -329,6 +391,9 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
 
+        # NCCL's kernels for the expert all-to-all get at most 32 CTAs, the
+        # size of the communication partition beside the 112-SM GEMM partition
+        os.environ.setdefault("NCCL_MAX_CTAS", "32")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     from elastikernel_b200 import _lib, sm_aware_matmul as smm
@@ -396,6 +461,7 @@ def main() -> None:
         extras["partitions"] = partition_sweep(dev, peak_tf, args.steps)
         extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
         extras["moe"] = moe_bench(dev, args.steps, hbm)
+        extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
         if rank == 0 and world == 1:
             extras["cpu_baseline"] = cpu_baseline_sample()
     if world > 1:

@@ -70,6 +70,7 @@ _SIGNATURES = {
     "ek_gemm_fp8": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                              _c_vp, _c_size, _c_vp]),
     "ek_quant_e4m3": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_quant_e4m3_kmajor": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_gemm_noalloc": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _c_vp]),
     "ek_gemm_noalloc_max_scratch_bytes": (_c_size, []),
@@ -85,9 +86,10 @@ _SIGNATURES = {
     "ek_moe_gate_up_packed": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp] + [_c_int] * 7 + [_c_vp]),
     "ek_moe_down_packed": (_c_int, [_c_vp] * 6 + [_c_int] * 9 + [_c_vp]),
     "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
-    "ek_moe_gate_up_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 6 + [_c_vp]),
-    "ek_moe_down_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 8 + [_c_vp]),
+    "ek_moe_gate_up_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 7 + [_c_vp]),
+    "ek_moe_down_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 9 + [_c_vp]),
     "ek_moe_gather_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
+    "ek_moe_gather_cols_f32": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
     "ek_moe_slot_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),
     "ek_ep_pack_meta": (_c_int, [_c_vp, _c_int, _c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_combine_rows": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp]),

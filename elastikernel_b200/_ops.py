@@ -158,6 +158,43 @@ def quant_e4m3(x: torch.Tensor, block: tuple[int, int] = (1, 0)) -> tuple[torch.
     return q, scales
 
 
+def quant_e4m3_kmajor(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """e4m3 codes and 1 x 128 group scales of a bf16/fp32 [rows, cols] tensor, the
+    scales K-block-major: [ceil(cols/128), rows] (the transpose of quant_e4m3's
+    (1, 128) scales, bit for bit). The FP8 block-scaled MoE GEMMs take this layout."""
+    dev = _require_cuda(x)
+    if x.dtype not in (torch.bfloat16, torch.float32) or x.dim() != 2:
+        raise RuntimeError("quant_e4m3_kmajor takes a 2-D bf16 or fp32 tensor")
+    _contig("x", x)
+    if _FP8 is None:
+        raise RuntimeError("this torch has no float8_e4m3fn")
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=_FP8, device=dev)
+    scales = torch.empty((-(-cols // 128), rows), dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        check(lib().ek_quant_e4m3_kmajor(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols,
+                                         q.data_ptr(), scales.data_ptr(), current_stream_handle(dev)),
+              "ek_quant_e4m3_kmajor")
+    return q, scales
+
+
+def moe_gather_cols_f32(perm: dict, src: torch.Tensor) -> torch.Tensor:
+    """[cols, max_rows] fp32: column c, row r = src[sorted_slots[r] // topk, c] (0 for
+    unused rows) - per-row values such as received group scales, gathered in the
+    permutation's order and transposed to the K-block-major layout."""
+    dev = _require_cuda(src)
+    if src.dtype != torch.float32 or src.dim() != 2:
+        raise RuntimeError("moe_gather_cols_f32 takes a 2-D fp32 tensor")
+    _contig("src", src)
+    rows, cols = perm["max_rows"], src.shape[1]
+    dst = torch.empty((cols, rows), dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_gather_cols_f32(perm["sorted_slots"].data_ptr(), perm["num_rows_padded"].data_ptr(), rows,
+                                           perm["T"] * perm["topk"], perm["topk"], src.data_ptr(), cols,
+                                           dst.data_ptr(), current_stream_handle(dev)), "ek_moe_gather_cols_f32")
+    return dst
+
+
 _SIZE_MAX = ctypes.c_size_t(-1).value
 _DEV_SMS: dict[int, int] = {}
 
@@ -353,37 +390,40 @@ def quant_moe_weights_fp8(w1: torch.Tensor, w2: torch.Tensor, w3: torch.Tensor) 
 
 
 def moe_gate_up_fp8bs(perm: dict, xq: torch.Tensor, xs: torch.Tensor, qw: dict, num_sms: int | None = None,
-                      tok_tile: int = 0) -> torch.Tensor:
-    """Block-scaled FP8 gate/up (SwiGLU) over the packed layout; bf16 act [rows, I]."""
+                      tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+    """Block-scaled FP8 gate/up (SwiGLU) over the packed layout; bf16 act [rows, I].
+    xs: K-block-major token scales [H/128, rows] (quant_e4m3_kmajor).
+    tok_tile 0 and pair -1 let the library choose (CTA pairs for tiles of 128/256)."""
     dev = _require_cuda(xq, xs)
     if perm["block_m"] != 1:
         raise RuntimeError("the FP8 block-scaled GEMMs take the packed layout (block_m=1)")
     rows, E, H, I = perm["max_rows"], qw["E"], qw["H"], qw["I"]
-    if xq.shape != (rows, H) or xs.shape != (rows, H // 128):
+    if xq.shape != (rows, H) or xs.shape != (H // 128, rows):
         raise RuntimeError("gate_up_fp8bs: activation shape mismatch")
     act = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
     with _on_device(dev):
         check(lib().ek_moe_gate_up_fp8bs(xq.data_ptr(), xs.data_ptr(), qw["w1q"].data_ptr(), qw["w3q"].data_ptr(),
                                          qw["w1s"].data_ptr(), qw["w3s"].data_ptr(), perm["expert_counts"].data_ptr(),
-                                         act.data_ptr(), rows, E, H, I, int(tok_tile), int(num_sms or 0),
+                                         act.data_ptr(), rows, E, H, I, int(tok_tile), int(pair), int(num_sms or 0),
                                          current_stream_handle(dev)), "ek_moe_gate_up_fp8bs")
     return act
 
 
 def moe_down_fp8bs(perm: dict, aq: torch.Tensor, as_: torch.Tensor, qw: dict, topk_weights: torch.Tensor,
-                   num_sms: int | None = None, tok_tile: int = 0) -> torch.Tensor:
-    """Block-scaled FP8 down projection with the routing weight, scattered to slots (bf16 [T*k, H])."""
+                   num_sms: int | None = None, tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+    """Block-scaled FP8 down projection with the routing weight, scattered to slots (bf16 [T*k, H]).
+    as_: K-block-major act scales [I/128, rows]."""
     dev = _require_cuda(aq, as_, topk_weights)
     rows, E, H, I = perm["max_rows"], qw["E"], qw["H"], qw["I"]
     T, k = perm["T"], perm["topk"]
-    if aq.shape != (rows, I) or as_.shape != (rows, I // 128) or topk_weights.numel() != T * k:
+    if aq.shape != (rows, I) or as_.shape != (I // 128, rows) or topk_weights.numel() != T * k:
         raise RuntimeError("down_fp8bs: shape mismatch")
     y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
     with _on_device(dev):
         check(lib().ek_moe_down_fp8bs(aq.data_ptr(), as_.data_ptr(), qw["w2q"].data_ptr(), qw["w2s"].data_ptr(),
                                       perm["expert_counts"].data_ptr(), perm["sorted_slots"].data_ptr(),
                                       topk_weights.data_ptr(), y.data_ptr(), rows, E, H, I, T, k, int(tok_tile),
-                                      int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_fp8bs")
+                                      int(pair), int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_fp8bs")
     return y
 
 
@@ -399,9 +439,9 @@ def fused_moe_fp8(hidden_states: torch.Tensor, gate_logits: torch.Tensor, qw: di
         return out if out is not None else torch.empty_like(hidden_states)
     ids, wts = moe_route(gate_logits, topk)
     perm = moe_permute(ids, qw["E"], x=hidden_states, block_m=1)
-    xq, xs = quant_e4m3(perm["x_perm"], block=(1, 128))
+    xq, xs = quant_e4m3_kmajor(perm["x_perm"])
     act = moe_gate_up_fp8bs(perm, xq, xs, qw, num_sms=num_sms)
-    aq, as_ = quant_e4m3(act, block=(1, 128))
+    aq, as_ = quant_e4m3_kmajor(act)
     y = moe_down_fp8bs(perm, aq, as_, qw, wts, num_sms=num_sms)
     return moe_combine(y, T, topk, out=out)
 

@@ -36,13 +36,37 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, 
     if (rc) return rc;
     attr_done[dev] = true;
   }
-  gemm_fp8bs_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tx, P);
-  return check_cuda(cudaGetLastError(), "fp8 block-scaled launch");
+  if constexpr (Cfg::kPair) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_fp8bs_kernel<Cfg>, ta, tb, tx, P), "fp8 block-scaled pair launch");
+  } else {
+    gemm_fp8bs_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tx, P);
+    return check_cuda(cudaGetLastError(), "fp8 block-scaled launch");
+  }
 }
 
 template <int kEpi>
-int launch_tok(int tok, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, const Fp8BsParams& P,
-               int grid, cudaStream_t s) {
+int launch_tok(int tok, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx,
+               const Fp8BsParams& P, int grid, cudaStream_t s) {
+  if (pair) {
+    switch (tok) {
+      case 128: return launch<Fp8BsCfg<128, kEpi, true>>(ta, tb, tx, P, grid, s);
+      case 192: return launch<Fp8BsCfg<192, kEpi, true>>(ta, tb, tx, P, grid, s);
+      case 256: return launch<Fp8BsCfg<256, kEpi, true>>(ta, tb, tx, P, grid, s);
+    }
+    return set_error(EK_ERR_INVALID, "fp8 block-scaled pair token tile must be 128, 192 or 256 (got %d)", tok);
+  }
   switch (tok) {
     case 16: return launch<Fp8BsCfg<16, kEpi>>(ta, tb, tx, P, grid, s);
     case 32: return launch<Fp8BsCfg<32, kEpi>>(ta, tb, tx, P, grid, s);
@@ -52,15 +76,30 @@ int launch_tok(int tok, const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   return set_error(EK_ERR_INVALID, "fp8 block-scaled token tile must be 16, 32, 64 or 128 (got %d)", tok);
 }
 
-// Token tile sized for the busiest expert (mean + 3 sigma), at most 128.
-int tok_tile(long long rows, int E, int force) {
-  if (force > 0) return force;
+// Token tile sized for the busiest expert (mean + 3 sigma of a uniform
+// routing's per-expert count), since an expert's weight tile is streamed once
+// per token tile, and the CTA-pair choice: above 64 tokens the tile runs on a
+// CTA pair (128, 192 or 256 tokens; each SM streams half of the token rows),
+// below on one CTA (16 .. 128, powers of two). `pair_ok` is false where the
+// weight rows do not divide into pair tiles.
+void tiles(long long rows, int E, int S, int force_tok, int force_pair, bool pair_ok, int* tok, int* pair) {
   const double used = (double)std::max<long long>(1, std::min<long long>(E, rows));
   const double avg = (double)rows / used;
   const double want = avg + 3.0 * std::sqrt(avg) + 1.0;
-  int t = 16;
-  while (t < want && t < 128) t *= 2;
-  return t;
+  int pr = force_pair >= 0 ? force_pair : (want > 64 ? 1 : 0);
+  if (!pair_ok || S < 2) pr = 0;
+  int t = force_tok;
+  if (t <= 0) {
+    if (pr) {
+      t = want <= 128 ? 128 : want <= 192 ? 192 : 256;
+    } else {
+      t = 16;
+      while (t < want && t < 128) t *= 2;
+    }
+  }
+  if (!pr && t > 128) t = 128;
+  *tok = t;
+  *pair = pr;
 }
 
 }  // namespace
@@ -72,7 +111,7 @@ extern "C" {
 
 int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, const void* w3q,
                          const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
-                         int E, int H, int I, int tok, int num_sms, void* stream) {
+                         int E, int H, int I, int tok, int pair, int num_sms, void* stream) {
   clear_error();
   if (!xq || !x_scale || !w1q || !w3q || !w1_scale || !w3_scale || !expert_counts || !act)
     return set_error(EK_ERR_INVALID, "gate_up_fp8bs: null pointer");
@@ -84,11 +123,13 @@ int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, 
   int S = 0;
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
-  const int t = tok_tile(rows, E, tok);
+  int t = 0, pr = 0;
+  tiles(rows, E, S, tok, pair, true, &t, &pr);
+  const int ctas = pr ? 2 : 1;
   CUtensorMap ta, tx, tb;
   if ((rc = make_tmap_2d(&ta, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
   if ((rc = make_tmap_2d(&tx, w3q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
-  if ((rc = make_tmap_2d(&tb, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, rows, H, 128, t))) return rc;
+  if ((rc = make_tmap_2d(&tb, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, rows, H, 128, t / ctas))) return rc;
   Fp8BsParams P{};
   P.g.M = rows;
   P.g.N = I;
@@ -99,17 +140,18 @@ int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, 
   P.g.num_experts = E;
   P.g.expert_counts = expert_counts;
   P.g.w_rows_per_expert = I;
-  P.g.feat_tiles = I / 64;
+  P.g.feat_tiles = I / (64 * ctas);
   P.x_scale = x_scale;
   P.w_scale = w1_scale;
   P.w_scale2 = w3_scale;
   P.ksb = H / 128;
-  return launch_tok<kEpiSwiGLUT>(t, ta, tb, tx, P, S, static_cast<cudaStream_t>(stream));
+  const int grid = std::max(1, S / ctas) * ctas;
+  return launch_tok<kEpiSwiGLUT>(t, pr != 0, ta, tb, tx, P, grid, static_cast<cudaStream_t>(stream));
 }
 
 int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
                       const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
-                      int E, int H, int I, int T, int topk, int tok, int num_sms, void* stream) {
+                      int E, int H, int I, int T, int topk, int tok, int pair, int num_sms, void* stream) {
   clear_error();
   if (!aq || !a_scale || !w2q || !w2_scale || !expert_counts || !sorted_slots || !topk_weights || !y)
     return set_error(EK_ERR_INVALID, "down_fp8bs: null pointer");
@@ -121,10 +163,13 @@ int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, con
   int S = 0;
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
-  const int t = tok_tile(rows, E, tok);
+  // a pair tile covers 256 output features, so H must divide into them
+  int t = 0, pr = 0;
+  tiles(rows, E, S, tok, pair, H % 256 == 0, &t, &pr);
+  const int ctas = pr ? 2 : 1;
   CUtensorMap ta, tb;
   if ((rc = make_tmap_2d(&ta, w2q, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, (uint64_t)E * H, I, 128, 128))) return rc;
-  if ((rc = make_tmap_2d(&tb, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, rows, I, 128, t))) return rc;
+  if ((rc = make_tmap_2d(&tb, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, rows, I, 128, t / ctas))) return rc;
   Fp8BsParams P{};
   P.g.M = rows;
   P.g.N = H;
@@ -135,7 +180,7 @@ int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, con
   P.g.num_experts = E;
   P.g.expert_counts = expert_counts;
   P.g.w_rows_per_expert = H;
-  P.g.feat_tiles = H / 128;
+  P.g.feat_tiles = H / (128 * ctas);
   P.g.sorted_slots = sorted_slots;
   P.g.slot_weights = topk_weights;
   P.g.num_slots = T * topk;
@@ -143,7 +188,8 @@ int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, con
   P.w_scale = w2_scale;
   P.w_scale2 = w2_scale;
   P.ksb = I / 128;
-  return launch_tok<kEpiScatterT>(t, ta, tb, ta, P, S, static_cast<cudaStream_t>(stream));
+  const int grid = std::max(1, S / ctas) * ctas;
+  return launch_tok<kEpiScatterT>(t, pr != 0, ta, tb, ta, P, grid, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

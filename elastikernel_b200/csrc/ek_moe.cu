@@ -226,6 +226,26 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Transposing gather of per-row fp32 values (e.g. 1 x 128 group scales):
+// dst[c][r] = src[sorted_slots[r] / topk][c], 0 for unused rows; consecutive
+// threads take consecutive rows, so the stores are coalesced.
+__global__ void gather_cols_kernel(const int* __restrict__ sorted_slots, const int* __restrict__ num_rows_padded,
+                                   int max_rows, int n_slots, int topk, const float* __restrict__ src, int cols,
+                                   float* __restrict__ dst) {
+  const int rows = min(*num_rows_padded, max_rows);
+  const long long total = (long long)cols * max_rows;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i / max_rows), r = (int)(i - (long long)c * max_rows);
+    float v = 0.f;
+    if (r < rows) {
+      const int s = sorted_slots[r];
+      if (s >= 0 && s < n_slots) v = __ldg(src + (size_t)(s / topk) * cols + c);
+    }
+    dst[i] = v;
+  }
+}
+
 // ------------------------------------------------------------------ combine
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ out, int T, int k,
                                int H) {
@@ -611,6 +631,19 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (pr) return launch_packed_tok<kEpiScatterT, true>(tok, ta, tb, ta, p, grid, s);
   return launch_packed_tok<kEpiScatterT, false>(tok, ta, tb, ta, p, grid, s);
+}
+
+int ek_moe_gather_cols_f32(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
+                           const float* src, int cols, float* dst, void* stream) {
+  clear_error();
+  if (!sorted_slots || !num_rows_padded || !src || !dst || max_rows < 0 || n_slots < 0 || topk < 1 || cols <= 0)
+    return set_error(EK_ERR_INVALID, "gather_cols_f32: bad arguments");
+  if (max_rows == 0) return EK_OK;
+  const long long total = (long long)cols * max_rows;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  gather_cols_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(sorted_slots, num_rows_padded, max_rows,
+                                                                            n_slots, topk, src, cols, dst);
+  return check_cuda(cudaGetLastError(), "column gather launch");
 }
 
 int ek_moe_gather_rows(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,

@@ -140,9 +140,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
 }
-// Arrive (release, cluster scope) on an mbarrier given by a shared::cluster address.
+// Arrive on an mbarrier given by a shared::cluster address (possibly the
+// peer's). Default semantics (release at CTA scope): the arrivals only hand a
+// TMEM buffer back to the pair's MMA issuer after this thread's tcgen05.ld
+// have completed (tcgen05.wait::ld + tcgen05.fence::before_thread_sync), and
+// TMEM is not ordered by a memory fence, so a cluster-scope release fence on
+// every arrival would only add latency.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -329,5 +334,44 @@ __device__ __forceinline__ int named_bar_red_or(int id, int nthreads, int pred) 
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// acc = a * b + acc on two packed fp32 lanes (one fused multiply-add each,
+// round to nearest even, as the scalar fma).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 acc) {
+  uint64_t ua = *reinterpret_cast<uint64_t*>(&a), ub = *reinterpret_cast<uint64_t*>(&b);
+  uint64_t uc = *reinterpret_cast<uint64_t*>(&acc);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(uc) : "l"(ua), "l"(ub));
+  return *reinterpret_cast<float2*>(&uc);
+}
+
+// a * b on two packed fp32 lanes (round to nearest even).
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t ua = *reinterpret_cast<uint64_t*>(&a), ub = *reinterpret_cast<uint64_t*>(&b), uc;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(uc) : "l"(ua), "l"(ub));
+  return *reinterpret_cast<float2*>(&uc);
+}
+
+// Per-thread asynchronous 4-byte global -> shared copy (no register is held
+// while it is in flight); completion is tracked per thread in commit groups.
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+// As cp_async_4, reading src_bytes (0 or 4) and zero-filling the rest.
+__device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gmem_src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` once all of this thread's earlier cp.async copies have
+// landed (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's most recent commit groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 }  // namespace ek

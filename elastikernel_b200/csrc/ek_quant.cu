@@ -83,31 +83,47 @@ __global__ void quant_blocks_kernel(const void* __restrict__ x, int dt, int rows
   if (threadIdx.x == 0) scales[blockIdx.x] = s;
 }
 
-// 1 x 128 blocks: one warp per 128-column group of a row (activations)
+// 1 x 128 blocks: one warp per 128-column group of a row (activations); each
+// lane owns 4 consecutive elements (one vector load, one 4-byte store) when
+// the row length is a multiple of 4. Scales go to scales[row][group], or
+// K-block-major to scales[group][row] when kmajor is set.
 __global__ void quant_groups_kernel(const void* __restrict__ x, int dt, int rows, int cols, uint8_t* __restrict__ q,
-                                    float* __restrict__ scales) {
+                                    float* __restrict__ scales, int kmajor) {
   const int groups = (cols + 127) / 128;
   const long long gid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gid >= (long long)rows * groups) return;
   const int row = (int)(gid / groups), g = (int)(gid % groups);
   const size_t base = (size_t)row * cols;
+  const int c0 = g * 128 + lane * 4;
   float v[4];
-  float amax = 0.f;
+  if ((cols & 3) == 0 && c0 + 3 < cols) {
+    if (dt == 0) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(x) + base + c0);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + base + c0);
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    }
+  } else {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = g * 128 + i * 32 + lane;
-    v[i] = c < cols ? load_f(x, dt, base + c) : 0.f;
-    amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < 4; ++i) v[i] = (c0 + i < cols) ? load_f(x, dt, base + c0 + i) : 0.f;
   }
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   amax = warp_max(amax);
   const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  if ((cols & 3) == 0 && c0 + 3 < cols) {
+    const uint32_t packed = (uint32_t)to_e4m3(v[0] / s) | ((uint32_t)to_e4m3(v[1] / s) << 8) |
+                            ((uint32_t)to_e4m3(v[2] / s) << 16) | ((uint32_t)to_e4m3(v[3] / s) << 24);
+    *reinterpret_cast<uint32_t*>(q + base + c0) = packed;
+  } else {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = g * 128 + i * 32 + lane;
-    if (c < cols) q[base + c] = to_e4m3(v[i] / s);
+    for (int i = 0; i < 4; ++i)
+      if (c0 + i < cols) q[base + c0 + i] = to_e4m3(v[i] / s);
   }
-  if (lane == 0) scales[gid] = s;
+  if (lane == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)gid] = s;
 }
 
 }  // namespace
@@ -132,7 +148,7 @@ int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows
   } else if (br == 1 && bc == 128) {
     const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
     quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
-                                                                        static_cast<uint8_t*>(q), scales);
+                                                                        static_cast<uint8_t*>(q), scales, 0);
   } else if (br >= 1 && bc >= 1) {
     const long long blocks = (long long)((rows + br - 1) / br) * ((cols + bc - 1) / bc);
     if (blocks > 0x7fffffffLL) return set_error(EK_ERR_INVALID, "quant: too many blocks");
@@ -142,6 +158,17 @@ int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows
     return set_error(EK_ERR_INVALID, "quant: bad block shape %d x %d", br, bc);
   }
   return check_cuda(cudaGetLastError(), "quant launch");
+}
+
+int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q, float* scales_t, void* stream) {
+  clear_error();
+  if (!x || !q || !scales_t || rows < 0 || cols <= 0 || (x_dtype != 0 && x_dtype != 3))
+    return set_error(EK_ERR_INVALID, "quant_kmajor: bad arguments (x_dtype 0 = bf16, 3 = fp32)");
+  if (rows == 0) return EK_OK;
+  const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
+  quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1);
+  return check_cuda(cudaGetLastError(), "quant_kmajor launch");
 }
 
 }  // extern "C"

@@ -133,9 +133,9 @@ class CudaEPOps:
         if R == 0:
             return torch.empty((0, qw["H"]), dtype=torch.bfloat16, device=xq_recv.device)
         perm = _ops.moe_permute(local_ids.view(R, 1), qw["E"], x=xq_recv, block_m=1)
-        xs = self.gather_rows(perm, xs_recv)
+        xs = _ops.moe_gather_cols_f32(perm, xs_recv)  # K-block-major scales of the gathered rows
         act = _ops.moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=self.num_sms)
-        aq, as_ = _ops.quant_e4m3(act, block=(1, 128))
+        aq, as_ = _ops.quant_e4m3_kmajor(act)
         return _ops.moe_down_fp8bs(perm, aq, as_, qw, w_recv, num_sms=self.num_sms)
 
     def combine_rows(self, y_back, slot_row, T, topk):

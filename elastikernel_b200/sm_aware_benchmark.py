@@ -197,6 +197,35 @@ def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None, layout: st
     torch.cuda.synchronize()
 
 
+def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256) -> None:
+    """Run the DeepSeek-V3-shaped e4m3 block-scaled MoE layer (top-8, H=7168,
+    I=2048) with all `experts` on this GPU a few times (for profilers)."""
+    import torch
+
+    from . import _ops
+
+    dev = torch.device("cuda:0")
+    E, k, H, I = experts, 8, 7168, 2048
+    g = torch.Generator(device=dev).manual_seed(1000)
+    qs = []
+    for c0 in range(0, E, 32):
+        n = min(32, E - c0)
+        w1 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w3 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn((n, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        qs.append(_ops.quant_moe_weights_fp8(w1, w2, w3))
+        del w1, w2, w3
+    qw = {"E": E, "I": I, "H": H}
+    for key in ("w1q", "w1s", "w3q", "w3s", "w2q", "w2s"):
+        qw[key] = torch.cat([q[key] for q in qs], dim=0)
+    del qs
+    x = torch.randn((tokens, H), device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn((tokens, E), device=dev, generator=g)
+    for _ in range(reps):
+        _ops.fused_moe_fp8(x, logits, qw, k)
+    torch.cuda.synchronize()
+
+
 def main():
     parser = argparse.ArgumentParser(description="SM-Aware Kernel Benchmark")
     parser.add_argument("--gemm", action="store_true", help="Benchmark GEMM")
@@ -206,8 +235,12 @@ def main():
                         help="only run the Mixtral fused-MoE layer at this token count (for profiling)")
     parser.add_argument("--reps", type=int, default=5)
     parser.add_argument("--layout", choices=["packed", "padded"], default="packed")
+    parser.add_argument("--fp8-layer-tokens", type=int, default=0,
+                        help="only run the DeepSeek-V3-shaped e4m3 MoE layer at this token count (for profiling)")
     args = parser.parse_args()
-    if args.layer_tokens > 0:
+    if args.fp8_layer_tokens > 0:
+        run_layer_fp8(args.fp8_layer_tokens, args.reps)
+    elif args.layer_tokens > 0:
         run_layer(args.layer_tokens, args.reps, layout=args.layout)
     elif args.all:
         run_gemm_benchmark()

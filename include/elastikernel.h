@@ -150,6 +150,11 @@ int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float*
  *   otherwise                       : per block_rows x block_cols block,
  *                                     scales[ceil(rows/br)][ceil(cols/bc)].
  * No counterpart in the reference (it has no FP8 path). */
+/* As ek_quant_e4m3 with 1 x 128 groups, the scales written K-block-major:
+ * scales_t[g][r] ([ceil(cols/128)][rows]), the layout the FP8 block-scaled
+ * grouped GEMMs read token scales in. No counterpart in the reference. */
+int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q, float* scales_t, void* stream);
+
 int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, void* q,
                   float* scales, void* stream);
 
@@ -234,22 +239,33 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
 
 /* FP8 e4m3 packed grouped GEMMs with DeepSeek-style scales: weights with
  * 128 x 128 fp32 block scales (w*_scale [E*rows/128][K/128]), tokens with
- * 1 x 128 fp32 group scales (x_scale / a_scale [rows][K/128]); fp32
+ * 1 x 128 fp32 group scales stored K-block-major (x_scale / a_scale
+ * [K/128][rows], as ek_quant_e4m3_kmajor writes them); fp32
  * accumulation with the scales applied per 128-wide K block; bf16 outputs as
  * ek_moe_gate_up_packed / ek_moe_down_packed. H and I must be multiples of
- * 128; tok = token tile (16/32/64/128, 0 = choose). No counterpart in the
- * reference (it has no FP8 path). */
+ * 128; tok = token tile (16/32/64/128 on one CTA, 128/192/256 on a CTA pair;
+ * 0 = choose), pair = 1 for the CTA-pair (2-SM MMA) kernel, 0 for one CTA,
+ * -1 = choose (the down projection runs a pair only when H % 256 == 0).
+ * No counterpart in the reference (it has no FP8 path). */
 int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, const void* w3q,
                          const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
-                         int E, int H, int I, int tok, int num_sms, void* stream);
+                         int E, int H, int I, int tok, int pair, int num_sms, void* stream);
 int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
                       const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
-                      int E, int H, int I, int T, int topk, int tok, int num_sms, void* stream);
+                      int E, int H, int I, int T, int topk, int tok, int pair, int num_sms, void* stream);
 
 /* Row gather of the padded/packed layout: dst[r] = src[sorted_slots[r] / topk]
  * for the used rows r < *num_rows_padded with a valid slot (row_bytes a
  * multiple of 16). Used to gather rows of a second tensor (e.g. FP8 scales)
  * with a permutation ek_moe_permute already made. */
+/* Transposing gather of per-row fp32 values in the same permutation:
+ * dst[c][r] = src[sorted_slots[r] / topk][c] for c < cols, r < max_rows
+ * (0 for unused rows); turns received [rows][K/128] group scales into the
+ * K-block-major layout of the FP8 block-scaled GEMMs. No counterpart in the
+ * reference. */
+int ek_moe_gather_cols_f32(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
+                           const float* src, int cols, float* dst, void* stream);
+
 int ek_moe_gather_rows(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
                        const void* src, int row_bytes, void* dst, void* stream);
 

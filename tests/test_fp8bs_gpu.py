@@ -51,25 +51,50 @@ def test_weight_block_quant_matches_oracle(cuda_dev):
     assert torch.equal(qw["w1q"].cpu().view(torch.uint8).reshape(512, 384), rq.view(torch.uint8))
 
 
-@pytest.mark.parametrize("tok", [16, 32, 64, 128])
-def test_fp8bs_gemms_token_tiles(cuda_dev, tok):
+def test_kmajor_quant_and_scale_gather(cuda_dev):
+    """K-block-major group scales are the transpose of the row-major ones, bit
+    for bit, and the transposing gather reorders them like the row gather."""
     from elastikernel_b200 import _ops
 
-    T, H, I, E, k = 300, 512, 256, 16, 4
-    x, logits, qw = _setup(T, H, I, E, seed=tok, dev=cuda_dev)
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn((333, 640), generator=g) * 3).to(torch.bfloat16).to(cuda_dev)
+    q0, s0 = _ops.quant_e4m3(x, block=(1, 128))
+    q1, s1 = _ops.quant_e4m3_kmajor(x)
+    assert torch.equal(q0.view(torch.uint8), q1.view(torch.uint8))
+    assert torch.equal(s0.t().contiguous(), s1)
+    ids, _ = _ops.moe_route(torch.randn((333, 8), generator=g).to(cuda_dev), 2)
+    perm = _ops.moe_permute(ids, 8, x=x, block_m=1)
+    st = _ops.moe_gather_cols_f32(perm, s0)
+    slots = perm["sorted_slots"].cpu()
+    ref = torch.zeros_like(st.cpu())
+    used = slots >= 0
+    ref[:, used] = s0.cpu()[slots[used] // 2].t()
+    assert torch.equal(st.cpu(), ref)
+
+
+@pytest.mark.parametrize("tok,pair,E", [(16, 0, 16), (32, 0, 16), (64, 0, 16), (128, 0, 16), (128, 0, 4),
+                                        (128, 1, 16), (128, 1, 4), (192, 1, 16), (192, 1, 4), (256, 1, 16),
+                                        (256, 1, 4)])
+def test_fp8bs_gemms_token_tiles(cuda_dev, tok, pair, E):
+    """Every token tile on one CTA and on a CTA pair; E=4 puts ~300 tokens on
+    each expert so every expert spans several token tiles."""
+    from elastikernel_b200 import _ops
+
+    T, H, I, k = 300, 512, 256, 4
+    x, logits, qw = _setup(T, H, I, E, seed=tok + pair, dev=cuda_dev)
     ids, wts = _ops.moe_route(logits.to(cuda_dev), k)
     perm = _ops.moe_permute(ids, E, x=x.to(cuda_dev), block_m=1)
-    xq, xs = _ops.quant_e4m3(perm["x_perm"], block=(1, 128))
-    act = _ops.moe_gate_up_fp8bs(perm, xq, xs, qw, tok_tile=tok)
-    aq, as_ = _ops.quant_e4m3(act, block=(1, 128))
-    y = _ops.moe_down_fp8bs(perm, aq, as_, qw, wts, tok_tile=tok)
+    xq, xs = _ops.quant_e4m3_kmajor(perm["x_perm"])
+    act = _ops.moe_gate_up_fp8bs(perm, xq, xs, qw, tok_tile=tok, pair=pair)
+    aq, as_ = _ops.quant_e4m3_kmajor(act)
+    y = _ops.moe_down_fp8bs(perm, aq, as_, qw, wts, tok_tile=tok, pair=pair)
     out = _ops.moe_combine(y, T, k)
     torch.cuda.synchronize()
     w1, w2, w3 = _dequant_weights(qw)
     xd = of8.dequant_blocks(*of8.quant_blocks(x, 1, 128), 1, 128)  # tokens quantised the same way
     ref = om.moe_ref(xd, logits, w1, w2, w3, k)
     err = og.max_rel_err(out, ref)
-    assert err <= TOL_FP8, f"tok={tok}: {err:.3e}"
+    assert err <= TOL_FP8, f"tok={tok} pair={pair} E={E}: {err:.3e}"
 
 
 @pytest.mark.parametrize("T", [64, 512])
