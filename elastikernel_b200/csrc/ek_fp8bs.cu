@@ -91,7 +91,9 @@ void tiles(long long rows, int E, int S, int force_tok, int force_pair, bool pai
   int t = force_tok;
   if (t <= 0) {
     if (pr) {
-      t = want <= 128 ? 128 : want <= 192 ? 192 : 256;
+      // 256-token pair tiles need 16 epilogue warps and run short of registers:
+      // a busier expert takes several 192-token tiles instead
+      t = want <= 128 ? 128 : 192;
     } else {
       t = 16;
       while (t < want && t < 128) t *= 2;

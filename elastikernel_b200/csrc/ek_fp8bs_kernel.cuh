@@ -24,8 +24,8 @@
 // runs once per unit and misses the instruction cache.
 //
 // Modes:
-//   single  one CTA: 128 weight rows x up to 128 tokens, 4 epilogue warps
-//           (one thread per weight row, all token columns)
+//   single  one CTA: 128 weight rows x up to 128 tokens; 4 epilogue warps
+//           (one thread per weight row, all token columns), 8 from 64 tokens
 //   pair    a CTA pair (2-SM MMA): 256 weight rows x up to 128 / 192 / 256
 //           tokens; each CTA loads its 128 weight rows and half of the
 //           tokens, so one SM streams 28 KB per K step for a 128 x 192 x 128
@@ -68,7 +68,7 @@ struct Fp8BsCfg {
   static constexpr int TMEM_COLS = (NBUF * BN <= 32) ? 32 : (NBUF * BN <= 64) ? 64 : (NBUF * BN <= 128) ? 128
                                  : (NBUF * BN <= 256) ? 256 : 512;
   // pair: 8 epilogue warps, 16 for the 256-token tile (64 accumulators per thread)
-  static constexpr int EPI_WARPS = kPair ? (BN == 256 ? 16 : 8) : 4;
+  static constexpr int EPI_WARPS = kPair ? (BN == 256 ? 16 : 8) : (BN >= 64 ? 8 : 4);
   static constexpr int EPI_THREADS = EPI_WARPS * 32;
   static constexpr int COL_GROUPS = EPI_WARPS / 4;   // epilogue warps per TMEM lane quarter
   static constexpr int CPT = BN / COL_GROUPS;        // token columns per epilogue thread
@@ -77,10 +77,12 @@ struct Fp8BsCfg {
   static constexpr int CHUNK = CPT < 32 ? CPT : (kPair ? 16 : 32);
   static constexpr int THREADS = 96 + EPI_THREADS;
   static constexpr int SCALE_SLOTS = 8;       // K blocks of scales in flight ahead of the epilogue
+  static constexpr int PREFETCH = 16;         // K blocks of weight tiles prefetched into L2 ahead of the loads
   static constexpr int SCALE_STRIDE = BN + 4;  // slot: BN token scales, 2 weight-block scales
   static constexpr int STAGE_STRIDE = 128 + 4; // staging row: one token column of 128 weight rows
+  static constexpr int STAGE_COLS = CHUNK < 16 ? CHUNK : 16;  // token columns staged per pass
   // expert tables, slots + weights, per-column-group staging, scale ring
-  static constexpr int EXTRA_BYTES = (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + COL_GROUPS * CHUNK * STAGE_STRIDE * 4 +
+  static constexpr int EXTRA_BYTES = (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + COL_GROUPS * STAGE_COLS * STAGE_STRIDE * 4 +
                                       SCALE_SLOTS * SCALE_STRIDE * 4 + 127) / 128 * 128;
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
@@ -105,17 +107,17 @@ struct Fp8BsParams {
 // column tt0) of a SwiGLU unit: act[tok0 + tt0 + t][c_col + f] =
 // silu(gate f) * up f for the 64 features of this CTA (rows f and 64 + f).
 // A warp writes one token row per pass, two features per lane (4-byte stores).
+// Scalars only: a struct passed by reference would live in local memory.
 __device__ __noinline__ void fp8bs_store_swiglu(const float* stage, int tt0, int nt, int tok0, int c_col,
-                                                const GemmParams& p, int cg_tid) {
+                                                __nv_bfloat16* out, int ldc, int N, int cg_tid) {
   constexpr int SR = 128 + 4;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C);
   for (int i = cg_tid; i < nt * 32; i += 128) {
     const int t = i >> 5, f = (i & 31) * 2;
-    if (c_col + f >= p.N) continue;
+    if (c_col + f >= N) continue;
     const float2 g = *reinterpret_cast<const float2*>(stage + t * SR + f);
     const float2 up = *reinterpret_cast<const float2*>(stage + t * SR + 64 + f);
     const __nv_bfloat162 v = __floats2bfloat162_rn(silu_f(g.x) * up.x, silu_f(g.y) * up.y);
-    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)(tok0 + tt0 + t) * p.ldc + c_col + f) = v;
+    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)(tok0 + tt0 + t) * ldc + c_col + f) = v;
   }
 }
 
@@ -123,13 +125,13 @@ __device__ __noinline__ void fp8bs_store_swiglu(const float* stage, int tt0, int
 // weight(t) * acc for the 128 output features of this CTA, four per lane
 // (8-byte stores); columns without a slot are skipped.
 __device__ __noinline__ void fp8bs_store_scatter(const float* stage, int tt0, int nt, const int* s_slot,
-                                                 const float* s_wt, int c_col, const GemmParams& p, int cg_tid) {
+                                                 const float* s_wt, int c_col, __nv_bfloat16* out, int ldc, int N,
+                                                 int cg_tid) {
   constexpr int SR = 128 + 4;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C);
   for (int i = cg_tid; i < nt * 32; i += 128) {
     const int t = i >> 5, f = (i & 31) * 4;
     const int slot = s_slot[tt0 + t];
-    if (slot < 0 || c_col + f >= p.N) continue;
+    if (slot < 0 || c_col + f >= N) continue;
     const float wt = s_wt[tt0 + t];
     const float4 v = *reinterpret_cast<const float4*>(stage + t * SR + f);
     __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * wt, v.y * wt);
@@ -137,7 +139,7 @@ __device__ __noinline__ void fp8bs_store_scatter(const float* stage, int tt0, in
     uint2 pk;
     pk.x = *reinterpret_cast<uint32_t*>(&lo);
     pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(out + (size_t)slot * p.ldc + c_col + f) = pk;
+    *reinterpret_cast<uint2*>(out + (size_t)slot * ldc + c_col + f) = pk;
   }
 }
 
@@ -164,8 +166,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(sempty_bar + Cfg::SCALE_SLOTS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem_base + 1);
   // 16-byte aligned regions first (vector loads), then the tables
-  float* s_stage = reinterpret_cast<float*>(sX);                        // [COL_GROUPS][CH][STAGE_STRIDE]
-  float* s_scale = s_stage + Cfg::COL_GROUPS * CH * Cfg::STAGE_STRIDE;  // [SCALE_SLOTS][SCALE_STRIDE]
+  float* s_stage = reinterpret_cast<float*>(sX);  // [COL_GROUPS][STAGE_COLS][STAGE_STRIDE]
+  float* s_scale = s_stage + Cfg::COL_GROUPS * Cfg::STAGE_COLS * Cfg::STAGE_STRIDE;  // [SCALE_SLOTS][SCALE_STRIDE]
   int* s_tables = reinterpret_cast<int*>(s_scale + Cfg::SCALE_SLOTS * Cfg::SCALE_STRIDE);
   ExpertTables xt{s_tables, s_tables + (kMaxExpertsT + 1)};
   int* s_slot = s_tables + 2 * (kMaxExpertsT + 1);      // [BN]
@@ -225,10 +227,28 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // L2 prefetch cursor PREFETCH K blocks ahead of the loads: the weight
+      // tiles come from HBM, and a prefetch holds no shared memory, so the
+      // loads of the pipeline find them in L2.
+      int fu = unit0, fkb = 0;
+      Unit fw{};
+      if (fu < nunits) fw = decode_unit<Cfg>(p, fu, 0, rank, xt);
+      auto prefetch_next = [&]() {
+        if (fu >= nunits) return;
+        tma_prefetch_2d(&tmA, fkb * 128, fw.a_row);
+        if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_prefetch_2d(&tmX, fkb * 128, fw.a_row);
+        if (++fkb == KB) {
+          fkb = 0;
+          fu += unit_step;
+          if (fu < nunits) fw = decode_unit<Cfg>(p, fu, 0, rank, xt);
+        }
+      };
+      for (int i = 0; i < Cfg::PREFETCH; ++i) prefetch_next();
       for (int u = unit0; u < nunits && ok; u += unit_step) {
         const Unit w = decode_unit<Cfg>(p, u, 0, rank, xt);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) { ok = false; break; }
+          prefetch_next();
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
           if constexpr (Cfg::kPair) {
@@ -343,7 +363,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     const uint32_t kempty_leader0 = Cfg::kPair ? mapa_shared(smem_u32(&kempty_bar[0]), 0) : 0u;
     const int half = (Cfg::kEpi == kEpiSwiGLUT && row_in_tile >= 64) ? 1 : 0;
     constexpr int NS = Cfg::SCALE_SLOTS, RS = Cfg::SCALE_STRIDE, SR = Cfg::STAGE_STRIDE;
-    float* stage = s_stage + cg * CH * SR;
+    constexpr int SC = Cfg::STAGE_COLS;
+    float* stage = s_stage + cg * SC * SR;
+    __nv_bfloat16* out_bf16 = reinterpret_cast<__nv_bfloat16*>(p.C);
     int gkb = 0;
     for (int u = unit0; u < nunits; u += unit_step) {
       const Unit w = decode_unit<Cfg>(p, u, 0, rank, xt);
@@ -413,16 +435,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       // (stage[t][row], conflict-free) and store them with a compact loop.
       const int nvalid = min(w.n_eff, w.row_end - w.tok0);  // token columns with a row
 #pragma unroll
-      for (int c = 0; c < CPT / CH; ++c) {
+      for (int c = 0; c < CPT / SC; ++c) {
 #pragma unroll
-        for (int t = 0; t < CH; ++t)
-          stage[t * SR + row_in_tile] = ((c * CH + t) & 1) ? acc2[(c * CH + t) >> 1].y : acc2[(c * CH + t) >> 1].x;
+        for (int t = 0; t < SC; ++t)
+          stage[t * SR + row_in_tile] = ((c * SC + t) & 1) ? acc2[(c * SC + t) >> 1].y : acc2[(c * SC + t) >> 1].x;
         named_bar_sync(1, ET);
-        const int tt0 = (c * GC + cg) * CH;
+        // tile column of this thread's accumulator c * SC (SC columns, contiguous within a TMEM chunk)
+        const int tt0 = ((c * SC) / CH * GC + cg) * CH + (c * SC) % CH;
         if constexpr (Cfg::kEpi == kEpiSwiGLUT)
-          fp8bs_store_swiglu(stage, tt0, min(CH, nvalid - tt0), w.tok0, w.c_col, p, cg_tid);
+          fp8bs_store_swiglu(stage, tt0, min(SC, nvalid - tt0), w.tok0, w.c_col, out_bf16, p.ldc, p.N, cg_tid);
         else
-          fp8bs_store_scatter(stage, tt0, min(CH, nvalid - tt0), s_slot, s_wt, w.c_col, p, cg_tid);
+          fp8bs_store_scatter(stage, tt0, min(SC, nvalid - tt0), s_slot, s_wt, w.c_col, out_bf16, p.ldc, p.N,
+                              cg_tid);
         named_bar_sync(1, ET);  // the staging buffer (and s_slot / s_wt) are reused
       }
     }
