@@ -429,18 +429,21 @@ def moe_down_fp8bs(perm: dict, aq: torch.Tensor, as_: torch.Tensor, qw: dict, to
 
 def fused_moe_fp8(hidden_states: torch.Tensor, gate_logits: torch.Tensor, qw: dict, topk: int,
                   out: torch.Tensor | None = None, num_sms: int | None = None) -> torch.Tensor:
-    """MoE layer with e4m3 block-scaled experts: route -> permute(+gather) ->
-    quantise rows (1 x 128 groups) -> FP8 gate/up SwiGLU -> quantise act ->
-    FP8 down (+weight) -> combine."""
+    """MoE layer with e4m3 block-scaled experts: route -> quantise the token
+    rows (1 x 128 groups; a group lies in one row, so quantising before the
+    permutation gives the same codes and scales) -> permute + gather the e4m3
+    rows (half the bytes of bf16) and their scales (K-block-major) -> FP8
+    gate/up SwiGLU -> quantise act -> FP8 down (+weight) -> combine."""
     _require_cuda(hidden_states, gate_logits, out)
     _check_bf16("hidden_states", hidden_states)
     T = hidden_states.shape[0]
     if T == 0:
         return out if out is not None else torch.empty_like(hidden_states)
     ids, wts = moe_route(gate_logits, topk)
-    perm = moe_permute(ids, qw["E"], x=hidden_states, block_m=1)
-    xq, xs = quant_e4m3_kmajor(perm["x_perm"])
-    act = moe_gate_up_fp8bs(perm, xq, xs, qw, num_sms=num_sms)
+    xq_tok, xs_tok = quant_e4m3(hidden_states, block=(1, 128))
+    perm = moe_permute(ids, qw["E"], x=xq_tok, block_m=1)
+    xs = moe_gather_cols_f32(perm, xs_tok)
+    act = moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=num_sms)
     aq, as_ = quant_e4m3_kmajor(act)
     y = moe_down_fp8bs(perm, aq, as_, qw, wts, num_sms=num_sms)
     return moe_combine(y, T, topk, out=out)

@@ -251,6 +251,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           prefetch_next();
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
+          // one box of BN_CTA token rows: splitting it into boxes of the rows a
+          // unit uses saves L2 traffic but measured slower (more TMA boxes per K block)
           if constexpr (Cfg::kPair) {
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
             const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
