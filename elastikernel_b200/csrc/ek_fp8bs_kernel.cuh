@@ -107,10 +107,12 @@ struct Fp8BsParams {
 // column tt0) of a SwiGLU unit: act[tok0 + tt0 + t][c_col + f] =
 // silu(gate f) * up f for the 64 features of this CTA (rows f and 64 + f).
 // A warp writes one token row per pass, two features per lane (4-byte stores).
-// Scalars only: a struct passed by reference would live in local memory.
-__device__ __noinline__ void fp8bs_store_swiglu(const float* stage, int tt0, int nt, int tok0, int c_col,
+// Inlined with a rolled loop: a call would save the caller's live
+// accumulators to local memory around it.
+__device__ __forceinline__ void fp8bs_store_swiglu(const float* stage, int tt0, int nt, int tok0, int c_col,
                                                 __nv_bfloat16* out, int ldc, int N, int cg_tid) {
   constexpr int SR = 128 + 4;
+#pragma unroll 1
   for (int i = cg_tid; i < nt * 32; i += 128) {
     const int t = i >> 5, f = (i & 31) * 2;
     if (c_col + f >= N) continue;
@@ -124,10 +126,11 @@ __device__ __noinline__ void fp8bs_store_swiglu(const float* stage, int tt0, int
 // One staged chunk of a down-projection unit: y[slot(t)][c_col + f] =
 // weight(t) * acc for the 128 output features of this CTA, four per lane
 // (8-byte stores); columns without a slot are skipped.
-__device__ __noinline__ void fp8bs_store_scatter(const float* stage, int tt0, int nt, const int* s_slot,
+__device__ __forceinline__ void fp8bs_store_scatter(const float* stage, int tt0, int nt, const int* s_slot,
                                                  const float* s_wt, int c_col, __nv_bfloat16* out, int ldc, int N,
                                                  int cg_tid) {
   constexpr int SR = 128 + 4;
+#pragma unroll 1
   for (int i = cg_tid; i < nt * 32; i += 128) {
     const int t = i >> 5, f = (i & 31) * 4;
     const int slot = s_slot[tt0 + t];

@@ -40,7 +40,12 @@ struct Machine {
   double feed_bytes_clk = 64;    // operand bytes per clock one SM sustains from L2 with all SMs loading
   double hbm_gbs = 6500;         // device HBM bandwidth
   double hbm_per_sm_gbs = 80;    // bandwidth one SM can draw
-  double part_gbs_per_sm = 200;  // split partials: written and read back through L2
+  // Split-K: every slice writes its fp32 part, the last one reads the other
+  // slices' parts back with its 4 epilogue warps, latency-bound at about
+  // this rate per SM (measured: a 2-way split of the tail wave of 256x256
+  // tiles at 4096^3 costs ~10 us and saves ~12 us).
+  double red_gbs_per_sm = 45;
+  double red_fixed_us = 2.5;     // partial stores drained, ticket, barriers
   double launch_us = 2.0;        // fixed launch + prologue cost
 };
 
@@ -88,9 +93,9 @@ Candidate evaluate(int M, int N, int K, int S, int dtype, int pair, int bn, int 
     t += 128.0 * bn * 4 / (mc.feed_bytes_clk * mc.clk_ghz * 1e3);
     const int grid = grid_tiles * ctas;
     if (s > 1) {
-      // partial tiles: written once, read back once by the reducing slice
-      const double part_bytes = double(R) * s * tile_m * bn * 4.0 * 2.0;
-      t += part_bytes / (std::max(1, grid) * mc.part_gbs_per_sm * 1e3);
+      // every tail wave ends with reductions: a reducing CTA reads s parts of 128 x bn fp32
+      const double cta_part = 128.0 * bn * 4.0;
+      t += tail_waves * (s * cta_part / (mc.red_gbs_per_sm * 1e3) + mc.red_fixed_us);
     }
     const double unique = (double(M) * K + double(K) * N) * es + double(M) * N * 2;
     const double t_hbm = unique / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);

@@ -672,16 +672,19 @@ __global__ void __launch_bounds__(192, 1)
         } else {
           // K-split slice: write this CTA's fp32 partial (thread-major, so a
           // warp's float4 stores are contiguous), take a ticket, and let the
-          // last slice reduce all partials in slice order.
+          // last slice reduce all partials in slice order. The accumulator
+          // stays in TMEM until the ticket is known: the last slice reads its
+          // own part from there and only the other slices from memory.
           constexpr size_t kPart = (size_t)BM * BN;  // floats per CTA part
-          float4* part = reinterpret_cast<float4*>(
-              p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + w.split) * G + rank) * kPart);
+          const float4* part0 = reinterpret_cast<const float4*>(
+              p.ws_partial + ((size_t)(w.tail_slot * w.nsplit) * G + rank) * kPart);
+          const size_t sstride = (size_t)G * kPart / 4;  // float4s between slices
+          float4* part = const_cast<float4*>(part0) + w.split * sstride;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(t_row + c * 32, r);
             tmem_ld_wait(r);
-            if (c == BN / 32 - 1) release_tmem(buf);
 #pragma unroll
             for (int g = 0; g < 8; ++g)
               __stcg(part + (c * 8 + g) * BM + row_in_tile,
@@ -698,27 +701,85 @@ __global__ void __launch_bounds__(192, 1)
             *s_last = last;
           }
           named_bar_sync(1, 128);
-          if (*s_last) {
+          const bool is_last = *s_last != 0;
+          if (!is_last) release_tmem(buf);
+          if (is_last) {
             __threadfence();
+            // Sum the slices in slice order (own slice from TMEM, bit-equal to
+            // the part written above). The loads of a batch are all issued
+            // before any is used: 2 chunks of the one other slice for a 2-way
+            // split, else up to 2 slices of one chunk.
+            constexpr int CB = 2;
+            if (w.nsplit == 2) {
+              const float4* other = part0 + (1 - w.split) * sstride;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-              float v[32];
+              for (int c0 = 0; c0 < BN / 32; c0 += CB) {
+                float4 t[CB][8];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.f;
-              for (int s = 0; s < w.nsplit; ++s) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.ws_partial + ((size_t)(w.tail_slot * w.nsplit + s) * G + rank) * kPart);
+                for (int cc = 0; cc < CB; ++cc)
+                  if (c0 + cc < BN / 32) {
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                  const float4 t = __ldcg(src + (c * 8 + g) * BM + row_in_tile);
-                  v[4 * g] += t.x;
-                  v[4 * g + 1] += t.y;
-                  v[4 * g + 2] += t.z;
-                  v[4 * g + 3] += t.w;
+                    for (int g = 0; g < 8; ++g) t[cc][g] = __ldcg(other + ((c0 + cc) * 8 + g) * BM + row_in_tile);
+                  }
+#pragma unroll
+                for (int cc = 0; cc < CB; ++cc) {
+                  if (c0 + cc >= BN / 32) break;
+                  uint32_t r[32];
+                  tmem_ld32(t_row + (c0 + cc) * 32, r);
+                  tmem_ld_wait(r);
+                  float v[32];
+#pragma unroll
+                  for (int g = 0; g < 8; ++g) {
+                    const float4 o = t[cc][g];
+                    const float m0 = __uint_as_float(r[4 * g]), m1 = __uint_as_float(r[4 * g + 1]);
+                    const float m2 = __uint_as_float(r[4 * g + 2]), m3 = __uint_as_float(r[4 * g + 3]);
+                    // slice order: slice 0 first
+                    v[4 * g] = w.split == 0 ? (0.f + m0) + o.x : (0.f + o.x) + m0;
+                    v[4 * g + 1] = w.split == 0 ? (0.f + m1) + o.y : (0.f + o.y) + m1;
+                    v[4 * g + 2] = w.split == 0 ? (0.f + m2) + o.z : (0.f + o.z) + m2;
+                    v[4 * g + 3] = w.split == 0 ? (0.f + m3) + o.w : (0.f + o.w) + m3;
+                  }
+                  if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + (c0 + cc) * 32, v);
                 }
               }
-              if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
+            } else {
+#pragma unroll 1
+              for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(t_row + c * 32, r);
+                tmem_ld_wait(r);
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.f;
+                for (int s0 = 0; s0 < w.nsplit; s0 += 2) {
+                  float4 t[2][8];
+#pragma unroll
+                  for (int s = 0; s < 2; ++s)
+                    if (s0 + s < w.nsplit && s0 + s != w.split) {
+#pragma unroll
+                      for (int g = 0; g < 8; ++g) t[s][g] = __ldcg(part0 + (s0 + s) * sstride + (c * 8 + g) * BM + row_in_tile);
+                    }
+#pragma unroll
+                  for (int s = 0; s < 2; ++s) {
+                    if (s0 + s >= w.nsplit) break;
+                    if (s0 + s == w.split) {
+#pragma unroll
+                      for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+                    } else {
+#pragma unroll
+                      for (int g = 0; g < 8; ++g) {
+                        v[4 * g] += t[s][g].x;
+                        v[4 * g + 1] += t[s][g].y;
+                        v[4 * g + 2] += t[s][g].z;
+                        v[4 * g + 3] += t[s][g].w;
+                      }
+                    }
+                  }
+                }
+                if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
+              }
             }
+            release_tmem(buf);
           }
         }
       }
