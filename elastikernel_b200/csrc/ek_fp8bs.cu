@@ -62,10 +62,11 @@ int launch_tok(int tok, bool pair, const CUtensorMap& ta, const CUtensorMap& tb,
   if (pair) {
     switch (tok) {
       case 128: return launch<Fp8BsCfg<128, kEpi, true>>(ta, tb, tx, P, grid, s);
+      case 160: return launch<Fp8BsCfg<160, kEpi, true>>(ta, tb, tx, P, grid, s);
       case 192: return launch<Fp8BsCfg<192, kEpi, true>>(ta, tb, tx, P, grid, s);
       case 256: return launch<Fp8BsCfg<256, kEpi, true>>(ta, tb, tx, P, grid, s);
     }
-    return set_error(EK_ERR_INVALID, "fp8 block-scaled pair token tile must be 128, 192 or 256 (got %d)", tok);
+    return set_error(EK_ERR_INVALID, "fp8 block-scaled pair token tile must be 128, 160, 192 or 256 (got %d)", tok);
   }
   switch (tok) {
     case 16: return launch<Fp8BsCfg<16, kEpi>>(ta, tb, tx, P, grid, s);
@@ -92,8 +93,9 @@ void tiles(long long rows, int E, int S, int force_tok, int force_pair, bool pai
   if (t <= 0) {
     if (pr) {
       // 256-token pair tiles need 16 epilogue warps and run short of registers:
-      // a busier expert takes several 192-token tiles instead
-      t = want <= 128 ? 128 : 192;
+      // a busier expert takes several 192-token tiles instead. A 160-token
+      // tile leaves TMEM room for 3 K-block buffers (192: 2).
+      t = want <= 128 ? 128 : want <= 160 ? 160 : 192;
     } else {
       t = 16;
       while (t < want && t < 128) t *= 2;

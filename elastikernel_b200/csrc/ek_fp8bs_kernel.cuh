@@ -7,8 +7,9 @@
 // multiplied into its own TMEM buffer (a ring of NBUF buffers); the epilogue
 // warps read it back, multiply by  w_scale[row block, kb] * x_scale[kb, token]
 // and add it to fp32 accumulators held in registers (paired fp32 multiplies
-// and FMAs). The MMA of later K blocks runs while the epilogue scales earlier
-// ones.
+// and FMAs; forming the combined scales once per K block behind a barrier of
+// the epilogue warps measured slower). The MMA of later K blocks runs while
+// the epilogue scales earlier ones.
 //
 // Token scales are K-block-major ([K/128][rows]), so the scales of one K block
 // for a tile's tokens are contiguous. A scale warp copies them and the two
@@ -26,8 +27,8 @@
 // Modes:
 //   single  one CTA: 128 weight rows x up to 128 tokens; 4 epilogue warps
 //           (one thread per weight row, all token columns), 8 from 64 tokens
-//   pair    a CTA pair (2-SM MMA): 256 weight rows x up to 128 / 192 / 256
-//           tokens; each CTA loads its 128 weight rows and half of the
+//   pair    a CTA pair (2-SM MMA): 256 weight rows x up to 128 / 160 / 192 /
+//           256 tokens; each CTA loads its 128 weight rows and half of the
 //           tokens, so one SM streams 28 KB per K step for a 128 x 192 x 128
 //           product; 8 epilogue warps per CTA (16 for 256 tokens), two (four)
 //           per TMEM lane quarter, each owning an interleaved share of the
@@ -64,7 +65,7 @@ struct Fp8BsCfg {
   static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES * CTAS;
-  static constexpr int NBUF = (4 * BN <= 512) ? 4 : 2;  // TMEM ring of K-block products
+  static constexpr int NBUF = (512 / BN) < 4 ? (512 / BN) : 4;  // TMEM ring of K-block products
   static constexpr int TMEM_COLS = (NBUF * BN <= 32) ? 32 : (NBUF * BN <= 64) ? 64 : (NBUF * BN <= 128) ? 128
                                  : (NBUF * BN <= 256) ? 256 : 512;
   // pair: 8 epilogue warps, 16 for the 256-token tile (64 accumulators per thread)
@@ -72,9 +73,10 @@ struct Fp8BsCfg {
   static constexpr int EPI_THREADS = EPI_WARPS * 32;
   static constexpr int COL_GROUPS = EPI_WARPS / 4;   // epilogue warps per TMEM lane quarter
   static constexpr int CPT = BN / COL_GROUPS;        // token columns per epilogue thread
-  // 16-column TMEM loads for the pair tiles: more than 8 warps per CTA put 3 on
-  // some SM sub-partition, which caps a thread at 168 registers
-  static constexpr int CHUNK = CPT < 32 ? CPT : (kPair ? 16 : 32);
+  // 32-column TMEM loads (one wait per 32 columns) where the registers allow:
+  // 16 for the 192- and 256-token pair tiles (96 accumulators at the
+  // 168-register cap of 11+ warps, and 16 epilogue warps at 96 registers)
+  static constexpr int CHUNK = CPT < 32 ? CPT : ((kPair && BN >= 192) || CPT % 32 != 0 ? 16 : 32);
   static constexpr int THREADS = 96 + EPI_THREADS;
   static constexpr int SCALE_SLOTS = 8;       // K blocks of scales in flight ahead of the epilogue
   static constexpr int PREFETCH = 16;         // K blocks of weight tiles prefetched into L2 ahead of the loads
@@ -89,7 +91,8 @@ struct Fp8BsCfg {
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
   static constexpr uint32_t IDESC = umma_idesc(0u /*e4m3*/, false, TILE_M, BN);
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EXTRA_BYTES + 1024 + 512;
-  static_assert(kPair ? (BN == 128 || BN == 192 || BN == 256) : (BN == 16 || BN == 32 || BN == 64 || BN == 128),
+  static_assert(kPair ? (BN == 128 || BN == 160 || BN == 192 || BN == 256)
+                      : (BN == 16 || BN == 32 || BN == 64 || BN == 128),
                 "token tile");
   static_assert(kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT, "epilogue");
   static_assert(CPT % CHUNK == 0, "column chunks");

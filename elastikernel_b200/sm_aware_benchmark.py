@@ -237,9 +237,11 @@ def main():
     parser.add_argument("--layout", choices=["packed", "padded"], default="packed")
     parser.add_argument("--fp8-layer-tokens", type=int, default=0,
                         help="only run the DeepSeek-V3-shaped e4m3 MoE layer at this token count (for profiling)")
+    parser.add_argument("--experts", type=int, default=256,
+                        help="experts on this GPU for --fp8-layer-tokens (fewer experts: a smaller capture)")
     args = parser.parse_args()
     if args.fp8_layer_tokens > 0:
-        run_layer_fp8(args.fp8_layer_tokens, args.reps)
+        run_layer_fp8(args.fp8_layer_tokens, args.reps, args.experts)
     elif args.layer_tokens > 0:
         run_layer(args.layer_tokens, args.reps, layout=args.layout)
     elif args.all:

@@ -243,7 +243,7 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
  * [K/128][rows], as ek_quant_e4m3_kmajor writes them); fp32
  * accumulation with the scales applied per 128-wide K block; bf16 outputs as
  * ek_moe_gate_up_packed / ek_moe_down_packed. H and I must be multiples of
- * 128; tok = token tile (16/32/64/128 on one CTA, 128/192/256 on a CTA pair;
+ * 128; tok = token tile (16/32/64/128 on one CTA, 128/160/192/256 on a CTA pair;
  * 0 = choose), pair = 1 for the CTA-pair (2-SM MMA) kernel, 0 for one CTA,
  * -1 = choose (the down projection runs a pair only when H % 256 == 0).
  * No counterpart in the reference (it has no FP8 path). */

@@ -73,7 +73,8 @@ def test_kmajor_quant_and_scale_gather(cuda_dev):
 
 
 @pytest.mark.parametrize("tok,pair,E", [(16, 0, 16), (32, 0, 16), (64, 0, 16), (128, 0, 16), (128, 0, 4),
-                                        (128, 1, 16), (128, 1, 4), (192, 1, 16), (192, 1, 4), (256, 1, 16),
+                                        (128, 1, 16), (128, 1, 4), (160, 1, 16), (160, 1, 4), (192, 1, 16),
+                                        (192, 1, 4), (256, 1, 16),
                                         (256, 1, 4)])
 def test_fp8bs_gemms_token_tiles(cuda_dev, tok, pair, E):
     """Every token tile on one CTA and on a CTA pair; E=4 puts ~300 tokens on
