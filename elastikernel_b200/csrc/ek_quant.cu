@@ -126,6 +126,118 @@ __global__ void quant_groups_kernel(const void* __restrict__ x, int dt, int rows
   if (lane == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)gid] = s;
 }
 
+// Eight consecutive elements as fp32 (one 16-byte bf16 load or two 16-byte fp32 loads).
+__device__ __forceinline__ void load8(const void* x, int dt, size_t i, float (&v)[8]) {
+  if (dt == 0) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + i));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float s) {
+  uint2 r;
+  r.x = (uint32_t)to_e4m3(v[0] / s) | ((uint32_t)to_e4m3(v[1] / s) << 8) | ((uint32_t)to_e4m3(v[2] / s) << 16) |
+        ((uint32_t)to_e4m3(v[3] / s) << 24);
+  r.y = (uint32_t)to_e4m3(v[4] / s) | ((uint32_t)to_e4m3(v[5] / s) << 8) | ((uint32_t)to_e4m3(v[6] / s) << 16) |
+        ((uint32_t)to_e4m3(v[7] / s) << 24);
+  return r;
+}
+
+// 1 x 128 groups, rows a multiple of 8 elements long: a half-warp per group,
+// eight elements (one 16-byte load, one 8-byte store) per lane, two groups
+// per half-warp in flight. Scales as quant_groups_kernel.
+__global__ void quant_groups_vec_kernel(const void* __restrict__ x, int dt, int rows, int cols,
+                                        uint8_t* __restrict__ q, float* __restrict__ scales, int kmajor) {
+  const int groups = (cols + 127) / 128;
+  const long long total = (long long)rows * groups;
+  const int hl = threadIdx.x & 15;  // lane within the half-warp
+  const int half = (threadIdx.x >> 4) & 1;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  // the loop bound is uniform across the warp, so every lane reaches the shuffles
+  for (long long wb = (((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; wb < total; wb += 4 * nwarps) {
+    const long long gid[2] = {wb + half, wb + 2 * nwarps + half};
+    float v[2][8];
+    bool ok[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      ok[u] = gid[u] < total;
+      const int row = ok[u] ? (int)(gid[u] / groups) : 0, g = ok[u] ? (int)(gid[u] % groups) : 0;
+      const int c0 = g * 128 + hl * 8;
+      if (ok[u] && c0 < cols) {
+        load8(x, dt, (size_t)row * cols + c0, v[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[u][j]));
+#pragma unroll
+      for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (!ok[u]) continue;
+      const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+      const int row = (int)(gid[u] / groups), g = (int)(gid[u] % groups);
+      const int c0 = g * 128 + hl * 8;
+      if (c0 < cols) *reinterpret_cast<uint2*>(q + (size_t)row * cols + c0) = pack8_e4m3(v[u], s);
+      if (hl == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)gid[u]] = s;
+    }
+  }
+}
+
+// 128 x 128 blocks of a matrix whose rows are a multiple of 8 elements long:
+// a CTA of 256 threads per block, each thread eight rows x eight consecutive
+// columns held in registers between the amax and the quantisation (one read).
+__global__ void quant_blocks128_vec_kernel(const void* __restrict__ x, int dt, int rows, int cols,
+                                           uint8_t* __restrict__ q, float* __restrict__ scales) {
+  const int nbc = (cols + 127) / 128;
+  const int bi = blockIdx.x / nbc, bj = blockIdx.x % nbc;
+  const int cl = (threadIdx.x & 15) * 8;  // column within the block
+  const int r0 = threadIdx.x >> 4;        // first row (0..15), then every 16th
+  const int c = bj * 128 + cl;
+  float v[8][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = bi * 128 + r0 + 16 * i;
+    if (r < rows && c < cols) {
+      load8(x, dt, (size_t)r * cols + c, v[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+  }
+  __shared__ float red[8];
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  const float s = m > 0.f ? m / kE4M3Max : 1.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = bi * 128 + r0 + 16 * i;
+    if (r < rows && c < cols) *reinterpret_cast<uint2*>(q + (size_t)r * cols + c) = pack8_e4m3(v[i], s);
+  }
+  if (threadIdx.x == 0) scales[blockIdx.x] = s;
+}
+
 }  // namespace
 }  // namespace ek
 
@@ -146,9 +258,21 @@ int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows
     quant_rows_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
                                                                       static_cast<uint8_t*>(q), scales);
   } else if (br == 1 && bc == 128) {
-    const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
-    quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
-                                                                        static_cast<uint8_t*>(q), scales, 0);
+    if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
+      const long long halves = (long long)rows * ((cols + 127) / 128);
+      const long long blocks = std::min<long long>((halves + 31) / 32, 148LL * 32);
+      quant_groups_vec_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, s>>>(
+          x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales, 0);
+    } else {
+      const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
+      quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
+                                                                          static_cast<uint8_t*>(q), scales, 0);
+    }
+  } else if (br == 128 && bc == 128 && cols % 8 == 0 && aligned16(x) && aligned16(q)) {
+    const long long blocks = (long long)((rows + 127) / 128) * ((cols + 127) / 128);
+    if (blocks > 0x7fffffffLL) return set_error(EK_ERR_INVALID, "quant: too many blocks");
+    quant_blocks128_vec_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, x_dtype, rows, cols, static_cast<uint8_t*>(q),
+                                                                scales);
   } else if (br >= 1 && bc >= 1) {
     const long long blocks = (long long)((rows + br - 1) / br) * ((cols + bc - 1) / bc);
     if (blocks > 0x7fffffffLL) return set_error(EK_ERR_INVALID, "quant: too many blocks");
@@ -165,9 +289,17 @@ int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q
   if (!x || !q || !scales_t || rows < 0 || cols <= 0 || (x_dtype != 0 && x_dtype != 3))
     return set_error(EK_ERR_INVALID, "quant_kmajor: bad arguments (x_dtype 0 = bf16, 3 = fp32)");
   if (rows == 0) return EK_OK;
-  const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
-  quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
+    const long long halves = (long long)rows * ((cols + 127) / 128);
+    const long long blocks = std::min<long long>((halves + 31) / 32, 148LL * 32);
+    quant_groups_vec_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, s>>>(
+        x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1);
+  } else {
+    const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
+    quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
+                                                                        static_cast<uint8_t*>(q), scales_t, 1);
+  }
   return check_cuda(cudaGetLastError(), "quant_kmajor launch");
 }
 

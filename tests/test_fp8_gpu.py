@@ -31,11 +31,15 @@ def test_quant_rows_bit_exact(cuda_dev, dtype, rows, cols):
 
 
 @pytest.mark.parametrize("block", [(1, 128), (128, 128), (64, 32)])
-def test_quant_blocks_bit_exact(cuda_dev, block):
+@pytest.mark.parametrize("dtype,shape", [(torch.float32, (300, 520)), (torch.bfloat16, (300, 520)),
+                                         (torch.float32, (130, 517))])
+def test_quant_blocks_bit_exact(cuda_dev, block, dtype, shape):
+    """Partial edge blocks; rows of a multiple of 8 elements take the vector
+    kernels, 517 the element-wise ones."""
     from elastikernel_b200 import _ops
 
     g = torch.Generator().manual_seed(block[0] * 7 + block[1])
-    x = torch.randn((300, 520), generator=g) * 3.0
+    x = (torch.randn(shape, generator=g) * 3.0).to(dtype)
     q, s = _ops.quant_e4m3(x.to(cuda_dev), block=block)
     rq, rs = of8.quant_blocks(x, *block)
     np.testing.assert_array_equal(s.cpu().numpy(), rs)

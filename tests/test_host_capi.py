@@ -182,3 +182,20 @@ def test_planner_beats_reference_tiles_at_148():
     assert p["est_us"] < ref_tile["est_us"]
     assert p["est_us"] <= min(unsplit["est_us"], split2["est_us"])
     assert unsplit["wave_efficiency"] < 0.87 and split2["wave_efficiency"] > 0.98
+
+
+def test_plan_table_per_sm_level():
+    """The SM-level dispatch table holds, for each partition size, exactly the
+    plan the C planner makes for it; bigger partitions never get a slower
+    estimate for the same shape."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200 import sm_aware_matmul as smm
+
+    levels = [16, 32, 64, 96, 136, 148]
+    t = smm.plan_table(4096, 4096, 4096, levels)
+    assert sorted(t) == levels
+    for s in levels:
+        assert t[s] == _ops.plan(4096, 4096, 4096, s)
+        assert t[s]["num_sms"] == s
+    est = [t[s]["est_us"] for s in levels]
+    assert all(b <= a * 1.001 for a, b in zip(est, est[1:]))
