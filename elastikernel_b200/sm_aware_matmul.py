@@ -98,23 +98,15 @@ class GraphMatmul:
     tensor each time."""
 
     def __init__(self, a, b, num_sms=None, stream=None):
-        import torch
+        from .graph import Captured
 
-        self.stream = stream or torch.cuda.current_stream(a.device)
         self.a, self.b = a, b
-        with torch.cuda.stream(self.stream):
-            call_sm_aware(a, b, num_sms)  # warm-up: kernel attributes, per-stream scratch
-        self.stream.synchronize()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=self.stream):
-            self.c = call_sm_aware(a, b, num_sms)
+        self._cap = Captured(lambda: call_sm_aware(a, b, num_sms), stream, a.device)
+        self.stream = self._cap.stream
+        self.c = self._cap.out
 
     def __call__(self):
-        import torch
-
-        with torch.cuda.stream(self.stream):
-            self.graph.replay()
-        return self.c
+        return self._cap()
 
 
 def run_analytical(sm_levels=None, test_cases=None) -> None:

@@ -48,3 +48,30 @@ def test_graph_matmul_matches_eager(cuda_dev):
         eager2 = smm.call_sm_aware(a, b)
     torch.cuda.synchronize()
     assert torch.equal(out2, eager2) and not torch.equal(eager2, eager)
+
+
+@pytest.mark.parametrize("layout", ["packed", "padded"])
+def test_captured_moe_layer_matches_eager(cuda_dev, layout):
+    """The whole fused MoE layer captures as one CUDA graph (no host reads of
+    device data) and replays bit-exactly; new inputs copied in place are used."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.graph import Captured
+
+    T, H, I, E, k = 16, 512, 256, 8, 2
+    g = torch.Generator(device=cuda_dev).manual_seed(5)
+    x = torch.randn((T, H), device=cuda_dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn((T, E), device=cuda_dev, generator=g)
+    w1 = (torch.randn((E, I, H), device=cuda_dev, generator=g) * 0.05).to(torch.bfloat16)
+    w3 = (torch.randn((E, I, H), device=cuda_dev, generator=g) * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn((E, H, I), device=cuda_dev, generator=g) * 0.05).to(torch.bfloat16)
+    y = torch.empty((T, H), device=cuda_dev, dtype=torch.bfloat16)
+    cap = Captured(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k, out=y, layout=layout))
+    out = cap()
+    eager = _ops.fused_moe(x, logits, w1, w2, w3, k, layout=layout)
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    logits.copy_(torch.randn((T, E), device=cuda_dev, generator=g))
+    out2 = cap().clone()
+    eager2 = _ops.fused_moe(x, logits, w1, w2, w3, k, layout=layout)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, eager2)
