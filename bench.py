@@ -235,7 +235,7 @@ def fp8_bench(dev, peak_bf16_tflops: float, steps: int) -> dict:
             "fp8_peak_tflops": peak_fp8, "peak_note": "2 x measured bf16 burst", "results": res}
 
 
-def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float) -> dict:
+def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: int = 0) -> dict:
     """DeepSeek-V3-shaped expert-parallel MoE: 256 experts, top-8 softmax
     routing, H=7168, I=2048, e4m3 experts with 128 x 128 block scales, 4096
     tokens per rank, 256/world experts per rank, e4m3 dispatch over NCCL
@@ -272,18 +272,30 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float) -> dict:
         (comm_stream, comm_sms), (gemm_stream, gemm_sms) = create_disjoint_partitions(dev, [32, 112])
     else:
         gemm_stream, gemm_sms = torch.cuda.current_stream(dev), total
+        comm_stream = torch.cuda.Stream(dev)
     moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms))
-    with torch.cuda.stream(gemm_stream):
+    # Two chunks let the dispatch / combine of one half overlap the expert
+    # GEMMs of the other, but each chunk streams every local expert's weights
+    # again: worth it only where the experts are compute-bound, i.e. with
+    # ~1024+ tokens per local expert (8 GPUs: 4096 * 8 * 8 / 256 = 1024).
+    if chunks <= 0:
+        chunks = 2 if T * k * world // E >= 1024 else 1
+
+    def layer():
+        return moe(x, logits, chunks=chunks, compute_stream=gemm_stream, comm_stream=comm_stream)
+
+    main = torch.cuda.Stream(dev)
+    with torch.cuda.stream(main):
         for _ in range(2):
-            moe(x, logits)
+            layer()
         torch.cuda.synchronize()
         barrier(world)
         reps = max(3, steps // 10)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
+        s.record(main)
         for _ in range(reps):
-            moe(x, logits)
-        e.record()
+            layer()
+        e.record(main)
         torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / reps, world)
     flop = T * k * 6.0 * H * I
@@ -294,7 +306,8 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float) -> dict:
             "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
             "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
-            "host_sync": "per-layer count exchange read on the host (all-to-all split sizes)"}
+            "chunks": chunks,
+            "host_sync": "per-chunk count exchange read on the host (all-to-all split sizes)"}
 
 
 def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:

@@ -224,12 +224,69 @@ class ExpertParallelMoE:
         self._a2a(y_back, y_local, d.send_counts, d.recv_counts)
         return self.ops.combine_rows(y_back, d.slot_row, d.T, d.topk)
 
-    def forward(self, x, gate_logits):
-        x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)
+    def _experts(self, x_recv, ids_recv, w_recv):
         if self.fp8:
-            y_local = self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw)
-        else:
-            y_local = self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
-        return self.combine(y_local, d)
+            return self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw)
+        return self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
+
+    def forward(self, x, gate_logits, chunks: int = 1, compute_stream=None, comm_stream=None):
+        """The layer for this rank's tokens x [T, H] (router logits [T, E]).
+
+        chunks > 1 splits the tokens into that many contiguous chunks and
+        pipelines them: with CUDA streams given (the expert GEMMs on
+        `compute_stream`, e.g. the large green-context partition; routing,
+        dispatch and combine on `comm_stream`, e.g. the small one), the
+        dispatch of chunk i+1 and the combine of chunk i-1 run while chunk i's
+        experts compute. Every rank must use the same number of chunks (the
+        collectives of a chunk pair up across ranks). Results equal the
+        unchunked layer: every token's rows are computed and summed the same
+        way whichever chunk carries them."""
+        T = x.shape[0]
+        chunks = max(1, min(int(chunks), T))
+        if chunks == 1:
+            x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)
+            return self.combine(self._experts(x_recv, ids_recv, w_recv), d)
+        bounds = [(c * T // chunks, (c + 1) * T // chunks) for c in range(chunks)]
+        if not x.is_cuda or compute_stream is None or comm_stream is None:
+            # one stream: the chunks run one after another (same collectives, same results)
+            return torch.cat([self.forward(x[a:b], gate_logits[a:b]) for a, b in bounds], dim=0)
+        return self._forward_pipelined(x, gate_logits, bounds, compute_stream, comm_stream)
+
+    def _forward_pipelined(self, x, gate_logits, bounds, compute, comm):
+        cur = torch.cuda.current_stream(x.device)
+        out = torch.empty_like(x)
+        comm.wait_stream(cur)
+        compute.wait_stream(cur)
+
+        def dispatch(c):
+            a, b = bounds[c]
+            with torch.cuda.stream(comm):
+                r = self.dispatch(x[a:b], gate_logits[a:b])
+                ev = torch.cuda.Event()
+                ev.record(comm)
+            return r, ev
+
+        pending = dispatch(0)
+        for c, (a, b) in enumerate(bounds):
+            (x_recv, ids_recv, w_recv, d), ev_d = pending
+            with torch.cuda.stream(compute):
+                compute.wait_event(ev_d)
+                for t in (x_recv if isinstance(x_recv, tuple) else (x_recv,)) + (ids_recv, w_recv):
+                    t.record_stream(compute)  # made on the comm stream, read here
+                y_local = self._experts(x_recv, ids_recv, w_recv)
+                ev_e = torch.cuda.Event()
+                ev_e.record(compute)
+            if c + 1 < len(bounds):
+                # The next chunk's routing and dispatch (and its host read of
+                # the split sizes) go ahead of this chunk's combine on the comm
+                # stream, so they overlap the experts just queued.
+                pending = dispatch(c + 1)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_e)
+                y_local.record_stream(comm)  # made on the compute stream, sent from here
+                out[a:b].copy_(self.combine(y_local, d))
+        out.record_stream(comm)
+        cur.wait_stream(comm)
+        return out
 
     __call__ = forward

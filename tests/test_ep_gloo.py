@@ -103,7 +103,8 @@ def _worker(rank, world, port, q, mode):
                 q.close()
                 q.join_thread()  # the message must reach the parent before the hard exit
                 os._exit(0)  # leaves between steps, without cleanup
-        out = moe(x, logits)
+        # "chunked": the tokens go through in 3 chunks (ragged: T is not a multiple of 3)
+        out = moe(x, logits, chunks=3) if mode == "chunked" else moe(x, logits)
         ref = om.moe_ref(x.numpy(), logits.numpy(), w1, w2, w3, K_TOP)
         err = float(np.abs(out.numpy() - ref).max() / np.abs(ref).max())
         q.put((rank, err))
@@ -130,9 +131,9 @@ def _run(world, mode):
     return results
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_matches_single_process_oracle(world):
-    res = _run(world, "normal")
+@pytest.mark.parametrize("world,mode", [(2, "normal"), (4, "normal"), (2, "chunked")])
+def test_ep_matches_single_process_oracle(world, mode):
+    res = _run(world, mode)
     for rank, err in res.items():
         assert not isinstance(err, str), f"rank {rank}: {err}"
         assert err < 1e-5, f"rank {rank}: max rel err {err:.3e}"

@@ -66,6 +66,27 @@ def test_ep_world1_fp8(cuda_dev):
     assert max_rel_err(out, ref.float().cpu().numpy()) <= 1e-2
 
 
+@pytest.mark.parametrize("fp8", [False, True])
+def test_ep_world1_chunked_streams(cuda_dev, fp8):
+    """Chunks pipelined over two green-context partitions (experts on the
+    large one, routing / dispatch / combine on the small one) give the same
+    layer as the unchunked forward."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.ep_moe import CudaEPOps, ExpertParallelMoE
+    from elastikernel_b200.green_ctx import create_disjoint_partitions
+
+    w1, w2, w3 = _weights(cuda_dev)
+    (comm, _), (comp, comp_sms) = create_disjoint_partitions(cuda_dev, [32, 112])
+    kw = {"qw": _ops.quant_moe_weights_fp8(w1, w2, w3)} if fp8 else {"w1": w1, "w2": w2, "w3": w3}
+    moe = ExpertParallelMoE(E, K_TOP, ops=CudaEPOps(num_sms=comp_sms), **kw)
+    x, logits = _tokens(cuda_dev, 0, 333)
+    ref = moe(x, logits)
+    out = moe(x, logits, chunks=3, compute_stream=comp, comm_stream=comm)
+    torch.cuda.synchronize()
+    assert out.shape == ref.shape
+    assert max_rel_err(out, ref.float().cpu().numpy()) <= 1e-3
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -100,6 +121,11 @@ def _worker(rank, world, port, q):
         out8 = ExpertParallelMoE(E, K_TOP, qw=qw)(x, logits)
         ref8 = _ops.fused_moe_fp8(x, logits, qw_all, K_TOP)
         err_fp8 = max_rel_err(out8, ref8.float().cpu().numpy())
+        # the same layer pipelined in 2 chunks over two streams (dispatch of one
+        # chunk and combine of the other overlap the experts)
+        comp, comm = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        out8c = ExpertParallelMoE(E, K_TOP, qw=qw)(x, logits, chunks=2, compute_stream=comp, comm_stream=comm)
+        err_fp8 = max(err_fp8, max_rel_err(out8c, ref8.float().cpu().numpy()))
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
