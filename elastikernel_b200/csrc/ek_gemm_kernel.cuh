@@ -53,6 +53,9 @@ enum Epi : int {
 enum Sched : int { kSchedDense = 0, kSchedBlocks = 1, kSchedSegments = 2, kSchedExperts = 3 };
 
 constexpr int kMaxExpertsT = 256;  // experts per launch of the swapped schedule
+// Split-K tickets occupy ints [0, 1024) of the workspace front, the 2-way
+// split's "part written" flags ints [1024, 2048).
+constexpr int kGemmFlagOffset = 1024;
 
 template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false>
 struct GemmCfg {
@@ -670,48 +673,49 @@ __global__ void __launch_bounds__(192, 1)
             if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
           }
         } else {
-          // K-split slice: write this CTA's fp32 partial (thread-major, so a
-          // warp's float4 stores are contiguous), take a ticket, and let the
-          // last slice reduce all partials in slice order. The accumulator
-          // stays in TMEM until the ticket is known: the last slice reads its
-          // own part from there and only the other slices from memory.
+          // K-split slice. Parts are fp32, thread-major (a warp's float4
+          // stores and loads are contiguous), one per slice and CTA.
           constexpr size_t kPart = (size_t)BM * BN;  // floats per CTA part
-          const float4* part0 = reinterpret_cast<const float4*>(
-              p.ws_partial + ((size_t)(w.tail_slot * w.nsplit) * G + rank) * kPart);
-          const size_t sstride = (size_t)G * kPart / 4;  // float4s between slices
-          float4* part = const_cast<float4*>(part0) + w.split * sstride;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(t_row + c * 32, r);
-            tmem_ld_wait(r);
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              __stcg(part + (c * 8 + g) * BM + row_in_tile,
-                     make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
-                                 __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
-          }
-          __threadfence();
-          named_bar_sync(1, 128);
           const int ticket = w.tail_slot * G + rank;
-          if (epi_tid == 0) {
-            const int old = atomicAdd(&p.ws_counters[ticket], 1);
-            const int last = (old == w.nsplit - 1);
-            if (last) p.ws_counters[ticket] = 0;  // ready for the next launch
-            *s_last = last;
-          }
-          named_bar_sync(1, 128);
-          const bool is_last = *s_last != 0;
-          if (!is_last) release_tmem(buf);
-          if (is_last) {
-            __threadfence();
-            // Sum the slices in slice order (own slice from TMEM, bit-equal to
-            // the part written above). The loads of a batch are all issued
-            // before any is used: 2 chunks of the one other slice for a 2-way
-            // split, else up to 2 slices of one chunk.
-            constexpr int CB = 2;
-            if (w.nsplit == 2) {
-              const float4* other = part0 + (1 - w.split) * sstride;
+          if (w.nsplit == 2) {
+            // Two slices: the first to finish its K half writes its part and
+            // raises a flag; the second waits for the flag (bounded; the
+            // first never waits, so this cannot deadlock), adds that part to
+            // its own accumulator straight from TMEM and stores the tile. One
+            // part is written and read per tile instead of two written and two
+            // read. The sum is in slice order, as in the general path.
+            int* flag = p.ws_counters + kGemmFlagOffset + ticket;
+            if (epi_tid == 0) *s_last = atomicAdd(&p.ws_counters[ticket], 1);
+            named_bar_sync(1, 128);
+            const bool second = *s_last != 0;
+            const float4* part_w = reinterpret_cast<const float4*>(
+                p.ws_partial + ((size_t)(w.tail_slot * 2) * G + rank) * kPart);  // the tile's one part
+            if (!second) {
+#pragma unroll 1
+              for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(t_row + c * 32, r);
+                tmem_ld_wait(r);
+                if (c == BN / 32 - 1) release_tmem(buf);
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                  __stcg(const_cast<float4*>(part_w) + (c * 8 + g) * BM + row_in_tile,
+                         make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                     __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+              }
+              __threadfence();
+              named_bar_sync(1, 128);
+              if (epi_tid == 0) st_release_gpu(flag, 1);
+            } else {
+              if (epi_tid == 0) {
+                if (!spin_flag_acquire(flag, s_abort)) atomicOr(&g_ek_status, kStatusWaitTimeout);
+                p.ws_counters[ticket] = 0;  // ready for the next launch
+                *flag = 0;
+              }
+              named_bar_sync(1, 128);
+              __threadfence();
+              const bool other_first = w.split == 1;  // the part holds slice 0 when this is slice 1
+              constexpr int CB = 2;
 #pragma unroll 1
               for (int c0 = 0; c0 < BN / 32; c0 += CB) {
                 float4 t[CB][8];
@@ -719,7 +723,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int cc = 0; cc < CB; ++cc)
                   if (c0 + cc < BN / 32) {
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) t[cc][g] = __ldcg(other + ((c0 + cc) * 8 + g) * BM + row_in_tile);
+                    for (int g = 0; g < 8; ++g) t[cc][g] = __ldcg(part_w + ((c0 + cc) * 8 + g) * BM + row_in_tile);
                   }
 #pragma unroll
                 for (int cc = 0; cc < CB; ++cc) {
@@ -733,16 +737,51 @@ __global__ void __launch_bounds__(192, 1)
                     const float4 o = t[cc][g];
                     const float m0 = __uint_as_float(r[4 * g]), m1 = __uint_as_float(r[4 * g + 1]);
                     const float m2 = __uint_as_float(r[4 * g + 2]), m3 = __uint_as_float(r[4 * g + 3]);
-                    // slice order: slice 0 first
-                    v[4 * g] = w.split == 0 ? (0.f + m0) + o.x : (0.f + o.x) + m0;
-                    v[4 * g + 1] = w.split == 0 ? (0.f + m1) + o.y : (0.f + o.y) + m1;
-                    v[4 * g + 2] = w.split == 0 ? (0.f + m2) + o.z : (0.f + o.z) + m2;
-                    v[4 * g + 3] = w.split == 0 ? (0.f + m3) + o.w : (0.f + o.w) + m3;
+                    v[4 * g] = other_first ? (0.f + o.x) + m0 : (0.f + m0) + o.x;
+                    v[4 * g + 1] = other_first ? (0.f + o.y) + m1 : (0.f + m1) + o.y;
+                    v[4 * g + 2] = other_first ? (0.f + o.z) + m2 : (0.f + m2) + o.z;
+                    v[4 * g + 3] = other_first ? (0.f + o.w) + m3 : (0.f + m3) + o.w;
                   }
                   if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + (c0 + cc) * 32, v);
                 }
               }
-            } else {
+              release_tmem(buf);
+            }
+          } else {
+            // More slices: every slice writes its part and takes a ticket;
+            // the last one reduces. The accumulator stays in TMEM until the
+            // ticket is known: the last slice reads its own part from there.
+            const float4* part0 = reinterpret_cast<const float4*>(
+                p.ws_partial + ((size_t)(w.tail_slot * w.nsplit) * G + rank) * kPart);
+            const size_t sstride = (size_t)G * kPart / 4;  // float4s between slices
+            float4* part = const_cast<float4*>(part0) + w.split * sstride;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(t_row + c * 32, r);
+              tmem_ld_wait(r);
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                __stcg(part + (c * 8 + g) * BM + row_in_tile,
+                       make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                   __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+            }
+            __threadfence();
+            named_bar_sync(1, 128);
+            if (epi_tid == 0) {
+              const int old = atomicAdd(&p.ws_counters[ticket], 1);
+              const int last = (old == w.nsplit - 1);
+              if (last) p.ws_counters[ticket] = 0;  // ready for the next launch
+              *s_last = last;
+            }
+            named_bar_sync(1, 128);
+            const bool is_last = *s_last != 0;
+            if (!is_last) release_tmem(buf);
+            if (is_last) {
+              __threadfence();
+              // Sum the slices in slice order (own slice from TMEM, bit-equal
+              // to the part written above); the loads of up to 2 slices of a
+              // chunk are issued before any is used.
 #pragma unroll 1
               for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -778,8 +817,8 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 if (row_ok) finish_chunk<Cfg>(p, row, w.c_col + c * 32, v);
               }
+              release_tmem(buf);
             }
-            release_tmem(buf);
           }
         }
       }

@@ -44,7 +44,7 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Split-K workspace layout of the dense GEMM: ticket counters first (a fixed
 // region, so tickets of one shape never land on another shape's partials in
 // a reused buffer), then the fp32 partial tiles.
-constexpr size_t kGemmTicketBytes = 8192;
+constexpr size_t kGemmTicketBytes = 8192;  // 1024 tickets + 1024 flags (ints)
 constexpr int kGemmMaxSms = 1024;  // tail tiles (< SMs) x 2 CTAs fit the ticket region
 
 // Dense GEMM schedule for a partition of S SMs (ek_gemm_plan_make).

@@ -89,6 +89,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- flags in global memory
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait (bounded like mbar_wait) until *p == 1 with acquire semantics at GPU
+// scope. Returns false if the CTA was aborted or the wait timed out (which
+// raises the abort flag).
+__device__ __forceinline__ bool spin_flag_acquire(const int* p, volatile int* abort_flag) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v == 1) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
