@@ -465,17 +465,25 @@ def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = N
 
 
 PACKED_MIN_SMS = 112
+PACKED_MAX_ROWS_PER_EXPERT = 384
 
 
-def moe_layout(num_sms: int, num_experts: int) -> str:
-    """Layout the fused MoE uses on a partition of `num_sms` SMs.
+def moe_layout(num_sms: int, num_experts: int, rows: int | None = None) -> str:
+    """Layout the fused MoE uses on a partition of `num_sms` SMs for `rows`
+    routed rows (tokens x top-k; None: not known).
 
     Measured on B200 (Mixtral shapes, T = 1..4096): the packed layout with the
-    swapped-operand GEMMs is faster on (nearly) the full device -- T=128 takes
-    512 us packed vs 597 us padded on 148 SMs -- while the 128-row padded
-    layout is faster on small partitions (T=128 on 80 SMs: 650 us padded vs
-    795 us packed)."""
-    return "packed" if num_sms >= PACKED_MIN_SMS and num_experts <= 256 else "padded"
+    swapped-operand GEMMs is faster on (nearly) the full device while experts
+    get up to a few hundred rows -- T=128: 519 us packed vs 578 us padded,
+    T=1024 (256 rows per expert): 845 vs 877 us on 148 SMs -- and the 128-row
+    padded layout from 512 rows per expert (T=2048: 1334 vs 1379 us, T=4096:
+    2402 vs 2572 us) and on small partitions (T=128 on 72 SMs: 632 us padded
+    vs 833 us packed)."""
+    if num_sms < PACKED_MIN_SMS or num_experts > 256:
+        return "padded"
+    if rows is not None and rows > PACKED_MAX_ROWS_PER_EXPERT * num_experts:
+        return "padded"
+    return "packed"
 
 
 def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
@@ -493,7 +501,7 @@ def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.
         return out if out is not None else torch.empty_like(hidden_states)
     if layout == "auto":
         sms = int(num_sms) if num_sms else _stream_sms(dev, current_stream_handle(dev))
-        layout = moe_layout(sms, w1.shape[0])
+        layout = moe_layout(sms, w1.shape[0], T * topk)
     ids, wts = moe_route(gate_logits, topk)
     if layout == "packed" and w1.shape[0] <= 256:
         perm = moe_permute(ids, w1.shape[0], x=hidden_states, block_m=1)

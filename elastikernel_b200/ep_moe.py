@@ -95,7 +95,7 @@ class CudaEPOps:
             return torch.empty((0, H), dtype=torch.bfloat16, device=x_recv.device)
         E = w1.shape[0]
         layout = _ops.moe_layout(int(self.num_sms or _ops._stream_sms(x_recv.device, _ops.current_stream_handle(
-            x_recv.device))), E)
+            x_recv.device))), E, R)
         if layout == "packed":
             perm = _ops.moe_permute(local_ids.view(R, 1), E, x=x_recv, block_m=1)
             act = _ops.moe_gate_up_packed(perm, w1, w3, num_sms=self.num_sms)
