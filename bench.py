@@ -166,6 +166,40 @@ def timed_steps(step_fn, steps: int, flush) -> tuple[float, list]:
     return sum(ms) / len(ms), ms
 
 
+def e2e_pipelined(smm, a_h, b_h, a_like, b_like, steps: int) -> float:
+    """Mean ms per step of `steps` end-to-end GEMM steps through the public
+    call: every step copies its inputs from pinned host memory, multiplies
+    with sm_aware_matmul.call_sm_aware and reads the product back to pinned
+    host memory. Host->device copies run on a copy stream into two device
+    buffers, so step i+1's inputs cross PCIe while step i computes and reads
+    back; every copy of every step is inside the timed region."""
+    cmp = torch.cuda.current_stream()
+    cin = torch.cuda.Stream()
+    bufs = [(torch.empty_like(a_like), torch.empty_like(b_like)) for _ in range(2)]
+    c_hs = [torch.empty((a_like.shape[0], b_like.shape[1]), dtype=a_like.dtype).pin_memory() for _ in range(2)]
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(cmp)
+    cin.wait_event(start)
+    for i in range(steps):
+        j = i % 2
+        with torch.cuda.stream(cin):
+            if i >= 2:
+                cin.wait_event(free[j])  # the product of step i-2 no longer reads buffer j
+            bufs[j][0].copy_(a_h, non_blocking=True)
+            bufs[j][1].copy_(b_h, non_blocking=True)
+            loaded[j].record(cin)
+        cmp.wait_event(loaded[j])
+        c = smm.call_sm_aware(bufs[j][0], bufs[j][1])
+        free[j].record(cmp)
+        c_hs[j].copy_(c, non_blocking=True)
+    end.record(cmp)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
 def partition_sweep(dev, peak_tflops: float, steps: int) -> dict:
     from elastikernel_b200 import sm_aware_matmul as smm
     from elastikernel_b200.green_ctx import create_sm_partition, full_device_partition, get_total_sm_count
@@ -447,21 +481,9 @@ def main() -> None:
         # ------------------------------------------------------------ end-to-end (host buffers)
         a_h = a.cpu().pin_memory()
         b_h = b.cpu().pin_memory()
-        c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-        a_d = torch.empty_like(a)
-        b_d = torch.empty_like(b)
-
-        def e2e_step():
-            a_d.copy_(a_h, non_blocking=True)
-            b_d.copy_(b_h, non_blocking=True)
-            c = smm.call_sm_aware(a_d, b_d)
-            c_h.copy_(c, non_blocking=True)
-
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
+        e2e_ms = e2e_pipelined(smm, a_h, b_h, a, b, 2)  # warm-up
         barrier(world)
-        e2e_ms, _ = timed_steps(e2e_step, args.steps, None)
+        e2e_ms = e2e_pipelined(smm, a_h, b_h, a, b, args.steps)
         barrier(world)
     clocks = sampler.summary()
     status = _lib.device_status(local_rank)
@@ -507,7 +529,8 @@ def main() -> None:
                                                       "wave_efficiency")}},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": 2 * M * K * 2,
                 "d2h_bytes_per_step": M * N * 2,
-                "path": "sm_aware_matmul.call_sm_aware with pinned host A, B -> device -> host C"},
+                "path": "sm_aware_matmul.call_sm_aware with pinned host A, B -> device -> host C; the next step's "
+                    "host-to-device copies overlap this step (copy stream, two device buffers)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": UNIT,
                      "frac": round(achieved / peak_tf, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16_tflops (burst)"},
