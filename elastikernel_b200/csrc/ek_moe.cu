@@ -138,25 +138,52 @@ __global__ void __launch_bounds__(kPermChunk)
   __shared__ int s_total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  // Totals per expert and the counts of earlier chunks: every thread takes
+  // a strided share of the [n_chunks][E] count matrix (coalesced, all loads
+  // independent) and adds into shared memory.
   for (int e = tid; e < E; e += blockDim.x) {
-    int tot = 0, before = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int v = chunk_counts[(size_t)c * E + e];
-      tot += v;
-      if (c < (int)blockIdx.x) before += v;
-    }
-    s_tot[e] = tot;
-    s_before[e] = before;
+    s_tot[e] = 0;
+    s_before[e] = 0;
   }
   for (int i = tid; i < 32 * E; i += blockDim.x) s_wcnt[i] = 0;
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < E; ++e) {
-      s_start[e] = acc;
-      acc += (s_tot[e] + block_m - 1) / block_m * block_m;
+  const int n_counts = n_chunks * E;
+#pragma unroll 4
+  for (int i = tid; i < n_counts; i += blockDim.x) {
+    const int v = __ldcg(chunk_counts + i);
+    if (v) {
+      const int c = i / E, e = i - c * E;
+      atomicAdd(&s_tot[e], v);
+      if (c < (int)blockIdx.x) atomicAdd(&s_before[e], v);
     }
-    s_total = acc;
+  }
+  __syncthreads();
+  // Exclusive scan of the padded expert sizes (E <= blockDim): warp scans,
+  // then a scan of the warp totals.
+  __shared__ int s_wsum[32];
+  {
+    const int v = tid < E ? (s_tot[tid] + block_m - 1) / block_m * block_m : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = lane < (int)(blockDim.x >> 5) ? s_wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      s_wsum[lane] = w;
+    }
+    __syncthreads();
+    const int excl = (warp ? s_wsum[warp - 1] : 0) + incl - v;
+    if (tid < E) s_start[tid] = excl;
+    if (tid == (int)blockDim.x - 1) s_total = excl + v;
   }
   __syncthreads();
 
@@ -247,26 +274,41 @@ __global__ void gather_cols_kernel(const int* __restrict__ sorted_slots, const i
 }
 
 // ------------------------------------------------------------------ combine
+// out[t] = sum_j y[t*k + j] in fp32, j in order. One thread per 8 columns of
+// a token; all k <= kMaxK rows are loaded before the sum (kMaxK is the
+// smallest of 2, 4, 8 that holds k; larger k loops).
+__device__ __forceinline__ void add8_bf16(float (&acc)[8], const uint4& v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    acc[2 * i] += f.x;
+    acc[2 * i + 1] += f.y;
+  }
+}
+
+template <int kMaxK>
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ out, int T, int k,
                                int H) {
-  const int chunks = H / 8;
-  const long long total = (long long)T * chunks;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int t = (int)(idx / chunks);
-    const int c = (int)(idx - (long long)t * chunks) * 8;
+  const unsigned chunks = (unsigned)H / 8;
+  const unsigned total = (unsigned)T * chunks;  // < 2^31 (host check), so idx never wraps
+  for (unsigned idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const unsigned t = idx / chunks;
+    const unsigned c = (idx - t * chunks) * 8;
+    const __nv_bfloat16* src = y + (size_t)t * k * H + c;
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + ((size_t)t * k + j) * H + c));
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+    if (k <= kMaxK) {
+      uint4 v[kMaxK];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        acc[2 * i] += f.x;
-        acc[2 * i + 1] += f.y;
-      }
+      for (int j = 0; j < kMaxK; ++j)
+        if (j < k) v[j] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)j * H));
+#pragma unroll
+      for (int j = 0; j < kMaxK; ++j)
+        if (j < k) add8_bf16(acc, v[j]);
+    } else {
+      for (int j = 0; j < k; ++j) add8_bf16(acc, __ldg(reinterpret_cast<const uint4*>(src + (size_t)j * H)));
     }
     uint4 o;
     __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -666,10 +708,18 @@ int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* strea
   if (T == 0) return EK_OK;
   if (!y || !out || !aligned16(y) || !aligned16(out)) return set_error(EK_ERR_INVALID, "combine: bad pointers");
   const long long work = (long long)T * (H / 8);
+  if (work >= (1ll << 31)) return set_error(EK_ERR_INVALID, "combine: too many rows (T=%d, H=%d)", T, H);
   const int threads = 256;
   const int blocks = (int)std::min<long long>((work + threads - 1) / threads, 148LL * 16);
-  combine_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(out), T, topk, H);
+  const auto* yb = static_cast<const __nv_bfloat16*>(y);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (topk <= 2)
+    combine_kernel<2><<<blocks, threads, 0, s>>>(yb, ob, T, topk, H);
+  else if (topk <= 4)
+    combine_kernel<4><<<blocks, threads, 0, s>>>(yb, ob, T, topk, H);
+  else
+    combine_kernel<8><<<blocks, threads, 0, s>>>(yb, ob, T, topk, H);
   return check_cuda(cudaGetLastError(), "combine launch");
 }
 

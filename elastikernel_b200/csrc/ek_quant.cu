@@ -145,57 +145,130 @@ __device__ __forceinline__ void load8(const void* x, int dt, size_t i, float (&v
   }
 }
 
+// Two codes per conversion (the low byte holds the first value).
+__device__ __forceinline__ uint32_t pack2_e4m3(float a, float b) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+
 __device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float s) {
   uint2 r;
-  r.x = (uint32_t)to_e4m3(v[0] / s) | ((uint32_t)to_e4m3(v[1] / s) << 8) | ((uint32_t)to_e4m3(v[2] / s) << 16) |
-        ((uint32_t)to_e4m3(v[3] / s) << 24);
-  r.y = (uint32_t)to_e4m3(v[4] / s) | ((uint32_t)to_e4m3(v[5] / s) << 8) | ((uint32_t)to_e4m3(v[6] / s) << 16) |
-        ((uint32_t)to_e4m3(v[7] / s) << 24);
+  r.x = pack2_e4m3(v[0] / s, v[1] / s) | (pack2_e4m3(v[2] / s, v[3] / s) << 16);
+  r.y = pack2_e4m3(v[4] / s, v[5] / s) | (pack2_e4m3(v[6] / s, v[7] / s) << 16);
   return r;
 }
 
-// 1 x 128 groups, rows a multiple of 8 elements long: a half-warp per group,
-// eight elements (one 16-byte load, one 8-byte store) per lane, two groups
-// per half-warp in flight. Scales as quant_groups_kernel.
-__global__ void quant_groups_vec_kernel(const void* __restrict__ x, int dt, int rows, int cols,
-                                        uint8_t* __restrict__ q, float* __restrict__ scales, int kmajor) {
-  const int groups = (cols + 127) / 128;
-  const long long total = (long long)rows * groups;
-  const int hl = threadIdx.x & 15;  // lane within the half-warp
-  const int half = (threadIdx.x >> 4) & 1;
-  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
-  // the loop bound is uniform across the warp, so every lane reaches the shuffles
-  for (long long wb = (((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2; wb < total; wb += 4 * nwarps) {
-    const long long gid[2] = {wb + half, wb + 2 * nwarps + half};
-    float v[2][8];
-    bool ok[2];
+// 1 x 128 groups, rows a multiple of 8 elements long. A work item is one row
+// and a run of 2 * kU consecutive groups of it; a warp takes one item at a
+// time (grid-stride), a half-warp one group, eight elements per lane (one
+// 16-byte bf16 load or two fp32 loads, one 8-byte store). The raw loads of
+// the warp's next item are issued before the current item is reduced and
+// stored, so a warp keeps its loads in flight while it computes. Scales as
+// quant_groups_kernel.
+constexpr int kGroupPairs = 4;  // kU: group pairs per warp item
+
+template <bool kF32>
+struct Raw8 {
+  uint4 w[kF32 ? 2 : 1];
+};
+
+template <bool kF32>
+__device__ __forceinline__ void load_raw8(const void* x, size_t i, Raw8<kF32>& r) {
+  if constexpr (kF32) {
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(x) + i);
+    r.w[0] = __ldg(p);
+    r.w[1] = __ldg(p + 1);
+  } else {
+    r.w[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + i));
+  }
+}
+
+template <bool kF32>
+__device__ __forceinline__ void unpack8(const Raw8<kF32>& r, float (&v)[8]) {
+  if constexpr (kF32) {
+    v[0] = __uint_as_float(r.w[0].x); v[1] = __uint_as_float(r.w[0].y);
+    v[2] = __uint_as_float(r.w[0].z); v[3] = __uint_as_float(r.w[0].w);
+    v[4] = __uint_as_float(r.w[1].x); v[5] = __uint_as_float(r.w[1].y);
+    v[6] = __uint_as_float(r.w[1].z); v[7] = __uint_as_float(r.w[1].w);
+  } else {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r.w[0]);
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      ok[u] = gid[u] < total;
-      const int row = ok[u] ? (int)(gid[u] / groups) : 0, g = ok[u] ? (int)(gid[u] % groups) : 0;
-      const int c0 = g * 128 + hl * 8;
-      if (ok[u] && c0 < cols) {
-        load8(x, dt, (size_t)row * cols + c0, v[u]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      float amax = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[u][j]));
-#pragma unroll
-      for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (!ok[u]) continue;
-      const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
-      const int row = (int)(gid[u] / groups), g = (int)(gid[u] % groups);
-      const int c0 = g * 128 + hl * 8;
-      if (c0 < cols) *reinterpret_cast<uint2*>(q + (size_t)row * cols + c0) = pack8_e4m3(v[u], s);
-      if (hl == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)gid[u]] = s;
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
     }
   }
+}
+
+template <int kU, bool kF32>
+__global__ void __launch_bounds__(256) quant_groups_vec_kernel(const void* __restrict__ x, int rows, int cols,
+                                                               uint8_t* __restrict__ q, float* __restrict__ scales,
+                                                               int kmajor) {
+  const int groups = (cols + 127) / 128;
+  const unsigned parts = (unsigned)(groups + 2 * kU - 1) / (2 * kU);  // items per row
+  const unsigned items = (unsigned)rows * parts;                       // < 2^31 (host check)
+  const int hl = threadIdx.x & 15;                                     // lane within the half-warp
+  const int half = (threadIdx.x >> 4) & 1;
+  const unsigned nwarps = (gridDim.x * blockDim.x) >> 5;
+  Raw8<kF32> raw[kU];
+  auto issue = [&](unsigned it) {
+    const int row = (int)(it / parts);
+    const int g0 = (int)(it - (unsigned)row * parts) * 2 * kU + half;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c0 = (g0 + 2 * u) * 128 + hl * 8;
+      if (c0 < cols) load_raw8<kF32>(x, (size_t)row * cols + c0, raw[u]);
+    }
+  };
+  unsigned it = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (it < items) issue(it);
+  // the loop bound is uniform across the warp, so every lane reaches the shuffles
+  for (; it < items; it += nwarps) {
+    const int row = (int)(it / parts);
+    const int g0 = (int)(it - (unsigned)row * parts) * 2 * kU + half;  // this half-warp's first group
+    const size_t base = (size_t)row * cols;
+    Raw8<kF32> cur[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) cur[u] = raw[u];
+    if (it + nwarps < items) issue(it + nwarps);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c0 = (g0 + 2 * u) * 128 + hl * 8;
+      float v[8];
+      if (c0 < cols) {
+        unpack8<kF32>(cur[u], v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+      for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (c0 >= cols) continue;  // past the row (group >= groups)
+      const int g = g0 + 2 * u;
+      const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+      *reinterpret_cast<uint2*>(q + base + c0) = pack8_e4m3(v, s);
+      if (hl == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)row * groups + g] = s;
+    }
+  }
+}
+
+static int launch_groups_vec(const void* x, int dt, int rows, int cols, uint8_t* q, float* scales, int kmajor,
+                             cudaStream_t s) {
+  const long long groups = (cols + 127) / 128;
+  const long long items = (long long)rows * ((groups + 2 * kGroupPairs - 1) / (2 * kGroupPairs));
+  if (items >= (1ll << 30)) return set_error(EK_ERR_INVALID, "quant: too many rows (%d)", rows);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned blocks = (unsigned)std::max<long long>(std::min<long long>((items + 7) / 8, (long long)sms * 8), 1);
+  if (dt == 0)
+    quant_groups_vec_kernel<kGroupPairs, false><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor);
+  else
+    quant_groups_vec_kernel<kGroupPairs, true><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor);
+  return EK_OK;
 }
 
 // 128 x 128 blocks of a matrix whose rows are a multiple of 8 elements long:
@@ -259,10 +332,8 @@ int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows
                                                                       static_cast<uint8_t*>(q), scales);
   } else if (br == 1 && bc == 128) {
     if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
-      const long long halves = (long long)rows * ((cols + 127) / 128);
-      const long long blocks = std::min<long long>((halves + 31) / 32, 148LL * 32);
-      quant_groups_vec_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, s>>>(
-          x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales, 0);
+      const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales, 0, s);
+      if (rc) return rc;
     } else {
       const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
       quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
@@ -291,10 +362,8 @@ int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q
   if (rows == 0) return EK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
-    const long long halves = (long long)rows * ((cols + 127) / 128);
-    const long long blocks = std::min<long long>((halves + 31) / 32, 148LL * 32);
-    quant_groups_vec_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, s>>>(
-        x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1);
+    const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1, s);
+    if (rc) return rc;
   } else {
     const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
     quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,

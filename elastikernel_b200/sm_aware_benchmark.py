@@ -226,6 +226,82 @@ def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256) -> None:
     torch.cuda.synchronize()
 
 
+HBM_SPEC_GBS = 8000.0  # B200 HBM3e spec-sheet bandwidth
+
+
+def run_stages(tokens: int, experts: int, topk: int, hidden: int, inter: int = 2048, reps: int = 20) -> list:
+    """Time the memory-bound MoE stages one by one -- routing, permutation
+    (count + stable scatter), row gather, e4m3 quantisation of the token rows
+    and of the activations (1 x 128 groups) and top-k combine -- at `tokens`
+    tokens, with their algorithmic bytes and GB/s (L2 flushed before each
+    repetition)."""
+    import torch
+
+    from . import _ops
+    from .timing import time_on_stream
+
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(42)
+    T, E, k, H = tokens, experts, topk, hidden
+    logits = torch.randn((T, E), device=dev, generator=g)
+    x = torch.randn((T, H), device=dev, generator=g).to(torch.bfloat16)
+    y = torch.randn((T * k, H), device=dev, generator=g).to(torch.bfloat16)
+    act = torch.randn((T * k, inter), device=dev, generator=g).to(torch.bfloat16)
+    ids, _ = _ops.moe_route(logits, k)
+    perm = _ops.moe_permute(ids, E, x)
+    used = int(perm["num_rows_padded"].item())
+    slots = T * k
+    stages = [
+        ("route", lambda: _ops.moe_route(logits, k), T * E * 4 + slots * 8),
+        ("permute", lambda: _ops.moe_permute(ids, E), slots * 4 + perm["max_rows"] * 4),
+        ("permute+gather", lambda: _ops.moe_permute(ids, E, x), slots * 4 + perm["max_rows"] * 4 + 2 * slots * H * 2),
+        ("quant tokens", lambda: _ops.quant_e4m3(x, block=(1, 128)), T * H * 3 + T * (H // 128) * 4),
+        ("quant act", lambda: _ops.quant_e4m3_kmajor(act), slots * inter * 3 + slots * (inter // 128) * 4),
+        ("combine", lambda: _ops.moe_combine(y, T, k), slots * H * 2 + T * H * 2),
+    ]
+    print(f"MoE stages: T={T}, E={E}, top-{k}, H={H}, I={inter} (bf16 rows; {used} padded rows)")
+    print(f"  {'stage':<16} {'us':>9} {'MB':>9} {'GB/s':>8} {'% 8TB/s':>8}")
+    out = []
+    for name, fn, nbytes in stages:
+        for _ in range(3):
+            fn()
+        r = time_on_stream(fn, reps=reps)
+        us = r["median_ms"] * 1e3
+        gbs = nbytes / (us * 1e-6) / 1e9
+        print(f"  {name:<16} {us:>9.1f} {nbytes / 1e6:>9.1f} {gbs:>8.0f} {100 * gbs / HBM_SPEC_GBS:>7.1f}%")
+        out.append({"stage": name, "us": us, "bytes": nbytes, "gbs": gbs})
+    return out
+
+
+def run_gemm_shape(M: int, N: int, K: int, dtype: str = "bf16", sm_count: int = 0, reps: int = 3) -> None:
+    """Run one GEMM shape a few times in a partition of `sm_count` SMs (0: the
+    whole device); bf16 is A[M,K] @ B[K,N], fp8 is e4m3 A[M,K] x W[N,K]^T with
+    per-row / per-channel scales (a fixed launch sequence for profilers)."""
+    import torch
+
+    from . import _ops
+    from . import sm_aware_matmul as smm
+    from .green_ctx import get_total_sm_count
+
+    dev = torch.device("cuda:0")
+    total = get_total_sm_count(dev)
+    stream, actual = _partition(dev, sm_count or total, total)
+    g = torch.Generator(device=dev).manual_seed(0)
+    with torch.cuda.stream(stream):
+        if dtype == "fp8":
+            aq, a_s = _ops.quant_e4m3(torch.randn((M, K), device=dev, generator=g))
+            wq, w_s = _ops.quant_e4m3(torch.randn((N, K), device=dev, generator=g))
+            fn = lambda: _ops.gemm_fp8(aq, wq, a_s, w_s)  # noqa: E731
+        else:
+            a = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+            b = torch.randn((K, N), device=dev, generator=g).to(torch.bfloat16)
+            fn = lambda: smm.call_sm_aware(a, b, actual)  # noqa: E731
+        for _ in range(reps):
+            fn()
+    torch.cuda.synchronize()
+    print(f"GEMM {dtype} {M}x{N}x{K} on {actual} SMs: {reps} launches")
+
+
 def main():
     parser = argparse.ArgumentParser(description="SM-Aware Kernel Benchmark")
     parser.add_argument("--gemm", action="store_true", help="Benchmark GEMM")
@@ -238,9 +314,22 @@ def main():
     parser.add_argument("--fp8-layer-tokens", type=int, default=0,
                         help="only run the DeepSeek-V3-shaped e4m3 MoE layer at this token count (for profiling)")
     parser.add_argument("--experts", type=int, default=256,
-                        help="experts on this GPU for --fp8-layer-tokens (fewer experts: a smaller capture)")
+                        help="experts on this GPU for --fp8-layer-tokens / --stages-tokens")
+    parser.add_argument("--stages-tokens", type=int, default=0,
+                        help="time routing, permutation, gather and combine at this token count")
+    parser.add_argument("--topk", type=int, default=8, help="top-k for --stages-tokens")
+    parser.add_argument("--hidden", type=int, default=7168, help="hidden size for --stages-tokens")
+    parser.add_argument("--inter", type=int, default=2048, help="expert intermediate size for --stages-tokens")
+    parser.add_argument("--gemm-shape", type=int, nargs=3, metavar=("M", "N", "K"),
+                        help="only run this GEMM shape --reps times (for profiling)")
+    parser.add_argument("--dtype", choices=["bf16", "fp8"], default="bf16", help="dtype for --gemm-shape")
+    parser.add_argument("--sms", type=int, default=0, help="partition size for --gemm-shape (0: whole device)")
     args = parser.parse_args()
-    if args.fp8_layer_tokens > 0:
+    if args.stages_tokens > 0:
+        run_stages(args.stages_tokens, args.experts, args.topk, args.hidden, args.inter, args.reps)
+    elif args.gemm_shape:
+        run_gemm_shape(*args.gemm_shape, dtype=args.dtype, sm_count=args.sms, reps=args.reps)
+    elif args.fp8_layer_tokens > 0:
         run_layer_fp8(args.fp8_layer_tokens, args.reps, args.experts)
     elif args.layer_tokens > 0:
         run_layer(args.layer_tokens, args.reps, layout=args.layout)

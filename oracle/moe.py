@@ -3,6 +3,7 @@
 * route_ref      softmax -> top-k -> renormalise      sm_aware_agent/definition.py:152-153
 * permute_ref    moe_align_block_size-style layout    (no reference code: defined here)
 * moe_ref        SwiGLU experts + weighted combine    sm_aware_agent/definition.py:155-170
+* combine_ref    top-k sum of weighted expert rows     sm_aware_agent/definition.py:168 (sum over choices)
 * moe_loop_ref   the definition's literal per-token loop in torch (CPU baseline)
 * moe_vec_ref    vectorised per-expert torch restatement (CPU baseline at all T)
 
@@ -103,6 +104,17 @@ def moe_ref(x, logits, w1, w2, w3, topk: int, ids=None, weights=None) -> np.ndar
         wt = weights[t_idx, j_idx][:, None]
         np.add.at(out, t_idx, wt * y)
     return out
+
+
+def combine_ref(y, T: int, topk: int) -> torch.Tensor:
+    """bf16 [T, H]: out[t] = sum_j y[t*k + j], accumulated in fp32 in j order
+    (the per-choice sum of definition.py:168 over rows that already carry
+    their routing weight), rounded once to bf16."""
+    Y = to_f32(y).reshape(T, topk, -1)
+    acc = np.zeros((T, Y.shape[2]), dtype=np.float32)
+    for j in range(topk):
+        acc = acc + Y[:, j]
+    return torch.from_numpy(acc).to(torch.bfloat16)
 
 
 def moe_loop_ref(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1, w2, w3, topk: int) -> torch.Tensor:

@@ -46,6 +46,29 @@ def test_quant_blocks_bit_exact(cuda_dev, block, dtype, shape):
     assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
 
 
+@pytest.mark.parametrize("rows,cols", [(512, 7168), (257, 1032), (1, 2048), (3, 8)])
+def test_quant_groups_wide_range(cuda_dev, rows, cols):
+    """1 x 128 group quantisation over 60 decades of group magnitude, with
+    subnormal elements and all-zero groups, row-major and K-block-major
+    scales, bit for bit against the oracle."""
+    from elastikernel_b200 import _ops
+
+    g = torch.Generator().manual_seed(rows + cols)
+    groups = -(-cols // 128)
+    mag = torch.pow(10.0, torch.empty((rows, groups)).uniform_(-30, 30, generator=g))
+    x = torch.randn((rows, groups * 128), generator=g) * mag.repeat_interleave(128, dim=1)
+    x[torch.rand(x.shape, generator=g) < 0.01] = 1e-39  # subnormal elements
+    x[:, :128][torch.rand(rows, generator=g) < 0.1] = 0.0  # all-zero first groups
+    x = x[:, :cols].contiguous().to(torch.bfloat16)
+    rq, rs = of8.quant_blocks(x, 1, 128)
+    q, s = _ops.quant_e4m3(x.to(cuda_dev), block=(1, 128))
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+    qk, sk = _ops.quant_e4m3_kmajor(x.to(cuda_dev))
+    np.testing.assert_array_equal(sk.cpu().numpy(), rs.T)
+    assert torch.equal(qk.cpu().view(torch.uint8), rq.view(torch.uint8))
+
+
 def _fp8_operands(M, N, K, dev, seed):
     from elastikernel_b200 import _ops
 

@@ -53,7 +53,8 @@ def test_route_golden_and_ties(cuda_dev):
     np.testing.assert_array_equal(rids, [[0, 1], [3, 35], [7, 39], [0, 1]])
 
 
-@pytest.mark.parametrize("T,E,k", [(4096, 8, 2), (1, 8, 2), (3000, 256, 8), (17, 4, 4), (2500, 64, 3)])
+@pytest.mark.parametrize("T,E,k", [(4096, 8, 2), (1, 8, 2), (3000, 256, 8), (17, 4, 4), (2500, 64, 3),
+                                   (16384, 256, 8), (2048, 1024, 8), (20000, 8, 2)])
 def test_permute_bit_exact(cuda_dev, T, E, k):
     from elastikernel_b200 import _ops
 
@@ -73,6 +74,18 @@ def test_permute_bit_exact(cuda_dev, T, E, k):
     got = perm["x_perm"][:n].cpu()[torch.from_numpy(used)]
     want = x[torch.from_numpy(slots[used] // k).long()]
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("T,k,H", [(4096, 8, 7168), (333, 2, 4096), (1, 1, 8), (64, 12, 520)])
+def test_combine_bit_exact(cuda_dev, T, k, H):
+    """Top-k combine: fp32 sum in choice order, one bf16 rounding (k = 12
+    takes the kernel's path for more than eight choices)."""
+    from elastikernel_b200 import _ops
+
+    g = torch.Generator().manual_seed(T + k + H)
+    y = torch.randn((T * k, H), generator=g).to(torch.bfloat16)
+    out = _ops.moe_combine(y.to(cuda_dev), T, k)
+    assert torch.equal(out.cpu(), om.combine_ref(y, T, k))
 
 
 def _moe_inputs(T, H, I, E, seed):
