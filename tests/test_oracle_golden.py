@@ -114,3 +114,22 @@ def test_permute_ref_layout():
     assert r["block_expert"][:3].tolist() == [0, 1, 3]
     assert (r["block_expert"][3:] == -1).all()
     assert len(r["sorted_slots"]) == om.max_padded_rows(4, 2, 4, 4)
+
+
+def test_combine_ref_sums_weighted_slots_to_reference():
+    """Per-slot weighted expert rows summed by combine_ref give the
+    reference operator's output (bf16 rounding of the sum only)."""
+    z = np.load(GOLD / "moe_def.npz")
+    x, logits = z["a_x"].astype(np.float32), z["a_logits"]
+    w1, w2, w3, k = z["a_w1"], z["a_w2"], z["a_w3"], int(z["a_k"])
+    ids, wts = om.route_ref(logits, k)
+    T = x.shape[0]
+    y = np.zeros((T * k, x.shape[1]), dtype=np.float32)
+    for t in range(T):
+        for j in range(k):
+            e = ids[t, j]
+            h = x[t]
+            a = (h @ w1[e].T) / (1 + np.exp(-(h @ w1[e].T))) * (h @ w3[e].T)
+            y[t * k + j] = wts[t, j] * (a @ w2[e].T)
+    out = om.combine_ref(torch.from_numpy(y), T, k)
+    assert og.max_rel_err(out.float().numpy(), z["a_out"]) < 1e-2
