@@ -83,8 +83,9 @@ _SIGNATURES = {
                                 _c_int, _c_int, _c_vp]),
     "ek_moe_down": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
                              _c_int, _c_int, _c_int, _c_int, _c_vp]),
-    "ek_moe_gate_up_packed": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp] + [_c_int] * 7 + [_c_vp]),
-    "ek_moe_down_packed": (_c_int, [_c_vp] * 6 + [_c_int] * 9 + [_c_vp]),
+    "ek_moe_gate_up_packed": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp] + [_c_int] * 7 + [_c_vp, _c_size, _c_vp]),
+    "ek_moe_down_packed": (_c_int, [_c_vp] * 6 + [_c_int] * 9 + [_c_vp, _c_size, _c_vp]),
+    "ek_moe_packed_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
     "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_gate_up_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 7 + [_c_vp]),
     "ek_moe_down_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 9 + [_c_vp]),

@@ -334,8 +334,9 @@ def moe_down(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torc
 
 
 def moe_gate_up_packed(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: int | None = None,
-                       tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
-    """Swapped-operand gate/up over the packed layout (permute with block_m=1)."""
+                       tok_tile: int = 0, pair: int = -1, ksplit: bool = True) -> torch.Tensor:
+    """Swapped-operand gate/up over the packed layout (permute with block_m=1).
+    ksplit=False withholds the workspace, so K is never split."""
     x_perm = perm["x_perm"]
     dev = _require_cuda(x_perm, w1, w3)
     for n, t in (("x_perm", x_perm), ("w1", w1), ("w3", w3)):
@@ -347,17 +348,26 @@ def moe_gate_up_packed(perm: dict, w1: torch.Tensor, w3: torch.Tensor, num_sms: 
         raise RuntimeError("gate_up_packed: shape mismatch")
     rows = perm["max_rows"]
     act = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
+    ws, nb = _packed_workspace(rows, H, I, dev) if ksplit else (None, 0)
     with _on_device(dev):
         check(lib().ek_moe_gate_up_packed(x_perm.data_ptr(), w1.data_ptr(), w3.data_ptr(),
                                           perm["expert_counts"].data_ptr(), act.data_ptr(), rows, E, H, I,
-                                          int(tok_tile), int(pair), int(num_sms or 0), current_stream_handle(dev)),
-              "ek_moe_gate_up_packed")
+                                          int(tok_tile), int(pair), int(num_sms or 0), _ptr(ws), nb,
+                                          current_stream_handle(dev)), "ek_moe_gate_up_packed")
     return act
 
 
+def _packed_workspace(rows: int, H: int, I: int, dev: torch.device) -> tuple[torch.Tensor | None, int]:
+    """Workspace of the packed GEMMs' K-split (None where the size never splits)."""
+    nb = int(lib().ek_moe_packed_workspace_bytes(int(rows), int(H), int(I)))
+    return (torch.empty(nb, dtype=torch.uint8, device=dev) if nb else None), nb
+
+
 def moe_down_packed(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
-                    num_sms: int | None = None, tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
-    """Swapped-operand down projection with the routing weight, scattered to slots."""
+                    num_sms: int | None = None, tok_tile: int = 0, pair: int = -1,
+                    ksplit: bool = True) -> torch.Tensor:
+    """Swapped-operand down projection with the routing weight, scattered to slots.
+    ksplit=False withholds the workspace, so K is never split."""
     dev = _require_cuda(act, w2, topk_weights)
     _check_bf16("act", act)
     _check_bf16("w2", w2)
@@ -367,11 +377,13 @@ def moe_down_packed(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weight
     if act.shape[1] != I or E != perm["E"] or topk_weights.numel() != T * k or perm["block_m"] != 1:
         raise RuntimeError("down_packed: shape mismatch")
     y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    ws, nb = _packed_workspace(perm["max_rows"], H, I, dev) if ksplit else (None, 0)
     with _on_device(dev):
         check(lib().ek_moe_down_packed(act.data_ptr(), w2.data_ptr(), perm["expert_counts"].data_ptr(),
                                        perm["sorted_slots"].data_ptr(), topk_weights.data_ptr(), y.data_ptr(),
                                        perm["max_rows"], E, H, I, T, k, int(tok_tile), int(pair),
-                                       int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_packed")
+                                       int(num_sms or 0), _ptr(ws), nb, current_stream_handle(dev)),
+              "ek_moe_down_packed")
     return y
 
 

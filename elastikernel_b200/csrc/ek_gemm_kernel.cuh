@@ -154,8 +154,9 @@ struct Unit {
 
 // Shared state of the swapped schedule, filled once per CTA.
 struct ExpertTables {
-  int* start;   // [E + 1] first packed row of each expert
-  int* tprefix; // [E + 1] prefix of units per expert
+  int* start;      // [E + 1] first packed row of each expert
+  int* tprefix;    // [E + 1] prefix of units per expert
+  int ksplit = 1;  // K slices per (feature tile, token tile)
 };
 
 __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
@@ -166,6 +167,27 @@ __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int g
   const int r = tile - g * group_size;
   tm = first_m + r % gm;
   tn = r / gm;
+}
+
+// K-split of the swapped schedule when its units fill the CTAs (or pairs)
+// poorly, as with a few experts hit at small token counts: the split count
+// s <= max_split that minimises rounds(s) x (K blocks per slice + overhead),
+// rounds(s) = ceil(units * s / ctas), with at least 8 K blocks per slice.
+// Every CTA computes the same value from the same expert counts.
+__host__ __device__ __forceinline__ int swapped_ksplit(int units, int ctas, int k_blocks, int max_split) {
+  constexpr float kUnitOverheadKb = 4.f;  // per-unit fill / drain, in K blocks
+  if (max_split <= 1 || units <= 0 || ctas <= 0) return 1;
+  int best_s = 1;
+  float best = (float)((units + ctas - 1) / ctas) * ((float)k_blocks + kUnitOverheadKb);
+  for (int s = 2; s <= max_split && k_blocks / s >= 8; ++s) {
+    const long long us = (long long)units * s;
+    const float c = (float)((us + ctas - 1) / ctas) * ((float)k_blocks / s + kUnitOverheadKb);
+    if (c < 0.97f * best) {
+      best = c;
+      best_s = s;
+    }
+  }
+  return best_s;
 }
 
 template <class Cfg>
@@ -239,7 +261,15 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     const int cnt = xt.start[e + 1] - xt.start[e];
     const int ttiles = (cnt + Cfg::BN - 1) / Cfg::BN;
     const int j = r % ttiles;  // token tile (fastest: tiles sharing a weight tile run together)
-    const int f = r / ttiles;  // feature tile
+    const int rs = r / ttiles;
+    const int f = rs / xt.ksplit;  // feature tile
+    if (xt.ksplit > 1) {
+      // K slice of a split schedule: its fp32 partial goes to the workspace
+      w.split = rs - f * xt.ksplit;
+      w.nsplit = xt.ksplit;
+      w.kb0 = (int)((long long)w.split * p.k_blocks / w.nsplit);
+      w.kb1 = (int)((long long)(w.split + 1) * p.k_blocks / w.nsplit);
+    }
     // the expert's tokens are split evenly over its tiles and the MMA N is
     // shrunk to the tokens present (a multiple of 16 per CTA of the pair)
     const int per = (cnt + ttiles - 1) / ttiles;
@@ -348,6 +378,7 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem_base + 1);
   volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem_base + 2);
+  volatile int* s_ksplit = reinterpret_cast<volatile int*>(s_tmem_base + 3);
   ExpertTables xt{reinterpret_cast<int*>(sX), reinterpret_cast<int*>(sX) + (kMaxExpertsT + 1)};
   int* s_slot = reinterpret_cast<int*>(sX) + 2 * (kMaxExpertsT + 1);  // [BN]
   float* s_wt = reinterpret_cast<float*>(s_slot + BN);                 // [BN]
@@ -374,17 +405,26 @@ __global__ void __launch_bounds__(192, 1)
     *s_last = 0;
     fence_mbar_init();
     if constexpr (Cfg::kSwapped) {
-      // packed starts and unit prefix per expert (units = feature tiles x token tiles)
+      // packed starts and unit prefix per expert (units = feature tiles x
+      // token tiles x K slices)
       int acc = 0, units = 0;
       for (int e = 0; e < p.num_experts; ++e) {
         const int c = max(0, p.expert_counts[e]);
         xt.start[e] = acc;
-        xt.tprefix[e] = units;
         acc += c;
         units += p.feat_tiles * ((c + BN - 1) / BN);
       }
       xt.start[p.num_experts] = acc;
+      const int S = swapped_ksplit(units, unit_step, p.k_blocks, p.tail_split);
+      units = 0;
+      for (int e = 0; e < p.num_experts; ++e) {
+        xt.tprefix[e] = units;
+        units += p.feat_tiles * ((xt.start[e + 1] - xt.start[e] + BN - 1) / BN) * S;
+      }
       xt.tprefix[p.num_experts] = units;
+      *s_ksplit = S;
+      // the split count for the kernels that reduce the slices (1: nothing to reduce)
+      if (p.tail_split > 1 && blockIdx.x == 0) p.ws_counters[0] = S;
     }
   }
   if (warp == 1) {
@@ -396,6 +436,7 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (Cfg::kPair) cluster_sync();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem_base;
+  if constexpr (Cfg::kSwapped) xt.ksplit = *s_ksplit;
 
   int rows_rt = p.M;
   int nunits = p.num_units;
@@ -583,6 +624,26 @@ __global__ void __launch_bounds__(192, 1)
         const int col = w.c_col + feat;
         const int nch = (w.n_eff + CH - 1) / CH;
         __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+        if (w.nsplit > 1) {
+          // K slice: raw fp32 gate / up sums to part[slice][token row][gate I | up I]
+          float* part = p.ws_partial + (size_t)w.split * p.M * (2 * p.N) + (is_gate ? 0 : p.N) + col;
+#pragma unroll 1
+          for (int c = 0; c < nch; ++c) {
+            uint32_t r[32];
+            tmem_ld_chunk<Cfg>(t_row + c * CH, r);
+            tmem_ld_wait(r);
+            if (c == nch - 1) release_tmem(buf);
+            if (col < p.N) {
+#pragma unroll
+              for (int t = 0; t < CH; ++t) {
+                const int tr = w.tok0 + c * CH + t;
+                if (tr < w.row_end) part[(size_t)tr * (2 * p.N)] = __uint_as_float(r[t]);
+              }
+            }
+          }
+          ++acc_i;  // as at the end of the loop body
+          continue;
+        }
 #pragma unroll 1
         for (int c = 0; c < nch; ++c) {
           uint32_t r[32];
@@ -612,13 +673,23 @@ __global__ void __launch_bounds__(192, 1)
         const int col = w.c_col + row_in_tile;
         const int nch = (w.n_eff + CH - 1) / CH;
         __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+        // K slice: weighted fp32 partials to part[slice][slot][feature]
+        float* part = w.nsplit > 1 ? p.ws_partial + (size_t)w.split * p.num_slots * p.N + col : nullptr;
 #pragma unroll 1
         for (int c = 0; c < nch; ++c) {
           uint32_t r[32];
           tmem_ld_chunk<Cfg>(t_row + c * CH, r);
           tmem_ld_wait(r);
           if (c == nch - 1) release_tmem(buf);
-          if (col < p.N) {
+          if (part != nullptr) {
+            if (col < p.N) {
+#pragma unroll
+              for (int t = 0; t < CH; ++t) {
+                const int slot = s_slot[c * CH + t];
+                if (slot >= 0) part[(size_t)slot * p.N] = __uint_as_float(r[t]) * s_wt[c * CH + t];
+              }
+            }
+          } else if (col < p.N) {
 #pragma unroll
             for (int t = 0; t < CH; ++t) {
               const int slot = s_slot[c * CH + t];

@@ -318,6 +318,63 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, __nv_bfloat1
   }
 }
 
+// ------------------------------------------------------------------ K-split reduction (packed GEMMs)
+// A packed GEMM that split K (small token counts, few experts hit) leaves
+// fp32 slice sums in the workspace; these kernels add the slices in slice
+// order and finish the epilogue. hdr[0] is the split the GEMM chose (1: the
+// GEMM wrote its output itself and there is nothing to do).
+constexpr int kSplitMaxRows = 64;   // packed rows (T * topk) up to which the GEMMs may split K
+constexpr int kSplitMax = 4;        // K slices at most
+constexpr size_t kSplitHeader = 256;
+
+__global__ void split_swiglu_kernel(const float* __restrict__ part, const int* __restrict__ hdr, int rows, int I,
+                                    __nv_bfloat16* __restrict__ act) {
+  const int S = *hdr;
+  if (S <= 1) return;
+  const size_t slice = (size_t)rows * 2 * I;
+  const int n = rows * I;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int r = i / I, f = i - r * I;
+    const float* g = part + (size_t)r * 2 * I + f;
+    float gs = 0.f, us = 0.f;
+    for (int sl = 0; sl < S; ++sl) {
+      gs += g[sl * slice];
+      us += g[sl * slice + I];
+    }
+    act[i] = __float2bfloat16_rn(silu_f(gs) * us);
+  }
+}
+
+__global__ void split_sum_kernel(const float* __restrict__ part, const int* __restrict__ hdr, int n,
+                                 __nv_bfloat16* __restrict__ out) {
+  const int S = *hdr;
+  if (S <= 1) return;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int sl = 0; sl < S; ++sl) acc += part[(size_t)sl * n + i];
+    out[i] = __float2bfloat16_rn(acc);
+  }
+}
+
+size_t split_workspace_bytes(int rows, int H, int I) {
+  if (rows <= 0 || rows > kSplitMaxRows || H <= 0 || I <= 0) return 0;
+  return kSplitHeader + (size_t)kSplitMax * rows * std::max(2 * I, H) * sizeof(float);
+}
+
+// Whether the packed GEMM is expected to split K: the kernel's own choice
+// (swapped_ksplit) for the units a uniform routing gives on average,
+// about E (1 - (1 - 1/E)^rows) experts hit by `rows` routed slots. Where it
+// is not, no workspace is handed over and the reduction launch is skipped;
+// where it is, the kernel still decides from the actual expert counts.
+bool split_expected(int rows, int E, int tok, int ctas, int S_sms, int feat_tiles, int k_blocks) {
+  if (rows <= 0 || E < 1) return false;
+  const double hit = std::max(1.0, std::min((double)E, E * (1.0 - std::pow(1.0 - 1.0 / E, (double)rows))));
+  const int experts = (int)std::lround(hit);
+  const int per = (rows + experts - 1) / experts;
+  const int units = experts * feat_tiles * ((per + tok - 1) / tok);
+  return swapped_ksplit(units, std::max(1, S_sms / ctas), k_blocks, kSplitMax) > 1;
+}
+
 // ------------------------------------------------------------------ grouped GEMM launch
 template <class Cfg>
 int launch_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& prm,
@@ -595,7 +652,8 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
 }
 
 int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, const int* expert_counts, void* act,
-                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* stream) {
+                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* workspace,
+                          size_t workspace_bytes, void* stream) {
   clear_error();
   if (!x_perm || !w1 || !w3 || !expert_counts || !act) return set_error(EK_ERR_INVALID, "gate_up_packed: null pointer");
   if (rows < 0 || E < 1 || E > kMaxExpertsT || H % 16 != 0 || I % 8 != 0 || H <= 0 || I <= 0)
@@ -627,15 +685,28 @@ int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, co
   p.expert_counts = expert_counts;
   p.w_rows_per_expert = I;
   p.feat_tiles = (I + 64 * ctas - 1) / (64 * ctas);
+  const size_t need = split_workspace_bytes(rows, H, I);
+  const bool may_split = need > 0 && workspace != nullptr && workspace_bytes >= need && aligned16(workspace) &&
+                         split_expected(rows, E, tok, ctas, S, p.feat_tiles, p.k_blocks);
+  if (may_split) {
+    p.tail_split = kSplitMax;
+    p.ws_counters = static_cast<int*>(workspace);
+    p.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kSplitHeader);
+  }
   const int grid = std::max(1, S / ctas) * ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (pr) return launch_packed_tok<kEpiSwiGLUT, true>(tok, ta, tb, tx, p, grid, s);
-  return launch_packed_tok<kEpiSwiGLUT, false>(tok, ta, tb, tx, p, grid, s);
+  rc = pr ? launch_packed_tok<kEpiSwiGLUT, true>(tok, ta, tb, tx, p, grid, s)
+          : launch_packed_tok<kEpiSwiGLUT, false>(tok, ta, tb, tx, p, grid, s);
+  if (rc || !may_split) return rc;
+  const int n = rows * I;
+  split_swiglu_kernel<<<std::max(1, std::min((n + 255) / 256, 148 * 4)), 256, 0, s>>>(
+      p.ws_partial, p.ws_counters, rows, I, static_cast<__nv_bfloat16*>(act));
+  return check_cuda(cudaGetLastError(), "split SwiGLU launch");
 }
 
 int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts, const int* sorted_slots,
                        const float* topk_weights, void* y, int rows, int E, int H, int I, int T, int topk,
-                       int tok_tile, int pair, int num_sms, void* stream) {
+                       int tok_tile, int pair, int num_sms, void* workspace, size_t workspace_bytes, void* stream) {
   clear_error();
   if (!act || !w2 || !expert_counts || !sorted_slots || !topk_weights || !y)
     return set_error(EK_ERR_INVALID, "down_packed: null pointer");
@@ -669,11 +740,27 @@ int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts
   p.sorted_slots = sorted_slots;
   p.slot_weights = topk_weights;
   p.num_slots = T * topk;
+  // the slices cover every slot only when the packed rows are exactly the T * topk slots
+  const size_t need = rows == T * topk ? split_workspace_bytes(rows, H, I) : 0;
+  const bool may_split = need > 0 && workspace != nullptr && workspace_bytes >= need && aligned16(workspace) &&
+                         split_expected(rows, E, tok, ctas, S, p.feat_tiles, p.k_blocks);
+  if (may_split) {
+    p.tail_split = kSplitMax;
+    p.ws_counters = static_cast<int*>(workspace);
+    p.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kSplitHeader);
+  }
   const int grid = std::max(1, S / ctas) * ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (pr) return launch_packed_tok<kEpiScatterT, true>(tok, ta, tb, ta, p, grid, s);
-  return launch_packed_tok<kEpiScatterT, false>(tok, ta, tb, ta, p, grid, s);
+  rc = pr ? launch_packed_tok<kEpiScatterT, true>(tok, ta, tb, ta, p, grid, s)
+          : launch_packed_tok<kEpiScatterT, false>(tok, ta, tb, ta, p, grid, s);
+  if (rc || !may_split) return rc;
+  const int n = T * topk * H;
+  split_sum_kernel<<<std::max(1, std::min((n + 255) / 256, 148 * 4)), 256, 0, s>>>(p.ws_partial, p.ws_counters, n,
+                                                                                  static_cast<__nv_bfloat16*>(y));
+  return check_cuda(cudaGetLastError(), "split sum launch");
 }
+
+size_t ek_moe_packed_workspace_bytes(int rows, int H, int I) { return split_workspace_bytes(rows, H, I); }
 
 int ek_moe_gather_cols_f32(const int* sorted_slots, const int* num_rows_padded, int max_rows, int n_slots, int topk,
                            const float* src, int cols, float* dst, void* stream) {

@@ -230,12 +230,25 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
  * tokens the N side, in tiles of tok_tile tokens (16/32/64/128/256). Weight
  * tiles stream from HBM once per token tile, which keeps small token counts
  * HBM-efficient. tok_tile = 0 and pair = -1 choose automatically.
- * Results equal the block-padded variants'. E <= 256. */
+ * Results equal the block-padded variants' (within fp32 summation order).
+ * E <= 256.
+ *
+ * workspace (16-byte aligned, ek_moe_packed_workspace_bytes(rows, H, I)
+ * bytes, or NULL) lets the kernel split K when its units would fill the SMs
+ * poorly (a few experts hit at small token counts): the kernel picks the
+ * split from the expert counts on the device, writes fp32 slice sums to the
+ * workspace, and a second launch adds the slices in order and applies the
+ * SwiGLU / writes y. With NULL (or a smaller buffer) K is never split. */
 int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, const int* expert_counts, void* act,
-                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* stream);
+                          int rows, int E, int H, int I, int tok_tile, int pair, int num_sms, void* workspace,
+                          size_t workspace_bytes, void* stream);
 int ek_moe_down_packed(const void* act, const void* w2, const int* expert_counts, const int* sorted_slots,
                        const float* topk_weights, void* y, int rows, int E, int H, int I, int T, int topk,
-                       int tok_tile, int pair, int num_sms, void* stream);
+                       int tok_tile, int pair, int num_sms, void* workspace, size_t workspace_bytes, void* stream);
+/* Workspace for the K-split of the packed GEMMs (0: no split at this size;
+ * rows = T * topk up to 64). Replaces nothing in the reference (its segment
+ * GEMM has no split); serves the decode-sized Mixtral layer. */
+size_t ek_moe_packed_workspace_bytes(int rows, int H, int I);
 
 /* FP8 e4m3 packed grouped GEMMs with DeepSeek-style scales: weights with
  * 128 x 128 fp32 block scales (w*_scale [E*rows/128][K/128]), tokens with

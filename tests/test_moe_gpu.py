@@ -192,3 +192,38 @@ def test_segment_gemm_reference_config(cuda_dev, dtype):
     torch.cuda.synchronize()
     ref = og.segment_gemm_ref(hs, w, offs, N, K)
     assert og.max_rel_err(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("T", [1, 2, 4, 16])
+def test_packed_ksplit(cuda_dev, T):
+    """Decode-sized packed GEMMs split K on the device (the split shows in
+    the workspace header) and agree with the unsplit kernels and the oracle."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200._lib import lib
+
+    H, I, E, k = 2048, 1024, 8, 2
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=T + 70)
+    x, logits = x.to(cuda_dev), logits.to(cuda_dev)
+    w1, w2, w3 = w1.to(cuda_dev), w2.to(cuda_dev), w3.to(cuda_dev)
+    ids, wts = _ops.moe_route(logits, k)
+    perm = _ops.moe_permute(ids, E, x=x, block_m=1)
+    rows = perm["max_rows"]
+    nb = int(lib().ek_moe_packed_workspace_bytes(rows, H, I))
+    assert nb > 0
+    ws = torch.full((nb,), 0, dtype=torch.uint8, device=cuda_dev)
+    act = torch.empty((rows, I), dtype=torch.bfloat16, device=cuda_dev)
+    assert lib().ek_moe_gate_up_packed(perm["x_perm"].data_ptr(), w1.data_ptr(), w3.data_ptr(),
+                                       perm["expert_counts"].data_ptr(), act.data_ptr(), rows, E, H, I, 0, -1, 0,
+                                       ws.data_ptr(), nb, _ops.current_stream_handle(cuda_dev)) == 0
+    split_gu = int(ws[:4].view(torch.int32).item())
+    act_ref = _ops.moe_gate_up_packed(perm, w1, w3, ksplit=False)
+    y = _ops.moe_down_packed(perm, act, w2, wts)
+    y_ref = _ops.moe_down_packed(perm, act, w2, wts, ksplit=False)
+    torch.cuda.synchronize()
+    if T == 1:
+        assert split_gu > 1, "T=1: the gate/up GEMM did not split K"
+    assert og.max_rel_err(act, act_ref.float().cpu().numpy()) <= 1e-2
+    assert og.max_rel_err(y, y_ref.float().cpu().numpy()) <= 1e-2
+    out = _ops.moe_combine(y, T, k)
+    ref = om.moe_ref(x.cpu(), logits.cpu(), w1.cpu(), w2.cpu(), w3.cpu(), k)
+    assert og.max_rel_err(out, ref) <= TOL
