@@ -478,6 +478,11 @@ def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = N
 
 PACKED_MIN_SMS = 112
 PACKED_MAX_ROWS_PER_EXPERT = 384
+# below PACKED_MIN_SMS the packed layout still wins at decode sizes (routed rows)
+PACKED_DECODE_MIN_SMS = 64
+PACKED_DECODE_ROWS = 2
+PACKED_DECODE_WIDE_SMS = 96
+PACKED_DECODE_ROWS_WIDE = 4
 
 
 def moe_layout(num_sms: int, num_experts: int, rows: int | None = None) -> str:
@@ -490,9 +495,16 @@ def moe_layout(num_sms: int, num_experts: int, rows: int | None = None) -> str:
     T=1024 (256 rows per expert): 845 vs 877 us on 148 SMs -- and the 128-row
     padded layout from 512 rows per expert (T=2048: 1334 vs 1379 us, T=4096:
     2402 vs 2572 us) and on small partitions (T=128 on 72 SMs: 632 us padded
-    vs 833 us packed)."""
-    if num_sms < PACKED_MIN_SMS or num_experts > 256:
+    vs 833 us packed), except at decode sizes, where the packed GEMMs stream
+    only the experts hit and split K over the idle SMs (96 SMs: T=1 202 vs
+    245 us, T=2 254 vs 284 us, T=4 347 vs 325 us; 72 SMs: T=1 248 vs 254 us,
+    T=2 339 vs 314 us)."""
+    if num_experts > 256:
         return "padded"
+    if num_sms < PACKED_MIN_SMS:
+        decode_rows = (PACKED_DECODE_ROWS_WIDE if num_sms >= PACKED_DECODE_WIDE_SMS
+                       else PACKED_DECODE_ROWS if num_sms >= PACKED_DECODE_MIN_SMS else 0)
+        return "packed" if rows is not None and rows <= decode_rows else "padded"
     if rows is not None and rows > PACKED_MAX_ROWS_PER_EXPERT * num_experts:
         return "padded"
     return "packed"

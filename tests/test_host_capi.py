@@ -199,3 +199,21 @@ def test_plan_table_per_sm_level():
         assert t[s]["num_sms"] == s
     est = [t[s]["est_us"] for s in levels]
     assert all(b <= a * 1.001 for a, b in zip(est, est[1:]))
+
+
+def test_moe_layout_policy():
+    """Packed expert-major layout on (nearly) the full device up to a few
+    hundred rows per expert and at decode sizes on partitions of 64+ SMs;
+    the 128-row padded layout otherwise."""
+    from elastikernel_b200._ops import moe_layout
+
+    assert moe_layout(148, 8, 2) == "packed"
+    assert moe_layout(148, 8, 2 * 1024) == "packed"
+    assert moe_layout(148, 8, 2 * 4096) == "padded"
+    assert moe_layout(148, 512, 2) == "padded"
+    assert moe_layout(96, 8, 4) == "packed"
+    assert moe_layout(96, 8, 8) == "padded"
+    assert moe_layout(72, 8, 2) == "packed"
+    assert moe_layout(72, 8, 4) == "padded"
+    assert moe_layout(32, 8, 2) == "padded"
+    assert moe_layout(72, 8, None) == "padded"
