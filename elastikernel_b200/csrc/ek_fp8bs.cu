@@ -94,8 +94,11 @@ void tiles(long long rows, int E, int S, int force_tok, int force_pair, bool pai
     if (pr) {
       // 256-token pair tiles need 16 epilogue warps and run short of registers:
       // a busier expert takes several 192-token tiles instead. A 160-token
-      // tile leaves TMEM room for 3 K-block buffers (192: 2).
-      t = want <= 128 ? 128 : want <= 160 ? 160 : 192;
+      // tile leaves TMEM room for 3 K-block buffers (192: 2) and stays ahead
+      // while a few experts overflow it into a second tile (DeepSeek-V3
+      // shapes, 128 rows per expert on average, mean + 3 sigma = 163: gate/up
+      // 2.29 vs 2.35 ms, down 1.36 vs 1.38 ms).
+      t = want <= 128 ? 128 : want <= 168 ? 160 : 192;
     } else {
       t = 16;
       while (t < want && t < 128) t *= 2;
