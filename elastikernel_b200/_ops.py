@@ -477,7 +477,7 @@ def moe_combine(y: torch.Tensor, T: int, topk: int, out: torch.Tensor | None = N
 
 
 PACKED_MIN_SMS = 112
-PACKED_MAX_ROWS_PER_EXPERT = 384
+PACKED_MAX_ROWS_PER_EXPERT = 288
 # below PACKED_MIN_SMS the packed layout still wins at decode sizes (routed rows)
 PACKED_DECODE_MIN_SMS = 64
 PACKED_DECODE_ROWS = 2
@@ -492,9 +492,10 @@ def moe_layout(num_sms: int, num_experts: int, rows: int | None = None) -> str:
     Measured on B200 (Mixtral shapes, T = 1..4096): the packed layout with the
     swapped-operand GEMMs is faster on (nearly) the full device while experts
     get up to a few hundred rows -- T=128: 519 us packed vs 578 us padded,
-    T=1024 (256 rows per expert): 845 vs 877 us on 148 SMs -- and the 128-row
-    padded layout from 512 rows per expert (T=2048: 1334 vs 1379 us, T=4096:
-    2402 vs 2572 us) and on small partitions (T=128 on 72 SMs: 632 us padded
+    T=1024 (256 rows per expert): 861 vs 875 us on 148 SMs -- and the 128-row
+    padded layout from 320 rows per expert (T=1280: 1029-1057 vs 1054-1206 us,
+    T=1536: 1241 vs 1322 us, T=2048: 1393 vs 1631 us, T=4096: 2402 vs 2572
+    us) and on small partitions (T=128 on 72 SMs: 632 us padded
     vs 833 us packed), except at decode sizes, where the packed GEMMs stream
     only the experts hit and split K over the idle SMs (96 SMs: T=1 202 vs
     245 us, T=2 254 vs 284 us, T=4 347 vs 325 us; 72 SMs: T=1 248 vs 254 us,

@@ -209,6 +209,7 @@ def test_moe_layout_policy():
 
     assert moe_layout(148, 8, 2) == "packed"
     assert moe_layout(148, 8, 2 * 1024) == "packed"
+    assert moe_layout(148, 8, 2 * 1280) == "padded"
     assert moe_layout(148, 8, 2 * 4096) == "padded"
     assert moe_layout(148, 512, 2) == "padded"
     assert moe_layout(96, 8, 4) == "packed"
