@@ -80,9 +80,9 @@ _SIGNATURES = {
     "ek_moe_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int,
                                 _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
-                                _c_int, _c_int, _c_vp]),
+                                _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_down": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
-                             _c_int, _c_int, _c_int, _c_int, _c_vp]),
+                             _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_gate_up_packed": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp] + [_c_int] * 7 + [_c_vp, _c_size, _c_vp]),
     "ek_moe_down_packed": (_c_int, [_c_vp] * 6 + [_c_int] * 9 + [_c_vp, _c_size, _c_vp]),
     "ek_moe_packed_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),

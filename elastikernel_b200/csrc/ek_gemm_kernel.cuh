@@ -99,8 +99,9 @@ struct GemmCfg {
   static_assert(!kBMN || BN_CTA % 64 == 0, "MN-major B is loaded in 64-column chunks");
   static_assert(!(kF8 && kBMN), "e4m3 B must be K-major");
   static_assert(!kPair || (kSched == kSchedDense && (kEpi == kEpiStore || kEpi == kEpiRowColScale)) ||
-                    (kSwapped && (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT)),
-                "the CTA-pair mode serves the dense and swapped schedules");
+                    (kSwapped && (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT)) ||
+                    (kSched == kSchedBlocks && !kBMN && (kEpi == kEpiSwiGLU || kEpi == kEpiWeightedScatter)),
+                "the CTA-pair mode serves the dense, swapped and 256-row padded schedules");
   static_assert(!kSwapped || (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT), "swapped schedule epilogues");
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
 };
@@ -222,9 +223,11 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     w.b_col = w.tn * Cfg::BN + rank * Cfg::BN_CTA;
     w.c_col = w.tn * Cfg::BN;
   } else if constexpr (Cfg::kSched == kSchedBlocks) {
-    const int mblocks = rows_runtime / Cfg::BM;
+    // row blocks of TILE_M rows (256 for a CTA pair, whose layout is padded
+    // to 256 rows per expert so that a pair never spans two experts)
+    const int mblocks = rows_runtime / Cfg::TILE_M;
     raster(u, mblocks, p.tiles_n, p.group_m, w.tm, w.tn);
-    w.a_row = w.tm * Cfg::BM;
+    w.a_row = w.tm * Cfg::TILE_M + rank * Cfg::BM;
     w.row_end = rows_runtime;
     const int e = p.block_expert[w.tm];
     if (e < 0 || e >= p.num_experts) {
@@ -232,7 +235,10 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
       if (e >= p.num_experts) atomicOr(&g_ek_status, kStatusBadExpert);
     }
     const int bn_rows = (Cfg::kEpi == kEpiSwiGLU) ? Cfg::BN / 2 : Cfg::BN;
-    w.b_row = e * p.b_rows_per_expert + w.tn * bn_rows;
+    // SwiGLU pair: both CTAs load the same feature rows, of w1 (rank 0) and
+    // w3 (rank 1); otherwise each CTA loads its half of the tile's B rows
+    w.b_row = e * p.b_rows_per_expert + w.tn * bn_rows +
+              ((Cfg::kPair && Cfg::kEpi != kEpiSwiGLU) ? rank * Cfg::BN_CTA : 0);
     w.b_col = 0;
     w.c_col = w.tn * bn_rows;
   } else if constexpr (Cfg::kSched == kSchedSegments) {
@@ -443,7 +449,7 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (Cfg::kSched == kSchedBlocks) {
     int r = *p.num_rows_ptr;
     rows_rt = max(0, min(r, p.M));
-    nunits = (rows_rt / Cfg::BM) * p.tiles_n;
+    nunits = (rows_rt / Cfg::TILE_M) * p.tiles_n;
   } else if constexpr (Cfg::kSwapped) {
     nunits = xt.tprefix[p.num_experts];
   }
@@ -478,6 +484,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
               for (int j = 0; j < Cfg::BN_CTA / 64; ++j)
                 tma_load_2d_pair(b_dst + j * (BK * 128), &tmB, fb, w.b_col + 64 * j, w.b_row + kb * BK);
+            } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
+              // columns [0, BN/2) of the pair's tile come from rank 0 (w1), [BN/2, BN) from rank 1 (w3)
+              tma_load_2d_pair(b_dst, leader ? &tmB : &tmX, fb, kb * BK, w.b_row);
             } else {
               tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, w.b_row);
             }

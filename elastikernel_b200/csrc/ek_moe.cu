@@ -559,19 +559,24 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
 
 int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
                    const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_slots, int num_sms,
-                   int force_bn, void* stream) {
+                   int force_bn, int block_m, void* stream) {
   clear_error();
   if (!x_perm || !w1 || !w3 || !block_expert || !num_rows_padded || !act)
     return set_error(EK_ERR_INVALID, "gate_up: null pointer");
-  if (max_rows % 128 != 0 || E < 1 || H % 16 != 0 || I % 8 != 0 || H <= 0 || I <= 0)
-    return set_error(EK_ERR_INVALID, "gate_up: max_rows %% 128, H %% 16 and I %% 8 must be 0");
+  if (block_m != 128 && block_m != 256) return set_error(EK_ERR_INVALID, "gate_up: block_m must be 128 or 256");
+  if (max_rows % block_m != 0 || E < 1 || H % 16 != 0 || I % 8 != 0 || H <= 0 || I <= 0)
+    return set_error(EK_ERR_INVALID, "gate_up: max_rows %% block_m, H %% 16 and I %% 8 must be 0");
   if (!aligned16(x_perm) || !aligned16(w1) || !aligned16(w3) || !aligned16(act))
     return set_error(EK_ERR_INVALID, "gate_up: buffers must be 16-byte aligned");
   int S = 0;
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   const int mblocks = max_rows / 128;
-  const int bn = force_bn > 0 ? force_bn : grouped_bn(est_mblocks(num_slots, E, mblocks), E, I, H, S, true);
+  // 256-row blocks run as CTA pairs with 256-wide tiles
+  const bool pair = block_m == 256;
+  if (pair && (S < 2 || (force_bn > 0 && force_bn != 256)))
+    return set_error(EK_ERR_INVALID, "gate_up: 256-row blocks need 2+ SMs and the 256-wide tile");
+  const int bn = pair ? 256 : force_bn > 0 ? force_bn : grouped_bn(est_mblocks(num_slots, E, mblocks), E, I, H, S, true);
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
   CUtensorMap ta, tb, tb2;
   if ((rc = make_tmap_2d(&ta, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, max_rows, (uint64_t)H * 2, 64, 128))) return rc;
@@ -593,8 +598,13 @@ int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int
   p.num_rows_ptr = num_rows_padded;
   p.num_experts = E;
   p.b_rows_per_expert = I;
-  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) {
+    p.tiles_m = max_rows / 256;
+    const int grid = (int)std::min<long long>(S / 2, (long long)p.tiles_m * p.tiles_n) * 2;
+    return launch_grouped<GemmCfg<256, kBF16, false, kEpiSwiGLU, kSchedBlocks, true>>(ta, tb, tb2, p, grid, s);
+  }
+  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
   switch (bn) {
     case 64: return launch_grouped<GemmCfg<64, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
     case 128: return launch_grouped<GemmCfg<128, kBF16, false, kEpiSwiGLU, kSchedBlocks>>(ta, tb, tb2, p, grid, s);
@@ -605,24 +615,31 @@ int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int
 
 int ek_moe_down(const void* act, const void* w2, const int* block_expert, const int* num_rows_padded,
                 const int* sorted_slots, const float* topk_weights, void* y, int max_rows, int E, int H, int I, int T,
-                int topk, int num_sms, int force_bn, void* stream) {
+                int topk, int num_sms, int force_bn, int block_m, void* stream) {
   clear_error();
   if (!act || !w2 || !block_expert || !num_rows_padded || !sorted_slots || !topk_weights || !y)
     return set_error(EK_ERR_INVALID, "down: null pointer");
-  if (max_rows % 128 != 0 || E < 1 || I % 16 != 0 || H % 8 != 0 || H <= 0 || I <= 0 || T < 0 || topk < 1)
-    return set_error(EK_ERR_INVALID, "down: max_rows %% 128, I %% 16 and H %% 8 must be 0");
+  if (block_m != 128 && block_m != 256) return set_error(EK_ERR_INVALID, "down: block_m must be 128 or 256");
+  if (max_rows % block_m != 0 || E < 1 || I % 16 != 0 || H % 8 != 0 || H <= 0 || I <= 0 || T < 0 || topk < 1)
+    return set_error(EK_ERR_INVALID, "down: max_rows %% block_m, I %% 16 and H %% 8 must be 0");
   if (!aligned16(act) || !aligned16(w2) || !aligned16(y))
     return set_error(EK_ERR_INVALID, "down: buffers must be 16-byte aligned");
   int S = 0;
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   const int mblocks = max_rows / 128;
-  const int bn = force_bn > 0 ? force_bn
-                              : grouped_bn(est_mblocks((long long)T * topk, E, mblocks), E, H, I, S, false);
+  // 256-row blocks run as CTA pairs with 256-wide tiles (each CTA loads 128 B rows)
+  const bool pair = block_m == 256;
+  if (pair && (S < 2 || (force_bn > 0 && force_bn != 256)))
+    return set_error(EK_ERR_INVALID, "down: 256-row blocks need 2+ SMs and the 256-wide tile");
+  const int bn = pair ? 256
+                      : force_bn > 0 ? force_bn
+                                     : grouped_bn(est_mblocks((long long)T * topk, E, mblocks), E, H, I, S, false);
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return set_error(EK_ERR_INVALID, "bad tile width %d", bn);
   CUtensorMap ta, tb;
   if ((rc = make_tmap_2d(&ta, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, max_rows, (uint64_t)I * 2, 64, 128))) return rc;
-  if ((rc = make_tmap_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, (uint64_t)E * H, (uint64_t)I * 2, 64, bn)))
+  if ((rc = make_tmap_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, (uint64_t)E * H, (uint64_t)I * 2, 64,
+                         pair ? bn / 2 : bn)))
     return rc;
   GemmParams p{};
   p.M = max_rows;
@@ -641,8 +658,13 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
   p.sorted_slots = sorted_slots;
   p.slot_weights = topk_weights;
   p.num_slots = T * topk;
-  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) {
+    p.tiles_m = max_rows / 256;
+    const int grid = (int)std::min<long long>(S / 2, (long long)p.tiles_m * p.tiles_n) * 2;
+    return launch_grouped<GemmCfg<256, kBF16, false, kEpiWeightedScatter, kSchedBlocks, true>>(ta, tb, tb, p, grid, s);
+  }
+  const int grid = std::min<long long>(S, (long long)mblocks * p.tiles_n);
   switch (bn) {
     case 64: return launch_grouped<GemmCfg<64, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);
     case 128: return launch_grouped<GemmCfg<128, kBF16, false, kEpiWeightedScatter, kSchedBlocks>>(ta, tb, tb, p, grid, s);

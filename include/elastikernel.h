@@ -208,19 +208,21 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
 
 /* Grouped gate/up GEMM with fused SiLU-and-multiply over the padded rows:
  *   act[r, n] = silu(x_perm[r] . w1[e, n]) * (x_perm[r] . w3[e, n]),
- * e = block_expert[r / 128], for r < *num_rows_padded; w1, w3 are [E, I, H]
- * bf16; act is [max_rows, I] bf16. num_slots (T * topk) only guides the
- * choice of tile width. */
+ * e = block_expert[r / block_m], for r < *num_rows_padded; w1, w3 are
+ * [E, I, H] bf16; act is [max_rows, I] bf16. num_slots (T * topk) only
+ * guides the choice of tile width. block_m is the padding the layout was
+ * permuted with: 128 (one CTA per 128-row tile) or 256 (2-SM CTA pairs with
+ * 256 x 256 tiles; needs 2+ SMs and force_bn 0 or 256). */
 int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int* block_expert,
                    const int* num_rows_padded, void* act, int max_rows, int E, int H, int I, int num_slots,
-                   int num_sms, int force_bn, void* stream);
+                   int num_sms, int force_bn, int block_m, void* stream);
 
 /* Grouped down projection with the top-k weight fused into the epilogue:
  *   y[s] = topk_weight[s] * (act[r] @ w2[e]^T),  s = sorted_slots[r] < T*k,
- * w2 is [E, H, I] bf16, y is [T*k, H] bf16. */
+ * w2 is [E, H, I] bf16, y is [T*k, H] bf16. block_m as for ek_moe_gate_up. */
 int ek_moe_down(const void* act, const void* w2, const int* block_expert, const int* num_rows_padded,
                 const int* sorted_slots, const float* topk_weights, void* y, int max_rows, int E, int H, int I,
-                int T, int topk, int num_sms, int force_bn, void* stream);
+                int T, int topk, int num_sms, int force_bn, int block_m, void* stream);
 
 /* Packed (expert-major) variants of the two grouped GEMMs, over the layout
  * ek_moe_permute produces with block_m = 1 (rows of expert e packed at

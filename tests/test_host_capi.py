@@ -218,3 +218,12 @@ def test_moe_layout_policy():
     assert moe_layout(72, 8, 4) == "padded"
     assert moe_layout(32, 8, 2) == "padded"
     assert moe_layout(72, 8, None) == "padded"
+
+
+def test_padded_block_m_policy():
+    """256-row padding (CTA-pair tiles) only for heavy loads on 2+ SMs."""
+    from elastikernel_b200._ops import padded_block_m
+
+    assert padded_block_m(148, 8, 2 * 4096) == 256
+    assert padded_block_m(148, 8, 2 * 2048) == 128
+    assert padded_block_m(1, 8, 2 * 4096) == 128

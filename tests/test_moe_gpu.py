@@ -227,3 +227,26 @@ def test_packed_ksplit(cuda_dev, T):
     out = _ops.moe_combine(y, T, k)
     ref = om.moe_ref(x.cpu(), logits.cpu(), w1.cpu(), w2.cpu(), w3.cpu(), k)
     assert og.max_rel_err(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("T,H,I,E,k", [(300, 256, 512, 8, 2), (1024, 512, 768, 8, 2), (64, 256, 256, 16, 4),
+                                       (1, 256, 512, 8, 2)])
+def test_padded_pair_tiles(cuda_dev, T, H, I, E, k):
+    """The layout padded to 256 rows per expert runs the gate/up and down
+    GEMMs on CTA pairs; the layer matches the oracle and the 128-row path."""
+    from elastikernel_b200 import _ops
+
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=T + H + 5)
+    x, logits = x.to(cuda_dev), logits.to(cuda_dev)
+    w1, w2, w3 = w1.to(cuda_dev), w2.to(cuda_dev), w3.to(cuda_dev)
+    ids, wts = _ops.moe_route(logits, k)
+    outs = []
+    for bm in (256, 128):
+        perm = _ops.moe_permute(ids, E, x=x, block_m=bm)
+        act = _ops.moe_gate_up(perm, w1, w3)
+        y = _ops.moe_down(perm, act, w2, wts)
+        outs.append(_ops.moe_combine(y, T, k))
+    torch.cuda.synchronize()
+    ref = om.moe_ref(x.cpu(), logits.cpu(), w1.cpu(), w2.cpu(), w3.cpu(), k)
+    assert og.max_rel_err(outs[0], ref) <= TOL
+    assert og.max_rel_err(outs[0], outs[1].float().cpu().numpy()) <= TOL
