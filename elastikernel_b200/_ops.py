@@ -513,16 +513,23 @@ def moe_layout(num_sms: int, num_experts: int, rows: int | None = None) -> str:
     return "packed"
 
 
-PAIR_MIN_ROWS_PER_EXPERT = 768
+PAIR_MIN_ROWS_PER_EXPERT = 768        # from PACKED_MIN_SMS SMs up
+PAIR_MIN_ROWS_PER_EXPERT_SMALL = 256  # on smaller partitions
 
 
 def padded_block_m(num_sms: int, num_experts: int, rows: int) -> int:
     """Row padding of the padded layout: 256 (2-SM CTA-pair tiles) from 768
-    routed rows per expert on 2+ SMs, else 128. Measured on B200 (Mixtral
-    shapes, 148 SMs): T=4096 (1024 rows per expert) gate/up 1751-1786 vs
-    1882 us and down 858-887 vs 957-969 us; T=2048 (512 rows per expert)
-    no gain, the extra padding eats the pair's higher per-row rate."""
-    return 256 if num_sms >= 2 and rows >= PAIR_MIN_ROWS_PER_EXPERT * num_experts else BLOCK_M
+    routed rows per expert on 112+ SMs and from 256 on 2..111 SMs, else 128.
+    Measured on B200 (Mixtral shapes): on 148 SMs T=4096 (1024 rows per
+    expert) gate/up 1751-1786 vs 1882 us and down 858-887 vs 957-969 us,
+    T=2048 (512 rows per expert) no gain, the extra padding eats the pair's
+    higher per-row rate; on 72 SMs the layer at T=1024 / 2048 / 4096 takes
+    1280 / 1903-1987 / 3598-3731 us with pairs vs 1303-1316 / 2144 /
+    4152-4257 us, at T=512 863-976 vs 859-884 us."""
+    if num_sms < 2:
+        return BLOCK_M
+    per_expert = PAIR_MIN_ROWS_PER_EXPERT if num_sms >= PACKED_MIN_SMS else PAIR_MIN_ROWS_PER_EXPERT_SMALL
+    return 256 if rows >= per_expert * num_experts else BLOCK_M
 
 
 def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,

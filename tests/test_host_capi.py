@@ -227,3 +227,5 @@ def test_padded_block_m_policy():
     assert padded_block_m(148, 8, 2 * 4096) == 256
     assert padded_block_m(148, 8, 2 * 2048) == 128
     assert padded_block_m(1, 8, 2 * 4096) == 128
+    assert padded_block_m(72, 8, 2 * 1024) == 256
+    assert padded_block_m(72, 8, 2 * 512) == 128
