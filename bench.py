@@ -200,7 +200,7 @@ def e2e_pipelined(smm, a_h, b_h, a_like, b_like, steps: int) -> float:
     return start.elapsed_time(end) / steps
 
 
-def partition_sweep(dev, peak_tflops: float, steps: int) -> dict:
+def partition_sweep(dev, peak_tflops: float, steps: int, hbm_gbs: float = FALLBACK_PEAKS["hbm_gbs"]) -> dict:
     from elastikernel_b200 import sm_aware_matmul as smm
     from elastikernel_b200.green_ctx import create_sm_partition, full_device_partition, get_total_sm_count
     from elastikernel_b200.timing import time_on_stream
@@ -226,16 +226,29 @@ def partition_sweep(dev, peak_tflops: float, steps: int) -> dict:
                                        "wave_eff": round(p["wave_efficiency"], 3)})
         except Exception as e:  # report and continue, as the reference benchmark does
             out["square_4096"].append({"sm": S, "error": str(e)[:200]})
+    # M sweep: the GEMM replayed from a CUDA graph (device time of the kernel;
+    # an eager call's host work -- planning, tensor maps, the ctypes launch --
+    # outlasts the L2 flush for the small M and would be timed too), with the
+    # eager call's time beside it, and the max(tensor, HBM) floor.
     for Mi in [128, 256, 512, 1024, 2048, 4096, 8192]:
         a2 = torch.randn((Mi, K), device=dev, dtype=torch.bfloat16, generator=g)
         for _ in range(2):
             smm.call_sm_aware(a2, b)
-        r = time_on_stream(lambda: smm.call_sm_aware(a2, b), reps=max(3, steps // 2))
-        tf = 2.0 * Mi * N * K / (r["mean_ms"] * 1e-3) / 1e12
+        r_eager = time_on_stream(lambda: smm.call_sm_aware(a2, b), reps=max(3, steps // 2))
+        gm = smm.GraphMatmul(a2, b, num_sms=total)
+        r = time_on_stream(gm, reps=max(3, steps // 2))
+        flop = 2.0 * Mi * N * K
+        nbytes = 2.0 * (Mi * K + K * N + Mi * N)
+        floor_us = max(flop / (peak_tflops * 1e12), nbytes / (hbm_gbs * 1e9)) * 1e6
+        tf = flop / (r["mean_ms"] * 1e-3) / 1e12
         p = smm.tcgen05_schedule(Mi, N, K, total)
-        out["m_sweep_148"].append({"M": Mi, "us": round(r["mean_ms"] * 1e3, 1), "tflops": round(tf, 1),
-                                   "pct_peak": round(100 * tf / peak_tflops, 1), "bn": p["bn"],
-                                   "split": p["tail_split"], "tiles": p["num_tiles"]})
+        out["m_sweep_148"].append({"M": Mi, "us": round(r["mean_ms"] * 1e3, 1),
+                                   "us_eager": round(r_eager["mean_ms"] * 1e3, 1), "tflops": round(tf, 1),
+                                   "pct_peak": round(100 * tf / peak_tflops, 1),
+                                   "pct_roofline_time": round(100 * floor_us / (r["mean_ms"] * 1e3), 1),
+                                   "bound": "tensor" if flop / (peak_tflops * 1e12) >= nbytes / (hbm_gbs * 1e9)
+                                   else "hbm", "bn": p["bn"], "split": p["tail_split"], "tiles": p["num_tiles"]})
+        del gm
     return out
 
 
@@ -504,7 +517,7 @@ def main() -> None:
 
     extras = {}
     if not args.no_extras:
-        extras["partitions"] = partition_sweep(dev, peak_tf, args.steps)
+        extras["partitions"] = partition_sweep(dev, peak_tf, args.steps, hbm)
         extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
         extras["moe"] = moe_bench(dev, args.steps, hbm)
         extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
