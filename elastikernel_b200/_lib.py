@@ -155,9 +155,21 @@ def check(rc: int, what: str = "") -> None:
 
 
 def device_status(dev: int, clear: bool = True) -> int:
-    """Synchronise `dev` and return (and by default clear) the kernels' status word."""
+    """Synchronise `dev` and return (and by default clear) the kernels' status word.
+
+    A bounded-wait timeout can strike in the middle of a split-K hand-off and
+    leave a ticket or a "part written" flag set in the split workspace; a later
+    launch over the same workspace would then read a part that was never
+    written. So when the word reports EK_STATUS_WAIT_TIMEOUT, every cached
+    workspace of the device is zero-filled again before this returns."""
     v = ctypes.c_int(0)
     check(lib().ek_device_status(int(dev), 1 if clear else 0, ctypes.byref(v)), "ek_device_status")
+    if v.value & EK_STATUS_WAIT_TIMEOUT:
+        import torch
+
+        from . import _workspace
+
+        _workspace.reset(torch.device("cuda", int(dev)))
     return v.value
 
 

@@ -88,6 +88,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, num_
         return out
     if K == 0:
         return out.zero_()
+    # the C-ABI takes 16-byte aligned operands (ragged shapes are padded
+    # there); a view that starts mid-line is copied to a fresh device buffer
+    if a.data_ptr() % 16:
+        a = a.clone()
+    if b.data_ptr() % 16:
+        b = b.clone()
+    if out.data_ptr() % 16:
+        tmp = gemm(a, b, None, num_sms, b_layout, force_bn, force_split)
+        return out.copy_(tmp)
     L = lib()
     stream = current_stream_handle(dev)
     sms = int(num_sms) if num_sms else _stream_sms(dev, stream)

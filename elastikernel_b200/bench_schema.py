@@ -77,7 +77,7 @@ def gemm_definition(name: str = "gemm_sm_aware", dtype: str = "bfloat16") -> dic
         },
         "outputs": {"C": {"shape": ["M", "N"], "dtype": dtype, "description": "product, written in place"}},
         "reference": _GEMM_REFERENCE,
-        "constraints": ["M > 0", "N > 0", "K > 0", "NUM_SMS > 0", "N % 8 == 0", "K % 8 == 0"],
+        "constraints": ["M > 0", "N > 0", "K > 0", "NUM_SMS > 0"],
         "description": "GEMM planned for the SM count of the partition it runs in",
         "tags": ["gemm", "sm-aware", "sm_100a", "tcgen05"],
     }

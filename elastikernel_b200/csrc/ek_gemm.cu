@@ -249,6 +249,89 @@ CUtensorMapDataType tma_dtype(int dtype) {
   }
 }
 
+// ------------------------------------------------------ ragged shapes
+// The kernel's TMA descriptors need 16-byte row strides and its epilogue
+// stores whole 16-byte column groups, so it runs on N % 8 == 0, K % 16 == 0.
+// The reference's Triton kernel masks any shape (sm_aware_matmul.py:164-172);
+// for a ragged bf16 / fp16 shape ek_gemm copies the operands that need it
+// into zero-padded buffers in the caller's workspace (K padded with zeros
+// adds nothing to the dot products), runs the aligned GEMM and copies the
+// first N columns of the padded product back. All on the device, on the
+// caller's stream.
+struct RaggedLayout {
+  int Np, Kp;                     // padded GEMM dimensions
+  bool pad_a, pad_b, pad_c;       // operands copied into padded buffers
+  size_t split_bytes;             // split-K scratch of the padded plan (front)
+  size_t a_off, b_off, c_off;     // byte offsets of the padded copies
+  size_t total;                   // workspace bytes in all
+};
+
+size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+bool is_ragged(int N, int K) { return N % 8 != 0 || K % 16 != 0; }
+
+RaggedLayout ragged_layout(int M, int N, int K, int b_layout, size_t split_bytes) {
+  RaggedLayout L{};
+  L.Np = (N + 7) / 8 * 8;
+  L.Kp = (K + 15) / 16 * 16;
+  L.pad_a = L.Kp != K;
+  // [K, N]: rows past K read as zero through the descriptor's bounds, so only
+  // a ragged N (row stride) needs a copy; [N, K]: a ragged K does
+  L.pad_b = b_layout == EK_B_KN ? L.Np != N : L.Kp != K;
+  L.pad_c = L.Np != N;
+  // the split-K ticket region stays at the front even when this plan does not
+  // split: a workspace is shared by later calls that may
+  L.split_bytes = round256(std::max(split_bytes, kGemmTicketBytes));
+  size_t off = L.split_bytes;
+  L.a_off = off;
+  if (L.pad_a) off += round256((size_t)M * L.Kp * 2);
+  L.b_off = off;
+  if (L.pad_b) off += round256(b_layout == EK_B_KN ? (size_t)K * L.Np * 2 : (size_t)L.Np * L.Kp * 2);
+  L.c_off = off;
+  if (L.pad_c) off += round256((size_t)M * L.Np * 2);
+  L.total = off;
+  return L;
+}
+
+// dst[r][c] = c < cols ? src[r * ld_src + c] : 0 for r < rows, c < dcols
+// (dcols a multiple of 8, dst 16-byte aligned); one 16-byte group per step.
+__global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int rows, int cols, long long ld_src,
+                                uint16_t* __restrict__ dst, int dcols) {
+  const int groups = dcols / 8;
+  const long long n = (long long)rows * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / groups);
+    const int c0 = (int)(i - (long long)r * groups) * 8;
+    const uint16_t* s = src + (size_t)r * ld_src;
+    uint16_t v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (c0 + j < cols) ? s[c0 + j] : (uint16_t)0;
+    uint4 pk;
+    pk.x = v[0] | ((uint32_t)v[1] << 16);
+    pk.y = v[2] | ((uint32_t)v[3] << 16);
+    pk.z = v[4] | ((uint32_t)v[5] << 16);
+    pk.w = v[6] | ((uint32_t)v[7] << 16);
+    *reinterpret_cast<uint4*>(dst + (size_t)r * dcols + c0) = pk;
+  }
+}
+
+// dst[r][c] = src[r][c] for c < cols: the first `cols` columns of a
+// [rows, ld_src] matrix into a dense [rows, cols] one.
+__global__ void unpad_rows_kernel(const uint16_t* __restrict__ src, int rows, int cols, int ld_src,
+                                  uint16_t* __restrict__ dst) {
+  const long long n = (long long)rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols);
+    const int c = (int)(i - (long long)r * cols);
+    dst[i] = src[(size_t)r * ld_src + c];
+  }
+}
+
+int copy_grid(long long work, int S) {
+  const long long blocks = (work + 255) / 256;
+  return (int)std::max<long long>(1, std::min<long long>(blocks, (long long)S * 8));
+}
+
 int gemm_common(const void* A, const void* B, void* C, const float* a_scale, const float* b_scale, int M, int N,
                 int K, int dtype, int b_layout, int num_sms, int force_bn, int force_split, void* workspace,
                 size_t ws_bytes, void* stream) {
@@ -256,26 +339,68 @@ int gemm_common(const void* A, const void* B, void* C, const float* a_scale, con
   if (!A || !B || !C) return set_error(EK_ERR_INVALID, "null operand");
   if (!aligned16(A) || !aligned16(B) || !aligned16(C))
     return set_error(EK_ERR_INVALID, "operands must be 16-byte aligned");
-  if (N % 8 != 0 || K % 16 != 0)
-    return set_error(EK_ERR_INVALID, "N must be a multiple of 8 and K of 16 (got N=%d K=%d)", N, K);
   if (b_layout != EK_B_KN && b_layout != EK_B_NK) return set_error(EK_ERR_INVALID, "bad b_layout");
+  const bool ragged = is_ragged(N, K);
+  if (ragged && dtype == EK_DTYPE_E4M3)
+    return set_error(EK_ERR_INVALID, "e4m3 GEMM needs N a multiple of 8 and K of 16 (got N=%d K=%d)", N, K);
   int S = 0;
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
+  const int Np = ragged ? (N + 7) / 8 * 8 : N;
+  const int Kp = ragged ? (K + 15) / 16 * 16 : K;
   ek_gemm_plan plan;
-  rc = plan_dense(M, N, K, S, dtype, b_layout, force_bn, force_split, &plan);
+  rc = plan_dense(M, Np, Kp, S, dtype, b_layout, force_bn, force_split, &plan);
   if (rc) return rc;
-  if (plan.workspace_bytes > 0 && (!workspace || ws_bytes < plan.workspace_bytes || !aligned16(workspace)))
-    return set_error(EK_ERR_INVALID, "workspace of %zu bytes required (got %zu)", plan.workspace_bytes, ws_bytes);
-  return launch_dense(plan, A, B, C, a_scale, b_scale, M, N, K, dtype, b_layout, workspace,
-                      static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!ragged) {
+    if (plan.workspace_bytes > 0 && (!workspace || ws_bytes < plan.workspace_bytes || !aligned16(workspace)))
+      return set_error(EK_ERR_INVALID, "workspace of %zu bytes required (got %zu)", plan.workspace_bytes, ws_bytes);
+    return launch_dense(plan, A, B, C, a_scale, b_scale, M, N, K, dtype, b_layout, workspace, s);
+  }
+  const RaggedLayout L = ragged_layout(M, N, K, b_layout, plan.workspace_bytes);
+  if (!workspace || ws_bytes < L.total || !aligned16(workspace))
+    return set_error(EK_ERR_INVALID, "workspace of %zu bytes required for the padded %dx%dx%d GEMM (got %zu)",
+                     L.total, M, N, K, ws_bytes);
+  char* ws = static_cast<char*>(workspace);
+  const void* A2 = A;
+  const void* B2 = B;
+  void* C2 = C;
+  if (L.pad_a) {
+    A2 = ws + L.a_off;
+    pad_rows_kernel<<<copy_grid((long long)M * Kp / 8, S), 256, 0, s>>>(
+        static_cast<const uint16_t*>(A), M, K, K, static_cast<uint16_t*>(const_cast<void*>(A2)), Kp);
+    if ((rc = check_cuda(cudaGetLastError(), "pad A"))) return rc;
+  }
+  if (L.pad_b) {
+    B2 = ws + L.b_off;
+    uint16_t* b2 = static_cast<uint16_t*>(const_cast<void*>(B2));
+    if (b_layout == EK_B_KN)
+      pad_rows_kernel<<<copy_grid((long long)K * Np / 8, S), 256, 0, s>>>(static_cast<const uint16_t*>(B), K, N, N,
+                                                                          b2, Np);
+    else
+      pad_rows_kernel<<<copy_grid((long long)N * Kp / 8, S), 256, 0, s>>>(static_cast<const uint16_t*>(B), N, K, K,
+                                                                          b2, Kp);
+    if ((rc = check_cuda(cudaGetLastError(), "pad B"))) return rc;
+  }
+  if (L.pad_c) C2 = ws + L.c_off;
+  // the padded product: K padded for A ([M, Kp]) and for a [N, K] B; a [K, N]
+  // B keeps K rows and the descriptor's bounds supply the zero rows
+  rc = launch_dense(plan, A2, B2, C2, a_scale, b_scale, M, Np, Kp, dtype, b_layout, plan.workspace_bytes ? ws : nullptr,
+                    s, b_layout == EK_B_KN ? K : Kp);
+  if (rc) return rc;
+  if (L.pad_c) {
+    unpad_rows_kernel<<<copy_grid((long long)M * N, S), 256, 0, s>>>(static_cast<const uint16_t*>(C2), M, N, Np,
+                                                                     static_cast<uint16_t*>(C));
+    if ((rc = check_cuda(cudaGetLastError(), "unpad C"))) return rc;
+  }
+  return EK_OK;
 }
 
 }  // namespace
 
 int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C, const float* a_scale,
                  const float* b_scale, int M, int N, int K, int dtype, int b_layout, void* workspace,
-                 cudaStream_t s) {
+                 cudaStream_t s, int b_rows) {
   const int es = elem_bytes(dtype);
   const CUtensorMapDataType tdt = tma_dtype(dtype);
   const int bn_cta = plan.bn / (plan.cta_pair ? 2 : 1);
@@ -283,7 +408,7 @@ int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C
   int rc = make_tmap_2d(&ta, A, tdt, K, M, (uint64_t)K * es, 128 / es, 128);
   if (rc) return rc;
   if (b_layout == EK_B_KN)
-    rc = make_tmap_2d(&tb, B, tdt, N, K, (uint64_t)N * es, 64, 64);  // [K, N]: 64 N x 64 K boxes
+    rc = make_tmap_2d(&tb, B, tdt, N, b_rows > 0 ? b_rows : K, (uint64_t)N * es, 64, 64);  // [K, N]: 64 N x 64 K boxes
   else
     rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * es, 128 / es, bn_cta);
   if (rc) return rc;
@@ -333,8 +458,14 @@ int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout,
 size_t ek_gemm_workspace_bytes(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn,
                                int force_split) {
   ek_gemm_plan p;
-  if (plan_dense(M, N, K, num_sms, dtype, b_layout, force_bn, force_split, &p) != EK_OK) return (size_t)-1;
-  return p.workspace_bytes;
+  if (!is_ragged(N, K)) {
+    if (plan_dense(M, N, K, num_sms, dtype, b_layout, force_bn, force_split, &p) != EK_OK) return (size_t)-1;
+    return p.workspace_bytes;
+  }
+  if (dtype == EK_DTYPE_E4M3 || (b_layout != EK_B_KN && b_layout != EK_B_NK)) return (size_t)-1;
+  const int Np = (N + 7) / 8 * 8, Kp = (K + 15) / 16 * 16;
+  if (plan_dense(M, Np, Kp, num_sms, dtype, b_layout, force_bn, force_split, &p) != EK_OK) return (size_t)-1;
+  return ragged_layout(M, N, K, b_layout, p.workspace_bytes).total;
 }
 
 int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,

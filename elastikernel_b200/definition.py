@@ -41,28 +41,3 @@ def run_fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: to
     else:
         out.copy_(_ops.fused_moe(hidden_states, gate_logits, w1, w2, w3, TOP_K, num_sms=NUM_SMS))
 
-
-def smoke_moe(dev: torch.device) -> None:
-    """One small fused-MoE layer checked against the CPU oracle (used by the smoke entry point)."""
-    from oracle.gemm import max_rel_err
-    from oracle.moe import moe_ref, route_ref
-
-    from . import _lib
-
-    T, H, I, E, k = 64, 256, 512, 8, 2
-    g = torch.Generator().manual_seed(42)
-    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
-    logits = torch.randn((T, E), generator=g)
-    w1 = (torch.randn((E, I, H), generator=g) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn((E, H, I), generator=g) * 0.02).to(torch.bfloat16)
-    w3 = (torch.randn((E, I, H), generator=g) * 0.02).to(torch.bfloat16)
-    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    run_fused_moe(x.to(dev), logits.to(dev), w1.to(dev), w2.to(dev), w3.to(dev), out, T, H, I, E, k, 148)
-    ids, _ = _ops.moe_route(logits.to(dev), k)
-    torch.cuda.synchronize()
-    err = max_rel_err(out, moe_ref(x, logits, w1, w2, w3, k))
-    same_ids = bool((ids.cpu().numpy() == route_ref(logits.numpy(), k)[0]).all())
-    status = _lib.device_status(dev.index or 0)
-    print(f"smoke fused MoE T={T} H={H} I={I} E={E} k={k}: max rel err {err:.2e}, routing exact {same_ids}, "
-          f"status {status}")
-    assert status == 0 and err <= 1e-2 and same_ids, "MoE smoke check failed"

@@ -109,39 +109,94 @@ class GraphMatmul:
         return self._cap()
 
 
-def run_analytical(sm_levels=None, test_cases=None) -> None:
+def compute_wave_efficiency(M: int, N: int, block_m: int, block_n: int, num_sms: int) -> Dict[str, float]:
+    """Tile count, waves, last-wave utilisation and overall efficiency of a
+    one-tile-per-CTA grid, as a dict (sm_aware_agent/workload.py:86-107)."""
+    nw, lwu, eff = wave_efficiency(M, N, block_m, block_n, num_sms)
+    return {"num_blocks": ceil_div(M, block_m) * ceil_div(N, block_n), "num_waves": nw,
+            "last_wave_util": lwu, "overall_efficiency": eff if nw > 0 else 0}
+
+
+# Default (BLOCK_M, BLOCK_N) candidates of suggest_optimal_block_size
+# (sm_aware_agent/workload.py:126-131), in order: the first of equally
+# efficient candidates wins.
+SUGGEST_BLOCKS: List[Tuple[int, int]] = [(16, 64), (32, 64), (32, 128), (64, 64), (64, 128), (128, 64), (128, 128),
+                                         (128, 256), (256, 128), (64, 256), (256, 64)]
+
+
+def suggest_optimal_block_size(M: int, N: int, num_sms: int, block_sizes=None):
+    """(block_m, block_n, metrics) of the candidate with the strictly highest
+    overall wave efficiency (sm_aware_agent/workload.py:110-143)."""
+    best, best_eff = None, 0
+    for bm, bn in block_sizes or SUGGEST_BLOCKS:
+        m = compute_wave_efficiency(M, N, bm, bn, num_sms)
+        if m["overall_efficiency"] > best_eff:
+            best_eff, best = m["overall_efficiency"], (bm, bn, m)
+    return best
+
+
+# tcgen05 tile modes of the persistent kernel: (cta_pair, tile_m, tile_n),
+# passed to the planner as force_bn (> 0 one CTA, < 0 a CTA pair)
+TCGEN05_MODES = [(1, 256, 256), (1, 256, 128), (0, 128, 256), (0, 128, 192), (0, 128, 128), (0, 128, 64)]
+
+
+def get_configs_for_sm(num_sms: int, M: int = 4096, N: int = 4096, K: int = 4096, dtype: str = "bf16") -> List[dict]:
+    """The candidate tiles for a partition of `num_sms` SMs, best first.
+
+    The reference preselects Triton configs by SM regime -- small tiles up to
+    24 SMs, medium up to 64, large above (sm_aware_agent/generator.py:41-79) --
+    and lets autotuning pick among them. The tcgen05 kernel has six tile
+    modes; its planner prices every mode for the partition and shape (MMA vs
+    operand-feed rate per K step, the busiest CTA's K steps, a split of the
+    tail wave, the HBM floor), so the "regime" becomes this ranking: each
+    mode's schedule at its best tail split, sorted by the model's time. The
+    first entry is the schedule call_sm_aware runs."""
+    import torch
+
+    from . import _ops
+
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+    out = []
+    for pair, tm, tn in TCGEN05_MODES:
+        if pair and num_sms < 2:
+            continue
+        p = _ops.plan(M, N, K, num_sms, dt, force_bn=-tn if pair else tn)
+        out.append({"cta_pair": pair, "tile_m": tm, "tile_n": tn, "tail_split": p["tail_split"],
+                    "tiles": p["num_tiles"], "units": p["num_units"], "waves": p["waves"],
+                    "wave_efficiency": p["wave_efficiency"], "est_us": p["est_us"]})
+    out.sort(key=lambda c: c["est_us"])
+    return out
+
+
+def run_analytical(sm_levels=None, test_cases=None) -> list:
+    """Wave table per shape and partition size: the best whole-tile grid among
+    the reference's candidate list (ranked by waves, then last-wave fill) next
+    to the tcgen05 kernel's own schedule, which can also split the tail wave
+    along K. Returns the rows it prints."""
     sm_levels = sm_levels or SM_LEVELS
     test_cases = test_cases or [(1024, 1024, 1024), (2048, 2048, 2048), (4096, 4096, 4096)]
+    rows = []
+    hdr = (f"{'SMs':>4} | {'grid tile':>9} {'tiles':>6} {'waves':>5} {'fill':>6} {'eff':>6} | "
+           f"{'tcgen05':>9} {'split':>5} {'units':>6} {'waves':>5} {'eff':>6} {'model us':>8}")
     for M, N, K in test_cases:
-        print(f"\n{'=' * 90}")
-        print(f"Wave Analysis: M={M}, N={N}, K={K}")
-        print(f"{'=' * 90}")
-        best_per_sm = {}
-        for num_sms in sm_levels:
-            ranked = rank_configs(M, N, num_sms)
-            best_per_sm[num_sms] = ranked[0]
-            print(f"\n--- {num_sms} SMs ---")
-            print(f"  {'Rank':<5} {'Config':<45} {'Waves':<7} {'LastUtil':<10} {'Eff':<10}")
-            for i, (c, nw, lwu, eff) in enumerate(ranked[:5], 1):
-                s = f"M={c['BLOCK_SIZE_M']},N={c['BLOCK_SIZE_N']},K={c['BLOCK_SIZE_K']}"
-                print(f"  {i:<5} {s:<45} {nw:<7} {lwu * 100:>5.1f}%    {eff * 100:>5.1f}%")
-        print(f"\n{'=' * 90}")
-        print(f"Best Config per SM (M={M}, N={N}, K={K})")
-        print(f"{'=' * 90}")
-        print(f"  {'SM':<6} {'Best Config':<45} {'Waves':<7} {'Eff':<10} {'Changed?'}")
+        print(f"\n[{M} x {N} x {K}]  whole-tile grid (candidate list)  vs  persistent tcgen05 schedule")
+        print(hdr)
+        print("-" * len(hdr))
         prev = None
-        for num_sms in sm_levels:
-            c, nw, lwu, eff = best_per_sm[num_sms]
-            s = f"M={c['BLOCK_SIZE_M']},N={c['BLOCK_SIZE_N']},K={c['BLOCK_SIZE_K']}"
-            changed = " <-- CHANGED" if prev is not None and c != prev else ""
-            print(f"  {num_sms:<6} {s:<45} {nw:<7} {eff * 100:>5.1f}%{changed}")
-            prev = c
-        print(f"\n  tcgen05 schedule (128 x BN tiles, split tail wave):")
-        print(f"  {'SM':<6} {'BN':<5} {'tiles':<7} {'split':<6} {'units':<7} {'waves':<6} {'Eff':<8} {'est us':<8}")
-        for num_sms in sm_levels:
-            p = tcgen05_schedule(M, N, K, num_sms)
-            print(f"  {num_sms:<6} {p['bn']:<5} {p['num_tiles']:<7} {p['tail_split']:<6} {p['num_units']:<7} "
-                  f"{p['waves']:<6} {p['wave_efficiency'] * 100:>5.1f}%  {p['est_us']:>7.1f}")
+        for S in sm_levels:
+            c, nw, lwu, eff = rank_configs(M, N, S)[0]
+            tile = f"{c['BLOCK_SIZE_M']}x{c['BLOCK_SIZE_N']}"
+            p = tcgen05_schedule(M, N, K, S)
+            mode = f"{p['bm']}x{p['bn']}" + ("p" if p["cta_pair"] else "")
+            mark = "" if prev is None or tile == prev else "  (grid tile changes)"
+            prev = tile
+            print(f"{S:>4} | {tile:>9} {ceil_div(M, c['BLOCK_SIZE_M']) * ceil_div(N, c['BLOCK_SIZE_N']):>6} "
+                  f"{nw:>5} {lwu * 100:>5.1f}% {eff * 100:>5.1f}% | {mode:>9} {p['tail_split']:>5} "
+                  f"{p['num_units']:>6} {p['waves']:>5} {p['wave_efficiency'] * 100:>5.1f}% {p['est_us']:>8.1f}{mark}")
+            rows.append({"M": M, "N": N, "K": K, "sms": S, "grid_tile": tile, "grid_waves": nw,
+                         "grid_last_util": lwu, "grid_eff": eff, "tcgen05": p})
+    print("\n(p = 2-SM CTA pair; fill = share of SMs busy in the last wave)")
+    return rows
 
 
 # =============================================================================

@@ -121,23 +121,29 @@ typedef struct ek_gemm_plan {
 int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
                       ek_gemm_plan* out);
 
-/* Scratch bytes ek_gemm / ek_gemm_fp8 need for this call (plan.workspace_bytes);
- * 0 when the schedule does not split. Returns (size_t)-1 on invalid input. */
+/* Scratch bytes ek_gemm / ek_gemm_fp8 need for this call: plan.workspace_bytes
+ * (0 when the schedule does not split), plus, for a bf16 / fp16 shape with N
+ * not a multiple of 8 or K not a multiple of 16, the zero-padded operand
+ * copies of that shape. Returns (size_t)-1 on invalid input. */
 size_t ek_gemm_workspace_bytes(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn,
                                int force_split);
 
 /* C[M,N] = A[M,K] @ B, fp32 accumulate, C in the input dtype (bf16 / fp16).
- * A row-major [M,K]; B per b_layout. K and N must be multiples of 8; all
- * pointers 16-byte aligned. workspace: ws_bytes of device memory holding
- * plan.workspace_bytes bytes, zero-filled before its first use; the kernel
- * leaves it zero-filled again (its split counters), so it can be reused by
- * later calls on the same stream. */
+ * A row-major [M,K]; B per b_layout; any M, N, K >= 1 (the reference's kernel
+ * masks every edge, sm_aware_matmul.py:164-172): when N is not a multiple of 8
+ * or K not a multiple of 16 the operands that need it are copied on the device
+ * into zero-padded buffers inside the workspace, and the product's first N
+ * columns are copied back into C. All pointers 16-byte aligned. workspace:
+ * ws_bytes >= ek_gemm_workspace_bytes(...) bytes of device memory, zero-filled
+ * before its first use; the kernel leaves its split counters at the front
+ * zero-filled again, so it can be reused by later calls on the same stream. */
 int ek_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,
             int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
 
 /* FP8 e4m3 GEMM with per-row activation scales and per-output-channel weight
  * scales: C[M,N] = (A[M,K] * a_scale[M]) @ (W[N,K] * w_scale[N])^T, bf16 C.
- * No counterpart kernel in the reference (it has no FP8 path). */
+ * N must be a multiple of 8 and K of 16. No counterpart kernel in the
+ * reference (it has no FP8 path). */
 int ek_gemm_fp8(const void* A, const void* W, const float* a_scale, const float* w_scale, void* C, int M, int N,
                 int K, int num_sms, int force_bn, int force_split, void* workspace, size_t ws_bytes, void* stream);
 
@@ -168,7 +174,11 @@ int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows
  * the device. Schedules needing more scratch fail with EK_ERR_UNSUPPORTED.
  * All calls on a device share the array: calls that overlap on the GPU race
  * and must be serialised by the caller. The first call on a device looks up
- * the array's address; make it before any stream capture on that device. */
+ * the array's address; make it before any stream capture on that device.
+ * That address is cached per device index for the life of the process and
+ * does not survive cudaDeviceReset (or any teardown of the device's primary
+ * context): after one, later calls would hand the kernel a stale address, so
+ * do not use this entry point again in that process. */
 int ek_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int dtype, int b_layout, int num_sms,
                     int force_bn, int force_split, void* stream);
 size_t ek_gemm_noalloc_max_scratch_bytes(void);

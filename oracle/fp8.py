@@ -50,3 +50,13 @@ def dequant_blocks(q: torch.Tensor, s: np.ndarray, br: int, bc: int) -> np.ndarr
     Q = q.to(torch.float32).numpy()
     S = np.repeat(np.repeat(s, br, axis=0), bc, axis=1)[:Q.shape[0], :Q.shape[1]]
     return Q * S
+
+
+def dequant_block_rows(q: torch.Tensor, s: np.ndarray, block: int = 128) -> np.ndarray:
+    """fp32 values of e4m3 codes q [R, C] with block x block scales s
+    [R/block, C/block] (R and C multiples of block): the same values as
+    dequant_blocks, by broadcasting instead of materialising the scale grid."""
+    Q = q.to(torch.float32).numpy()
+    R, C = Q.shape
+    S = np.asarray(s, dtype=np.float32).reshape(R // block, 1, C // block, 1)
+    return (Q.reshape(R // block, block, C // block, block) * S).reshape(R, C)

@@ -3,6 +3,7 @@
 * route_ref      softmax -> top-k -> renormalise      sm_aware_agent/definition.py:152-153
 * permute_ref    moe_align_block_size-style layout    (no reference code: defined here)
 * moe_ref        SwiGLU experts + weighted combine    sm_aware_agent/definition.py:155-170
+* moe_ref_by_expert  the same, one expert's weights fetched at a time (large layers)
 * combine_ref    top-k sum of weighted expert rows     sm_aware_agent/definition.py:168 (sum over choices)
 * moe_loop_ref   the definition's literal per-token loop in torch (CPU baseline)
 * moe_vec_ref    vectorised per-expert torch restatement (CPU baseline at all T)
@@ -103,6 +104,28 @@ def moe_ref(x, logits, w1, w2, w3, topk: int, ids=None, weights=None) -> np.ndar
         y = act @ W2[e].T
         wt = weights[t_idx, j_idx][:, None]
         np.add.at(out, t_idx, wt * y)
+    return out
+
+
+def moe_ref_by_expert(x, ids, weights, num_experts: int, expert_weights) -> np.ndarray:
+    """fp32 MoE output [T, H] for tokens x [T, H] with their routing (ids,
+    weights [T, k]), the definition.py:155-170 math, fetching one expert's
+    weights at a time: expert_weights(e) -> (w1_e [I, H], w2_e [H, I],
+    w3_e [I, H]) as fp32 arrays. Used on sampled tokens of layers whose weights
+    are too large to hold in fp32 all at once (Mixtral, 256-expert FP8 layers);
+    experts no sampled token routes to are never fetched."""
+    X = to_f32(x)
+    ids = np.asarray(ids)
+    weights = np.asarray(weights, dtype=np.float32)
+    out = np.zeros(X.shape, dtype=np.float32)
+    for e in range(num_experts):
+        t_idx, j_idx = np.nonzero(ids == e)
+        if t_idx.size == 0:
+            continue
+        w1e, w2e, w3e = expert_weights(e)
+        h = X[t_idx]
+        act = _silu(h @ w1e.T) * (h @ w3e.T)
+        np.add.at(out, t_idx, weights[t_idx, j_idx][:, None] * (act @ w2e.T))
     return out
 
 

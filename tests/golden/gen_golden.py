@@ -1,9 +1,10 @@
 """Generate the golden vectors in tests/golden/ by running the reference's own code.
 
-Run in a container that has the reference checked out (read-only) at
-REFERENCE_ROOT (default /root/reference) and Triton installed:
+Run in a container that has the reference checked out (read-only) and
+Triton installed, naming the checkout's root (the directory that holds the
+`elastikernel/` package):
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py --reference-root <path>
 
 What it records (all small; the files are committed and the tests read only
 them, never the reference):
@@ -40,7 +41,7 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+REF: Path = None  # the reference checkout's root, set from --reference-root
 OUT = Path(__file__).resolve().parent
 
 
@@ -208,4 +209,12 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="regenerate tests/golden/ from the reference's own code")
+    ap.add_argument("--reference-root", required=True, type=Path,
+                    help="root of the reference checkout (holds the elastikernel/ package)")
+    REF = ap.parse_args().reference_root.resolve()
+    if not (REF / "elastikernel" / "sm_aware_matmul.py").exists():
+        raise SystemExit(f"{REF} does not hold the reference's elastikernel/ package")
     main()

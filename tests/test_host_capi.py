@@ -229,3 +229,27 @@ def test_padded_block_m_policy():
     assert padded_block_m(1, 8, 2 * 4096) == 128
     assert padded_block_m(72, 8, 2 * 1024) == 256
     assert padded_block_m(72, 8, 2 * 512) == 128
+
+
+def test_ragged_gemm_workspace_sizes():
+    """Ragged bf16 / fp16 shapes (N % 8 or K % 16 non-zero) need room for the
+    zero-padded operand copies behind the split-K ticket region; aligned
+    shapes need exactly the plan's split scratch; e4m3 stays strict."""
+    from elastikernel_b200 import _lib, _ops
+
+    L = _lib.lib()
+    bf, kn, nk = _lib.EK_DTYPE_BF16, _lib.EK_B_KN, _lib.EK_B_NK
+
+    def r256(x):
+        return -(-x // 256) * 256
+
+    # M=77 N=100 K=100: A -> [77, 112], [K, N] B -> [100, 104], C through [77, 104]
+    got = L.ek_gemm_workspace_bytes(77, 100, 100, 148, bf, kn, 0, 0)
+    assert got == 8192 + r256(77 * 112 * 2) + r256(100 * 104 * 2) + r256(77 * 104 * 2)
+    # [N, K] weights with a ragged K: A and B padded along K, C needs no copy
+    got = L.ek_gemm_workspace_bytes(64, 128, 100, 148, bf, nk, 0, 0)
+    assert got == 8192 + r256(64 * 112 * 2) + r256(128 * 112 * 2)
+    # aligned: the split scratch of the plan only
+    for M, N, K, S in ((4096, 4096, 4096, 148), (512, 1024, 1024, 148)):
+        assert L.ek_gemm_workspace_bytes(M, N, K, S, bf, kn, 0, 0) == _ops.plan(M, N, K, S)["workspace_bytes"]
+    assert L.ek_gemm_workspace_bytes(64, 100, 128, 148, _lib.EK_DTYPE_E4M3, nk, 0, 0) == ctypes.c_size_t(-1).value

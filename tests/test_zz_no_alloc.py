@@ -68,3 +68,29 @@ def test_noalloc_rejects_oversized_schedule(cuda_dev):
     rc = _noalloc(a, b, c, M, N, K, "kn", 148, 256, 8)  # 68 tail tiles x 8 slices x 128 KB > 32 MiB
     assert rc == _lib.EK_ERR_UNSUPPORTED
     assert "scratch" in _lib.last_error()
+
+
+@pytest.mark.parametrize("req_sms", [16, 96])
+def test_noalloc_on_green_context_partition(cuda_dev, req_sms):
+    """Called on a green-context partition's stream with num_sms = 0, the entry
+    point sizes its grid from the partition registry, as ek_gemm does, and
+    gives ek_gemm's result there, on two calls in a row."""
+    from elastikernel_b200 import _lib, _ops
+    from elastikernel_b200.green_ctx import create_sm_partition
+
+    stream, actual = create_sm_partition(cuda_dev, req_sms)
+    M, N, K = 4096, 4096, 4096
+    g = torch.Generator(device=cuda_dev).manual_seed(req_sms)
+    a = torch.randn((M, K), device=cuda_dev, dtype=torch.bfloat16, generator=g)
+    b = torch.randn((K, N), device=cuda_dev, dtype=torch.bfloat16, generator=g)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ref = _ops.gemm(a, b)  # plans for the partition from the registry
+        for _ in range(2):
+            c = torch.full((M, N), float("nan"), device=cuda_dev, dtype=torch.bfloat16)
+            rc = _noalloc(a, b, c, M, N, K, "kn", 0)
+            assert rc == 0, _lib.last_error()
+            stream.synchronize()
+            assert _lib.device_status(0) == 0
+            err = max_rel_err(c, ref.float().cpu().numpy())
+            assert err <= TOL, f"{actual}-SM partition: max rel err {err:.3e}"
