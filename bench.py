@@ -11,10 +11,17 @@ Also on the same line:
 * e2e       the same metric through the public API (sm_aware_matmul.call_sm_aware)
             with pinned host buffers: H2D of A and B, the GEMM, D2H of C per step
 * roofline  achieved TFLOP/s of the GEMM kernel vs the measured bf16 peak
-* partitions  4096^3 on green-context partitions of {16,32,64,96,132,148} SMs,
-            % of the SM-scaled peak, plus the M sweep at 148 SMs
+* partitions  4096^3 on green-context partitions of {16,32,64,96,132,148} SMs:
+            % of the partition's own peak (SMs x 8192 FLOP/clk x the median SM
+            clock sampled while it ran) and of cuBLAS 8192^3 in the same
+            partition, cuBLAS 4096^3 beside it; the M sweep at 148 SMs
+* fp8       e4m3 GEMM 4096 x 14336 x 4096 (per-row / per-channel scales)
 * moe       Mixtral-shaped fused MoE tokens/s at T in {1,16,128,1024,4096}
+* moe_cpu   the reference's CPU MoE operator on the box's host cores
+* moe_ep    DeepSeek-V3-shaped FP8 expert-parallel layer: phases, NVLink
+            bytes, and its output checked against the oracle on a token sample
 * cpu_baseline  the reference's CPU GEMM (torch.matmul on CPU) on a bounded sample
+* summary   (the line's last key) the figures above in compact form
 
 `--impl reference` times the reference's own CPU implementation of the path
 (the oracle restatement of the GEMM operator, torch.matmul on CPU bf16) on the
@@ -24,13 +31,14 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
@@ -43,6 +51,8 @@ FLOP = 2.0 * M * N * K
 METRIC = "bf16 GEMM TFLOP/s per green-ctx partition (4096^3, 148-SM full device)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+# dense bf16 / fp16 MMA rate of one B200 SM per clock (tcgen05); e4m3 is twice it
+MMA_FLOP_PER_CLK_SM = 8192
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -60,9 +70,11 @@ def dist_env() -> tuple[int, int, int]:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region;
+    summary(window) restricts the statistics to samples taken inside a
+    (start, end) wall-clock window (time.time())."""
 
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -98,18 +110,28 @@ class ClockSampler:
                 self.proc.kill()
             self.fh.close()
 
-    def summary(self) -> dict:
+    def _rows(self) -> list:
         rows = []
         try:
             for line in self.path.read_text().splitlines():
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
                     continue
-                if self.uuid and self.uuid.replace("GPU-", "") not in parts[0]:
+                if self.uuid and self.uuid.replace("GPU-", "") not in parts[1]:
                     continue
-                rows.append(parts)
+                try:
+                    ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    ts = None
+                rows.append([ts] + parts[2:])
         except Exception:
             pass
+        return rows
+
+    def summary(self, window: tuple | None = None) -> dict:
+        rows = self._rows()
+        if window is not None:
+            rows = [r for r in rows if r[0] is not None and window[0] <= r[0] <= window[1]]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
 
@@ -200,7 +222,27 @@ def e2e_pipelined(smm, a_h, b_h, a_like, b_like, steps: int) -> float:
     return start.elapsed_time(end) / steps
 
 
+def _timed_window(fn, stream, min_s: float, max_reps: int = 20000) -> tuple[dict, tuple]:
+    """time_on_stream of fn with enough repetitions to last about min_s (so the
+    clock sampler sees several samples), and the wall-clock window it ran in."""
+    from elastikernel_b200.timing import time_on_stream
+
+    probe = time_on_stream(fn, stream, reps=3)
+    per_ms = probe["mean_ms"] + 0.05  # + the L2 flush between repetitions
+    reps = int(min(max_reps, max(3, math.ceil(min_s * 1e3 / per_ms))))
+    torch.cuda.synchronize()
+    t0 = time.time()
+    r = time_on_stream(fn, stream, reps=reps)
+    return r, (t0, time.time())
+
+
 def partition_sweep(dev, peak_tflops: float, steps: int, hbm_gbs: float = FALLBACK_PEAKS["hbm_gbs"]) -> dict:
+    """4096^3 bf16 on each partition size, with the partition's own peak as
+    denominator: SMs x 8192 FLOP/clk x the median SM clock sampled while the
+    GEMM ran (`pct_sm_peak_at_clock`), and cuBLAS 8192^3 launched in the same
+    partition (`pct_cublas_8192`). cuBLAS 4096^3 in the same partition is the
+    vendor comparator. Then the M sweep at 148 SMs, CUDA-graph timed, with the
+    max(tensor, HBM) floor and cuBLAS beside it."""
     from elastikernel_b200 import sm_aware_matmul as smm
     from elastikernel_b200.green_ctx import create_sm_partition, full_device_partition, get_total_sm_count
     from elastikernel_b200.timing import time_on_stream
@@ -210,26 +252,46 @@ def partition_sweep(dev, peak_tflops: float, steps: int, hbm_gbs: float = FALLBA
     out = {"square_4096": [], "m_sweep_148": []}
     a = torch.randn((M, K), device=dev, dtype=torch.bfloat16, generator=g)
     b = torch.randn((K, N), device=dev, dtype=torch.bfloat16, generator=g)
-    for S in [16, 32, 64, 96, 132, 148]:
-        try:
-            stream, actual = full_device_partition(dev) if S >= total else create_sm_partition(dev, S)
-            with torch.cuda.stream(stream):
-                for _ in range(2):
-                    smm.call_sm_aware(a, b)
-                r = time_on_stream(lambda: smm.call_sm_aware(a, b), stream, reps=max(3, steps // 2))
-            p = smm.tcgen05_schedule(M, N, K, actual)
-            tf = FLOP / (r["mean_ms"] * 1e-3) / 1e12
-            out["square_4096"].append({"sm": S, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
-                                       "tflops": round(tf, 1),
-                                       "pct_scaled_peak": round(100 * tf / (peak_tflops * actual / 148), 1),
-                                       "bn": p["bn"], "split": p["tail_split"],
-                                       "wave_eff": round(p["wave_efficiency"], 3)})
-        except Exception as e:  # report and continue, as the reference benchmark does
-            out["square_4096"].append({"sm": S, "error": str(e)[:200]})
+    a8 = torch.randn((8192, 8192), device=dev, dtype=torch.bfloat16, generator=g)
+    b8 = torch.randn((8192, 8192), device=dev, dtype=torch.bfloat16, generator=g)
+    sampler = ClockSampler(dev)
+    with sampler:
+        for S in [16, 32, 64, 96, 132, 148]:
+            try:
+                stream, actual = full_device_partition(dev) if S >= total else create_sm_partition(dev, S)
+                with torch.cuda.stream(stream):
+                    for _ in range(2):
+                        smm.call_sm_aware(a, b)
+                    r, win = _timed_window(lambda: smm.call_sm_aware(a, b), stream, min_s=1.0)
+                    torch.matmul(a, b)
+                    rc = time_on_stream(lambda: torch.matmul(a, b), stream, reps=max(3, steps // 2))
+                    torch.matmul(a8, b8)
+                    rc8 = time_on_stream(lambda: torch.matmul(a8, b8), stream, reps=3)
+                clk = sampler.summary(win)
+                p = smm.tcgen05_schedule(M, N, K, actual)
+                tf = FLOP / (r["mean_ms"] * 1e-3) / 1e12
+                tf_cub = FLOP / (rc["mean_ms"] * 1e-3) / 1e12
+                tf_cub8 = 2.0 * 8192 ** 3 / (rc8["min_ms"] * 1e-3) / 1e12
+                rec = {"sm": S, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
+                       "us_median": round(r["median_ms"] * 1e3, 1), "reps": r["reps"], "tflops": round(tf, 1),
+                       "sm_mhz": clk["sm_mhz"], "clock_samples": clk["samples"],
+                       "cublas_us": round(rc["mean_ms"] * 1e3, 1), "cublas_tflops": round(tf_cub, 1),
+                       "speedup_vs_cublas": round(rc["mean_ms"] / r["mean_ms"], 3),
+                       "cublas_8192_tflops": round(tf_cub8, 1), "pct_cublas_8192": round(100 * tf / tf_cub8, 1),
+                       "bm": p["bm"], "bn": p["bn"], "split": p["tail_split"],
+                       "wave_eff": round(p["wave_efficiency"], 3)}
+                if clk["sm_mhz"]:
+                    peak_clk = actual * MMA_FLOP_PER_CLK_SM * clk["sm_mhz"] * 1e6 / 1e12
+                    rec["peak_at_clock_tflops"] = round(peak_clk, 1)
+                    rec["pct_sm_peak_at_clock"] = round(100 * tf / peak_clk, 1)
+                out["square_4096"].append(rec)
+            except Exception as e:  # report and continue, as the reference benchmark does
+                out["square_4096"].append({"sm": S, "error": str(e)[:200]})
+    del a8, b8
     # M sweep: the GEMM replayed from a CUDA graph (device time of the kernel;
     # an eager call's host work -- planning, tensor maps, the ctypes launch --
     # outlasts the L2 flush for the small M and would be timed too), with the
-    # eager call's time beside it, and the max(tensor, HBM) floor.
+    # eager call's time beside it, cuBLAS, and the max(tensor, HBM) floor.
     for Mi in [128, 256, 512, 1024, 2048, 4096, 8192]:
         a2 = torch.randn((Mi, K), device=dev, dtype=torch.bfloat16, generator=g)
         for _ in range(2):
@@ -237,6 +299,8 @@ def partition_sweep(dev, peak_tflops: float, steps: int, hbm_gbs: float = FALLBA
         r_eager = time_on_stream(lambda: smm.call_sm_aware(a2, b), reps=max(3, steps // 2))
         gm = smm.GraphMatmul(a2, b, num_sms=total)
         r = time_on_stream(gm, reps=max(3, steps // 2))
+        torch.matmul(a2, b)
+        rc = time_on_stream(lambda: torch.matmul(a2, b), reps=max(3, steps // 2))
         flop = 2.0 * Mi * N * K
         nbytes = 2.0 * (Mi * K + K * N + Mi * N)
         floor_us = max(flop / (peak_tflops * 1e12), nbytes / (hbm_gbs * 1e9)) * 1e6
@@ -244,6 +308,7 @@ def partition_sweep(dev, peak_tflops: float, steps: int, hbm_gbs: float = FALLBA
         p = smm.tcgen05_schedule(Mi, N, K, total)
         out["m_sweep_148"].append({"M": Mi, "us": round(r["mean_ms"] * 1e3, 1),
                                    "us_eager": round(r_eager["mean_ms"] * 1e3, 1), "tflops": round(tf, 1),
+                                   "cublas_us": round(rc["mean_ms"] * 1e3, 1),
                                    "pct_peak": round(100 * tf / peak_tflops, 1),
                                    "pct_roofline_time": round(100 * floor_us / (r["mean_ms"] * 1e3), 1),
                                    "bound": "tensor" if flop / (peak_tflops * 1e12) >= nbytes / (hbm_gbs * 1e9)
@@ -273,11 +338,26 @@ def fp8_bench(dev, peak_bf16_tflops: float, steps: int) -> dict:
             for _ in range(2):
                 _ops.gemm_fp8(aq, wq, a_s, w_s)
             r = time_on_stream(lambda: _ops.gemm_fp8(aq, wq, a_s, w_s), stream, reps=max(3, steps // 2))
+            cub = None
+            try:  # the vendor path for the same math: torch._scaled_mm with row-wise scales
+                def scaled():
+                    return torch._scaled_mm(aq, wq.t(), scale_a=a_s.view(-1, 1), scale_b=w_s.view(1, -1),
+                                            out_dtype=torch.bfloat16)
+                scaled()
+                cub = time_on_stream(scaled, stream, reps=max(3, steps // 2))["mean_ms"]
+            except Exception as e:  # not every torch build has row-wise scaled FP8 on this GPU
+                cub = str(e)[:120]
         tf = flop / (r["mean_ms"] * 1e-3) / 1e12
         p = _ops.plan(Mf, Nf, Kf, actual, _ops._FP8, "nk")
-        res.append({"sm_request": req, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
-                    "tflops": round(tf, 1), "pct_scaled_fp8_peak": round(100 * tf / (peak_fp8 * actual / 148), 1),
-                    "bm": p["bm"], "bn": p["bn"], "split": p["tail_split"]})
+        rec = {"sm_request": req, "actual_sm": actual, "us": round(r["mean_ms"] * 1e3, 1),
+               "tflops": round(tf, 1), "pct_scaled_fp8_peak": round(100 * tf / (peak_fp8 * actual / 148), 1),
+               "bm": p["bm"], "bn": p["bn"], "split": p["tail_split"]}
+        if isinstance(cub, float):
+            rec["torch_scaled_mm_us"] = round(cub * 1e3, 1)
+            rec["speedup_vs_torch_scaled_mm"] = round(cub / r["mean_ms"], 3)
+        else:
+            rec["torch_scaled_mm"] = cub
+        res.append(rec)
     return {"config": "e4m3 4096x14336x4096, per-row A / per-channel W fp32 scales, bf16 out",
             "fp8_peak_tflops": peak_fp8, "peak_note": "2 x measured bf16 burst", "results": res}
 
@@ -286,9 +366,8 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
     """DeepSeek-V3-shaped expert-parallel MoE: 256 experts, top-8 softmax
     routing, H=7168, I=2048, e4m3 experts with 128 x 128 block scales, 4096
     tokens per rank, 256/world experts per rank, e4m3 dispatch over NCCL
-    all-to-all. The expert GEMMs run in a 112-SM green-context partition
-    disjoint from a 32-SM one (a 116-SM request rounds up to 120, which with
-    32 exceeds 148)."""
+    all-to-all. The expert GEMMs run in a 116-SM green-context partition, the
+    remainder of a 32-SM one split off for the collectives."""
     from elastikernel_b200 import _ops
     from elastikernel_b200.ep_moe import CudaEPOps, ExpertParallelMoE
     from elastikernel_b200.green_ctx import create_disjoint_partitions, get_total_sm_count
@@ -316,10 +395,10 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
     logits = torch.randn((T, E), device=dev, generator=gx)
     total = get_total_sm_count(dev)
     if total >= 148:
-        (comm_stream, comm_sms), (gemm_stream, gemm_sms) = create_disjoint_partitions(dev, [32, 112])
+        (comm_stream, comm_sms), (gemm_stream, gemm_sms) = create_disjoint_partitions(dev, [32], with_remainder=True)
     else:
         gemm_stream, gemm_sms = torch.cuda.current_stream(dev), total
-        comm_stream = torch.cuda.Stream(dev)
+        comm_stream, comm_sms = torch.cuda.Stream(dev), 0
     moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms))
     # Two chunks let the dispatch / combine of one half overlap the expert
     # GEMMs of the other, but each chunk streams every local expert's weights
@@ -341,24 +420,89 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(main)
         for _ in range(reps):
-            layer()
+            out = layer()
         e.record(main)
         torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+    # phase split of one unchunked layer (device time between phase events on
+    # the experts' partition stream; NCCL inside the same timeline)
+    barrier(world)
+    with torch.cuda.stream(gemm_stream):
+        prof = moe.profile_phases(x, logits)
+    phases = {kk: round(max_over_ranks(v, world), 3) for kk, v in prof["ms"].items()}
+    a2a = {"dispatch_bytes_per_rank": prof["dispatch_bytes"], "combine_bytes_per_rank": prof["combine_bytes"]}
+    if world > 1:
+        for key, ph in (("dispatch", "dispatch"), ("combine", "combine_exchange")):
+            t = phases.get(ph, 0.0)
+            a2a[f"{key}_gbs_per_rank"] = round(prof[f"{key}_bytes"] / (t * 1e-3) / 1e9, 1) if t > 0 else None
+    err = ep_parity(dev, x, logits, out, qw, E, k, world, rank)
     flop = T * k * 6.0 * H * I
     tf = flop / (ms * 1e-3) / 1e12
     peak_fp8 = 2.0 * peak_bf16_tflops
     return {"config": "DeepSeek-V3-shaped: E=256 top-8 H=7168 I=2048, e4m3 128x128 block scales, 4096 tokens/rank, "
                       f"{eg} experts/rank, e4m3 dispatch via NCCL all-to-all",
             "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
-            "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms,
+            "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms, "comm_partition_sms": comm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
-            "chunks": chunks,
+            "chunks": chunks, "phases_ms_unchunked": phases, "all_to_all": a2a,
+            "ep_max_rel_err": err, "ep_parity_tol": 3e-2,
             "host_sync": "per-chunk count exchange read on the host (all-to-all split sizes)"}
 
 
-def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:
-    """Mixtral-shaped fused MoE (E=8, top-2, H=4096, I=14336, bf16) tokens/s."""
+def ep_parity(dev, x, logits, out, qw, E: int, k: int, world: int, rank: int, per_rank: int = 32) -> float:
+    """The checker of the expert-parallel layer (outside every timed region):
+    `per_rank` seeded tokens of each rank are compared with the CPU oracle on
+    the dequantised inputs. Experts live on different ranks, so the oracle is
+    distributed the same way: the sampled tokens are gathered on every rank,
+    each rank computes with the oracle the contribution of ITS experts to
+    every sampled token, and a sum over ranks gives each token's reference.
+    Returns the max over ranks of max|out - ref| / max|ref|."""
+    import numpy as np
+
+    from oracle import fp8 as of8
+    from oracle import gemm as og
+    from oracle import moe as om
+
+    T, H = x.shape
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // max(1, world)))
+    rng = np.random.default_rng(7 + rank)
+    idx = sorted(rng.choice(T, size=per_rank, replace=False).tolist())
+    xs, ls = x[idx].contiguous(), logits[idx].contiguous()
+    if world > 1:
+        import torch.distributed as dist
+
+        xs_all = torch.empty((world * per_rank, H), dtype=xs.dtype, device=dev)
+        ls_all = torch.empty((world * per_rank, logits.shape[1]), dtype=ls.dtype, device=dev)
+        dist.all_gather_into_tensor(xs_all, xs)
+        dist.all_gather_into_tensor(ls_all, ls)
+    else:
+        xs_all, ls_all = xs, ls
+    ids, wts = om.route_ref(ls_all.cpu().numpy(), k)
+    eg = E // world
+    lo = rank * eg
+    ids_local = np.where((ids >= lo) & (ids < lo + eg), ids - lo, -1)
+    xd = of8.dequant_blocks(*of8.quant_blocks(xs_all.cpu(), 1, 128), 1, 128)  # e4m3 rows, as dispatched
+    nI, nH = qw["I"] // 128, qw["H"] // 128
+
+    def fetch(e):
+        w1e = of8.dequant_block_rows(qw["w1q"][e].cpu(), qw["w1s"][e * nI:(e + 1) * nI].cpu().numpy())
+        w3e = of8.dequant_block_rows(qw["w3q"][e].cpu(), qw["w3s"][e * nI:(e + 1) * nI].cpu().numpy())
+        w2e = of8.dequant_block_rows(qw["w2q"][e].cpu(), qw["w2s"][e * nH:(e + 1) * nH].cpu().numpy())
+        return w1e, w2e, w3e
+
+    part = torch.from_numpy(om.moe_ref_by_expert(xd, ids_local, wts, eg, fetch)).to(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(part)
+    ref = part[rank * per_rank:(rank + 1) * per_rank].cpu().numpy()
+    err = og.max_rel_err(out[idx], ref)
+    return round(max_over_ranks(err, world), 6)
+
+
+def moe_bench(dev, steps: int, hbm_gbs: float, peak_bf16_tflops: float, cpu: bool = False) -> dict:
+    """Mixtral-shaped fused MoE (E=8, top-2, H=4096, I=14336, bf16) tokens/s;
+    with cpu=True also the reference's CPU operator on the same weights."""
     from elastikernel_b200 import _ops
     from elastikernel_b200.graph import Captured
     from elastikernel_b200.green_ctx import create_sm_partition
@@ -391,15 +535,48 @@ def moe_bench(dev, steps: int, hbm_gbs: float) -> dict:
             tg_s = rg["mean_ms"] * 1e-3
             flop = T * k * 6.0 * H * I
             wbytes = hit * 3.0 * H * I * 2
-            t_floor = max(flop / (1.6654e15 * sms / 148), wbytes / (hbm_gbs * 1e9))
+            t_floor = max(flop / (peak_bf16_tflops * 1e12 * sms / 148), wbytes / (hbm_gbs * 1e9))
             res.append({"T": T, "sms": label, "actual_sm": sms, "us": round(r["mean_ms"] * 1e3, 1),
                         "tokens_per_s": round(T / t_s, 1), "tflops": round(flop / t_s / 1e12, 1),
                         "experts_hit": hit, "pct_roofline_time": round(100 * t_floor / t_s, 1),
                         "graph_us": round(rg["mean_ms"] * 1e3, 1), "graph_tokens_per_s": round(T / tg_s, 1),
                         "graph_pct_roofline_time": round(100 * t_floor / tg_s, 1)})
-    return {"config": "Mixtral E=8 k=2 H=4096 I=14336 bf16, weights N(0,0.02); us = eager launches from "
-                      "Python, graph_us = the layer replayed from a CUDA graph",
-            "results": res}
+    out = {"config": "Mixtral E=8 k=2 H=4096 I=14336 bf16, weights N(0,0.02); us = eager launches from "
+                     "Python, graph_us = the layer replayed from a CUDA graph; roofline = max(tensor at the "
+                     "measured bf16 burst x SMs/148, expert weights at the measured HBM rate)",
+           "results": res}
+    if cpu:
+        out["cpu"] = moe_cpu_baseline(w1, w2, w3, E, k, H)
+    return out
+
+
+def moe_cpu_baseline(w1, w2, w3, E: int, k: int, H: int) -> dict:
+    """The reference's CPU implementation of the MoE operator on the host
+    cores, same weights (bf16) and shapes: the definition's per-token loop
+    (definition.py:152-168) at T <= 16 and the vectorised per-expert
+    restatement at every T, each a bounded sample (one or two layers)."""
+    from oracle import cpu_baseline
+
+    threads = cpu_baseline.set_threads()
+    cw1, cw2, cw3 = w1.cpu(), w2.cpu(), w3.cpu()
+    g = torch.Generator().manual_seed(42)
+    res = []
+    for T in [1, 16, 128, 1024, 4096]:
+        x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        logits = torch.randn((T, E), generator=g)
+        rec = {"T": T}
+        for label, loop in (("loop", True), ("vectorised", False)):
+            if loop and T > 16:
+                continue
+            r = cpu_baseline.time_moe(x, logits, cw1, cw2, cw3, k, loop=loop, reps=2 if T <= 128 else 1,
+                                      budget_s=15.0)
+            mean_s = statistics.fmean(r["seconds"])
+            rec[f"{label}_ms"] = round(mean_s * 1e3, 2)
+            rec[f"{label}_tokens_per_s"] = round(T / mean_s, 1)
+        res.append(rec)
+    return {"cores": threads, "kind": "port", "dtype": "bf16",
+            "sample": "one or two Mixtral layers per T on CPU tensors (definition loop at T<=16, vectorised "
+                      "per-expert torch at every T)", "results": res}
 
 
 def cpu_baseline_sample() -> dict:
@@ -519,7 +696,7 @@ def main() -> None:
     if not args.no_extras:
         extras["partitions"] = partition_sweep(dev, peak_tf, args.steps, hbm)
         extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
-        extras["moe"] = moe_bench(dev, args.steps, hbm)
+        extras["moe"] = moe_bench(dev, args.steps, hbm, peak_tf, cpu=(rank == 0 and world == 1))
         extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
         if rank == 0 and world == 1:
             extras["cpu_baseline"] = cpu_baseline_sample()
@@ -554,7 +731,48 @@ def main() -> None:
     if "cpu_baseline" in extras:
         line["cpu_baseline"] = extras.pop("cpu_baseline")
     line.update(extras)
+    line["summary"] = summarize(line)  # last key: a driver that keeps the line's tail keeps this
     print(json.dumps(line), flush=True)
+
+
+def summarize(line: dict) -> dict:
+    """The line's figures in compact form (lists in a fixed, stated order)."""
+    sm = {}
+    sm["headline"] = [line["value"], line["roofline"]["frac"], line["e2e"]["value"], line["clocks"].get("sm_mhz")]
+    sm["headline_order"] = "TFLOP/s, frac of measured burst, e2e TFLOP/s, median SM MHz"
+    parts = line.get("partitions")
+    if parts:
+        sm["partitions_order"] = ("SMs: us, TFLOP/s, % SMs x 8192 x sampled clock, MHz, % cuBLAS 8192^3 there, "
+                                  "x vs cuBLAS 4096^3 there")
+        sm["partitions"] = {str(r["actual_sm"]): [r["us"], r["tflops"], r.get("pct_sm_peak_at_clock"), r["sm_mhz"],
+                                                  r["pct_cublas_8192"], r["speedup_vs_cublas"]]
+                            for r in parts["square_4096"] if "error" not in r}
+        sm["m_sweep_order"] = "M: graph us, % max(tensor, HBM) roofline time, cuBLAS us"
+        sm["m_sweep"] = {str(r["M"]): [r["us"], r["pct_roofline_time"], r["cublas_us"]] for r in parts["m_sweep_148"]}
+    fp8 = line.get("fp8")
+    if fp8:
+        sm["fp8_order"] = "SMs: TFLOP/s, % 2 x burst x SMs/148, x vs torch._scaled_mm"
+        sm["fp8"] = {str(r["actual_sm"]): [r["tflops"], r["pct_scaled_fp8_peak"], r.get("speedup_vs_torch_scaled_mm")]
+                     for r in fp8["results"]}
+    moe = line.get("moe")
+    if moe:
+        sm["moe_order"] = "T/partition: eager us, % roofline time, graph us, % roofline time"
+        sm["moe"] = {f"{r['T']}/{r['actual_sm']}": [r["us"], r["pct_roofline_time"], r["graph_us"],
+                                                     r["graph_pct_roofline_time"]] for r in moe["results"]}
+        if "cpu" in moe:
+            sm["moe_cpu_order"] = f"T: vectorised tokens/s, loop tokens/s ({moe['cpu']['cores']} cores)"
+            sm["moe_cpu"] = {str(r["T"]): [r.get("vectorised_tokens_per_s"), r.get("loop_tokens_per_s")]
+                             for r in moe["cpu"]["results"]}
+    ep = line.get("moe_ep")
+    if ep:
+        sm["moe_ep"] = {"n_gpus": ep["n_gpus"], "ms": ep["ms_per_layer"], "tokens_per_s": ep["tokens_per_s"],
+                        "pct_fp8_peak_scaled": ep["pct_fp8_peak_scaled"], "gemm_sms": ep["gemm_partition_sms"],
+                        "ep_max_rel_err": ep["ep_max_rel_err"], "phases_ms": ep["phases_ms_unchunked"],
+                        "a2a_gbs": [ep["all_to_all"].get("dispatch_gbs_per_rank"),
+                                    ep["all_to_all"].get("combine_gbs_per_rank")]}
+    if "cpu_baseline" in line:
+        sm["cpu_gemm_tflops"] = [line["cpu_baseline"]["value"], line["cpu_baseline"]["cores"]]
+    return sm
 
 
 if __name__ == "__main__":

@@ -59,6 +59,7 @@ _SIGNATURES = {
     "ek_device_status": (_c_int, [_c_int, _c_int, _c_ip]),
     "ek_device_sm_info": (_c_int, [_c_int, _c_ip, _c_ip, _c_ip, _c_ip, _c_ip]),
     "ek_gctx_create": (_c_int, [_c_int, _c_ip, _c_int, _c_int, ctypes.POINTER(_c_vp), _c_ip]),
+    "ek_gctx_create_remainder": (_c_int, [_c_int, _c_ip, _c_int, ctypes.POINTER(_c_vp), _c_ip]),
     "ek_gctx_stream_sm_count": (_c_int, [_c_vp, _c_ip]),
     "ek_gctx_destroy_all": (_c_int, []),
     "ek_gctx_fake_driver": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),

@@ -286,7 +286,7 @@ RaggedLayout ragged_layout(int M, int N, int K, int b_layout, size_t split_bytes
   L.a_off = off;
   if (L.pad_a) off += round256((size_t)M * L.Kp * 2);
   L.b_off = off;
-  if (L.pad_b) off += round256(b_layout == EK_B_KN ? (size_t)K * L.Np * 2 : (size_t)L.Np * L.Kp * 2);
+  if (L.pad_b) off += round256(b_layout == EK_B_KN ? (size_t)K * L.Np * 2 : (size_t)N * L.Kp * 2);
   L.c_off = off;
   if (L.pad_c) off += round256((size_t)M * L.Np * 2);
   L.total = off;
@@ -383,10 +383,12 @@ int gemm_common(const void* A, const void* B, void* C, const float* a_scale, con
     if ((rc = check_cuda(cudaGetLastError(), "pad B"))) return rc;
   }
   if (L.pad_c) C2 = ws + L.c_off;
-  // the padded product: K padded for A ([M, Kp]) and for a [N, K] B; a [K, N]
-  // B keeps K rows and the descriptor's bounds supply the zero rows
+  // the padded product [M, Np] over Kp. B keeps its true row count in the
+  // descriptor (K rows of a [K, Np] B, N rows of a [N, Kp] B), so the rows the
+  // padded shape adds are read as zeros through the descriptor's bounds and
+  // never from memory past the buffer.
   rc = launch_dense(plan, A2, B2, C2, a_scale, b_scale, M, Np, Kp, dtype, b_layout, plan.workspace_bytes ? ws : nullptr,
-                    s, b_layout == EK_B_KN ? K : Kp);
+                    s, b_layout == EK_B_KN ? K : N);
   if (rc) return rc;
   if (L.pad_c) {
     unpad_rows_kernel<<<copy_grid((long long)M * N, S), 256, 0, s>>>(static_cast<const uint16_t*>(C2), M, N, Np,
@@ -410,7 +412,7 @@ int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C
   if (b_layout == EK_B_KN)
     rc = make_tmap_2d(&tb, B, tdt, N, b_rows > 0 ? b_rows : K, (uint64_t)N * es, 64, 64);  // [K, N]: 64 N x 64 K boxes
   else
-    rc = make_tmap_2d(&tb, B, tdt, K, N, (uint64_t)K * es, 128 / es, bn_cta);
+    rc = make_tmap_2d(&tb, B, tdt, K, b_rows > 0 ? b_rows : N, (uint64_t)K * es, 128 / es, bn_cta);
   if (rc) return rc;
 
   GemmParams prm{};

@@ -283,7 +283,8 @@ int ek_device_sm_info(int dev, int* total_sms, int* min_sms, int* alignment, int
   return EK_OK;
 }
 
-int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** streams_out, int* actual_out) {
+static int gctx_create(int dev, const int* counts, int n, int disjoint, int with_remainder, void** streams_out,
+                       int* actual_out) {
   if (n < 0 || (n > 0 && (!counts || !streams_out || !actual_out)))
     return set_error(EK_ERR_INVALID, "ek_gctx_create: bad arguments");
   if (n == 0) return EK_OK;
@@ -312,6 +313,8 @@ int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** strea
   }
   if (disjoint && sum > total)
     return set_error(EK_ERR_OVERSUB, "Total requested SMs %lld exceeds device total of %d SMs", sum, total);
+  if (with_remainder && sum >= total)
+    return set_error(EK_ERR_OVERSUB, "Requested SMs %lld leave no remainder of the device's %d SMs", sum, total);
 
   CUdevResource cur = full;
   for (int i = 0; i < n; ++i) {
@@ -328,7 +331,18 @@ int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** strea
     streams_out[i] = s;
     actual_out[i] = actual;
     if (disjoint) {
-      if (i + 1 < n) {
+      if (i + 1 == n && with_remainder) {
+        // The SMs no request took become one more partition (green_ctx.py:110-132
+        // turns the same remainder into a resource for the next split).
+        CUstream rs;
+        rc = make_partition(R, api, cu_dev, &remaining, &rs);
+        if (rc) return rc;
+        const int rem = static_cast<int>(remaining.sm.smCount);
+        if (rem <= 0) return set_error(EK_ERR_OVERSUB, "the split left no SMs for the remainder partition");
+        R.stream_sms[reinterpret_cast<uintptr_t>(rs)] = rem;
+        streams_out[n] = rs;
+        actual_out[n] = rem;
+      } else if (i + 1 < n) {
         // The remainder of a split cannot be split again directly; wrap it in
         // a green context and split that context's SM resource.
         CUdevResourceDesc desc;
@@ -343,6 +357,14 @@ int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** strea
     }
   }
   return EK_OK;
+}
+
+int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** streams_out, int* actual_out) {
+  return gctx_create(dev, counts, n, disjoint, 0, streams_out, actual_out);
+}
+
+int ek_gctx_create_remainder(int dev, const int* counts, int n, void** streams_out, int* actual_out) {
+  return gctx_create(dev, counts, n, 1, 1, streams_out, actual_out);
 }
 
 int ek_gctx_stream_sm_count(void* stream, int* sm_count_out) {

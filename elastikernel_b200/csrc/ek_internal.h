@@ -54,8 +54,9 @@ int plan_dense(int M, int N, int K, int S, int dtype, int b_layout, int force_bn
 // Launch the dense GEMM kernel for `plan` on `stream`. `workspace` must hold
 // plan.workspace_bytes bytes whose ticket region is zero (unused when the
 // plan does not split). a_scale / b_scale only for e4m3.
-// b_rows > 0 sets the row extent of a [K, N] B operand when it differs from K
-// (a padded K whose extra rows the descriptor's bounds fill with zeros).
+// b_rows > 0 sets the true row extent of B (K rows of a [K, N] B, N rows of
+// an [N, K] B) when the launch's K or N is padded past it: the descriptor's
+// bounds then supply zeros for the padded rows.
 int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C, const float* a_scale,
                  const float* b_scale, int M, int N, int K, int dtype, int b_layout, void* workspace,
                  cudaStream_t stream, int b_rows = 0);

@@ -172,6 +172,13 @@ class ExpertParallelMoE:
         self.topk = topk
         self.w1, self.w2, self.w3, self.qw = w1, w2, w3, qw
         self.ops = ops or CudaEPOps()
+        self._marks = None  # (phase, CUDA event) pairs while profile_phases runs
+
+    def _mark(self, name: str) -> None:
+        if self._marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks.append((name, ev))
 
     # ---------------------------------------------------------------- phases
     def _a2a(self, out, inp, out_splits, in_splits):
@@ -187,6 +194,7 @@ class ExpertParallelMoE:
         Returns (x_recv, local_ids_recv, w_recv, Dispatched)."""
         ops = self.ops
         T, H = x.shape
+        self._mark("start")
         ids, wts = ops.route(gate_logits, self.topk)
         dest = ops.dest_of(ids, self.experts_per_rank)
         xs = None
@@ -195,10 +203,12 @@ class ExpertParallelMoE:
         perm = ops.permute_by_dest(dest, self.world, x)
         local_ids, row_w = ops.pack_meta(perm, ids, wts, self.experts_per_rank)
         counts = perm["expert_counts"].to(torch.int64)
+        self._mark("route_permute")
         recv = torch.empty_like(counts)
         self._a2a(recv, counts, None, None)
         send_counts = counts.cpu().tolist()
         recv_counts = recv.cpu().tolist()
+        self._mark("count_exchange")
         R = int(sum(recv_counts))
         n = T * self.topk
         x_send = perm["x_perm"][:n]
@@ -216,13 +226,43 @@ class ExpertParallelMoE:
         w_recv = torch.empty(R, dtype=torch.float32, device=ids.device)
         self._a2a(w_recv, row_w[:n], recv_counts, send_counts)
         slot_row = ops.slot_rows(perm)
+        self._mark("dispatch")
         return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, send_counts, recv_counts, slot_row)
 
     def combine(self, y_local, d: Dispatched):
         n = d.T * d.topk
+        self._mark("experts")
         y_back = torch.empty((n, y_local.shape[1]), dtype=y_local.dtype, device=y_local.device)
         self._a2a(y_back, y_local, d.send_counts, d.recv_counts)
-        return self.ops.combine_rows(y_back, d.slot_row, d.T, d.topk)
+        self._mark("combine_exchange")
+        out = self.ops.combine_rows(y_back, d.slot_row, d.T, d.topk)
+        self._mark("final_combine")
+        return out
+
+    def profile_phases(self, x, gate_logits) -> dict:
+        """One unchunked forward on the current stream with CUDA events at the
+        phase boundaries. Returns the output, each phase's device time (ms) and
+        the bytes this rank sent to other ranks in the two row exchanges. The
+        phases: route_permute (routing, FP8 quantisation of the rows, sort by
+        destination, metadata), count_exchange (the per-rank counts and their
+        host read), dispatch (rows, scales, expert ids and weights), experts
+        (the local grouped GEMMs), combine_exchange (weighted rows back),
+        final_combine (each token's k rows summed)."""
+        self._marks = []
+        try:
+            x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)
+            out = self.combine(self._experts(x_recv, ids_recv, w_recv), d)
+            torch.cuda.synchronize()
+            marks = self._marks
+        finally:
+            self._marks = None
+        ms = {name: marks[i - 1][1].elapsed_time(ev) for i, (name, ev) in enumerate(marks) if i > 0}
+        H = x.shape[1]
+        remote_send = sum(c for r, c in enumerate(d.send_counts) if r != self.rank)
+        remote_back = sum(c for r, c in enumerate(d.recv_counts) if r != self.rank)
+        row_bytes = (H + (H // 128) * 4 if self.fp8 else 2 * H) + 8  # row (+ scales) + expert id + weight
+        return {"out": out, "ms": ms, "dispatch_bytes": remote_send * row_bytes, "combine_bytes": remote_back * 2 * H,
+                "rows_sent": int(sum(d.send_counts)), "rows_received": int(sum(d.recv_counts))}
 
     def _experts(self, x_recv, ids_recv, w_recv):
         if self.fp8:

@@ -53,15 +53,19 @@ def _round_up(x: int, alignment: int) -> int:
     return ((x + alignment - 1) // alignment) * alignment
 
 
-def _create(dev, counts: List[int], disjoint: bool) -> List[Tuple[torch.cuda.Stream, int]]:
+def _create(dev, counts: List[int], disjoint: bool, remainder: bool = False) -> List[Tuple[torch.cuda.Stream, int]]:
     n = len(counts)
+    m = n + (1 if remainder else 0)
     arr = (ctypes.c_int * n)(*counts)
-    streams = (ctypes.c_void_p * n)()
-    actual = (ctypes.c_int * n)()
+    streams = (ctypes.c_void_p * m)()
+    actual = (ctypes.c_int * m)()
     idx = _dev_index(dev)
-    check(lib().ek_gctx_create(idx, arr, n, 1 if disjoint else 0, streams, actual), "ek_gctx_create")
+    if remainder:
+        check(lib().ek_gctx_create_remainder(idx, arr, n, streams, actual), "ek_gctx_create_remainder")
+    else:
+        check(lib().ek_gctx_create(idx, arr, n, 1 if disjoint else 0, streams, actual), "ek_gctx_create")
     device = torch.device("cuda", idx)
-    return [(torch.cuda.ExternalStream(int(streams[i]), device=device), int(actual[i])) for i in range(n)]
+    return [(torch.cuda.ExternalStream(int(streams[i]), device=device), int(actual[i])) for i in range(m)]
 
 
 def create_sm_partition(dev: torch.device, sm_count: int) -> Tuple[torch.cuda.Stream, int]:
@@ -80,21 +84,27 @@ def create_sm_partition(dev: torch.device, sm_count: int) -> Tuple[torch.cuda.St
     return _create(dev, [rounded], disjoint=False)[0]
 
 
-def create_disjoint_partitions(dev: torch.device, sm_counts: List[int]) -> List[Tuple[torch.cuda.Stream, int]]:
+def create_disjoint_partitions(dev: torch.device, sm_counts: List[int],
+                               with_remainder: bool = False) -> List[Tuple[torch.cuda.Stream, int]]:
     """Partitions with guaranteed disjoint SM sets, chain-split from the
     remainder of each previous split (green_ctx.py:169-235). Each count is
     rounded up to the alignment; ValueError if the rounded total exceeds the
-    device."""
+    device.
+
+    with_remainder=True appends one more partition holding every SM the
+    requests left over (the remainder the reference splits further but never
+    returns, green_ctx.py:110-132): [32] on a 148-SM B200 gives a 32-SM and a
+    116-SM partition, where a [32, 116] request fails (116 rounds up to 120)."""
     if not sm_counts:
         return []
     min_sm, alignment = get_sm_alignment(dev)
     total = get_total_sm_count(dev)
     rounded = [_round_up(max(sc, min_sm), alignment) for sc in sm_counts]
-    if sum(rounded) > total:
+    if sum(rounded) > total or (with_remainder and sum(rounded) >= total):
         raise ValueError(
             f"Total requested SMs {sum(rounded)} (after rounding {list(sm_counts)} -> {rounded}) "
-            f"exceeds device total of {total} SMs")
-    return _create(dev, rounded, disjoint=True)
+            f"exceeds device total of {total} SMs" + (" with SMs left for the remainder" if with_remainder else ""))
+    return _create(dev, rounded, disjoint=True, remainder=with_remainder)
 
 
 def full_device_partition(dev: torch.device) -> Tuple[torch.cuda.Stream, int]:

@@ -77,6 +77,15 @@ int ek_device_sm_info(int dev, int* total_sms, int* min_sms, int* alignment, int
  * green contexts are owned by the library until ek_gctx_destroy_all(). */
 int ek_gctx_create(int dev, const int* counts, int n, int disjoint, void** streams_out, int* actual_out);
 
+/* As ek_gctx_create with disjoint = 1, plus one more partition made of the
+ * SMs the n requests left over: streams_out[n] / actual_out[n] (n + 1 entries
+ * each). The reference turns that remainder into a resource for its next
+ * split (green_ctx.py:110-132) but never hands it out; this exposes it, e.g.
+ * a 32-SM communication partition and the 116 SMs beside it, which a
+ * 116-SM request could not give (it rounds up to 120). EK_ERR_OVERSUB when
+ * the requests leave no SMs over. */
+int ek_gctx_create_remainder(int dev, const int* counts, int n, void** streams_out, int* actual_out);
+
 /* SM count registered for `stream` (0 if the stream is not a partition). */
 int ek_gctx_stream_sm_count(void* stream, int* sm_count_out);
 

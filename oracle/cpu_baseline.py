@@ -47,3 +47,21 @@ def time_gemm(M: int, N: int, K: int, reps: int, budget_s: float = 20.0, seed: i
         if time.perf_counter() - t_start > budget_s:
             break
     return {"seconds": times, "flop": 2.0 * M * N * K}
+
+
+def time_moe(x, logits, w1, w2, w3, topk: int, loop: bool, reps: int = 2, budget_s: float = 10.0) -> dict:
+    """Time the fused-MoE operator on CPU tensors: the definition's per-token
+    loop (loop=True, definition.py:152-168) or the vectorised per-expert
+    restatement (loop=False), `reps` times or until budget_s has passed."""
+    from .moe import moe_loop_ref
+
+    fn = moe_loop_ref if loop else fused_moe_cpu
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn(x, logits, w1, w2, w3, topk)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return {"seconds": times, "tokens": int(x.shape[0])}

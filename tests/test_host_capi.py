@@ -70,6 +70,42 @@ def test_disjoint_chain_split(fake):
         assert v.value == a
 
 
+def test_remainder_partition(fake):
+    """32 SMs split off, the 116 left over as one more partition (the spec's
+    communication / expert-GEMM pairing; a 116-SM request rounds up to 120)."""
+    streams = (ctypes.c_void_p * 2)()
+    actual = (ctypes.c_int * 2)()
+    check(fake.ek_gctx_create_remainder(0, (ctypes.c_int * 1)(32), 1, streams, actual))
+    assert list(actual) == [32, 116] and streams[0] and streams[1] and streams[0] != streams[1]
+    v = ctypes.c_int()
+    check(fake.ek_gctx_stream_sm_count(ctypes.c_void_p(streams[1]), ctypes.byref(v)))
+    assert v.value == 116
+    rc = fake.ek_gctx_create_remainder(0, (ctypes.c_int * 2)(80, 72), 2, (ctypes.c_void_p * 3)(), (ctypes.c_int * 3)())
+    assert rc == _lib.EK_ERR_OVERSUB
+
+
+def test_remainder_partition_python(fake, monkeypatch):
+    from elastikernel_b200 import green_ctx
+
+    class _Ext:
+        def __init__(self, ptr, device=None):
+            self.cuda_stream, self.device = ptr, device
+
+    monkeypatch.setattr(green_ctx.torch.cuda, "ExternalStream", _Ext)
+    parts = green_ctx.create_disjoint_partitions(torch_device(), [32], with_remainder=True)
+    assert [n for _, n in parts] == [32, 116]
+    with pytest.raises(ValueError, match="remainder"):
+        green_ctx.create_disjoint_partitions(torch_device(), [80, 68], with_remainder=True)
+    with pytest.raises(ValueError):
+        green_ctx.create_disjoint_partitions(torch_device(), [32, 116])  # 116 -> 120: over the device
+
+
+def torch_device():
+    import torch
+
+    return torch.device("cuda", 0)
+
+
 def test_split_granularity_reports_actual(fake):
     # the driver rounds 20 up to its granularity; the shim reports the real count
     rc, _, actual = _create(fake, [20], False)
@@ -249,6 +285,9 @@ def test_ragged_gemm_workspace_sizes():
     # [N, K] weights with a ragged K: A and B padded along K, C needs no copy
     got = L.ek_gemm_workspace_bytes(64, 128, 100, 148, bf, nk, 0, 0)
     assert got == 8192 + r256(64 * 112 * 2) + r256(128 * 112 * 2)
+    # ragged N and K with [N, K] weights: B padded along K only (its N rows kept), C through [M, Np]
+    got = L.ek_gemm_workspace_bytes(64, 100, 100, 148, bf, nk, 0, 0)
+    assert got == 8192 + r256(64 * 112 * 2) + r256(100 * 112 * 2) + r256(64 * 104 * 2)
     # aligned: the split scratch of the plan only
     for M, N, K, S in ((4096, 4096, 4096, 148), (512, 1024, 1024, 148)):
         assert L.ek_gemm_workspace_bytes(M, N, K, S, bf, kn, 0, 0) == _ops.plan(M, N, K, S)["workspace_bytes"]
