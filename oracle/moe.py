@@ -107,17 +107,23 @@ def moe_ref(x, logits, w1, w2, w3, topk: int, ids=None, weights=None) -> np.ndar
     return out
 
 
-def moe_ref_by_expert(x, ids, weights, num_experts: int, expert_weights) -> np.ndarray:
+def moe_ref_by_expert(x, ids, weights, num_experts: int, expert_weights, act_quant=None):
     """fp32 MoE output [T, H] for tokens x [T, H] with their routing (ids,
     weights [T, k]), the definition.py:155-170 math, fetching one expert's
     weights at a time: expert_weights(e) -> (w1_e [I, H], w2_e [H, I],
     w3_e [I, H]) as fp32 arrays. Used on sampled tokens of layers whose weights
     are too large to hold in fp32 all at once (Mixtral, 256-expert FP8 layers);
-    experts no sampled token routes to are never fetched."""
+    experts no sampled token routes to are never fetched.
+
+    With act_quant (a function of the fp32 SwiGLU activations [rows, I]) a
+    second output is computed in the same pass from act_quant(act): the
+    reference for a layer that rounds its activations (e.g. to e4m3) before
+    the down projection. Returns (plain, quantised) then, else plain."""
     X = to_f32(x)
     ids = np.asarray(ids)
     weights = np.asarray(weights, dtype=np.float32)
     out = np.zeros(X.shape, dtype=np.float32)
+    out_q = np.zeros(X.shape, dtype=np.float32) if act_quant is not None else None
     for e in range(num_experts):
         t_idx, j_idx = np.nonzero(ids == e)
         if t_idx.size == 0:
@@ -125,8 +131,11 @@ def moe_ref_by_expert(x, ids, weights, num_experts: int, expert_weights) -> np.n
         w1e, w2e, w3e = expert_weights(e)
         h = X[t_idx]
         act = _silu(h @ w1e.T) * (h @ w3e.T)
-        np.add.at(out, t_idx, weights[t_idx, j_idx][:, None] * (act @ w2e.T))
-    return out
+        wt = weights[t_idx, j_idx][:, None]
+        np.add.at(out, t_idx, wt * (act @ w2e.T))
+        if out_q is not None:
+            np.add.at(out_q, t_idx, wt * (np.asarray(act_quant(act), dtype=np.float32) @ w2e.T))
+    return out if out_q is None else (out, out_q)
 
 
 def combine_ref(y, T: int, topk: int) -> torch.Tensor:
