@@ -21,12 +21,15 @@ EK_DTYPE_BF16 = 0
 EK_DTYPE_FP16 = 1
 EK_DTYPE_E4M3 = 2
 
+EK_QUANT_POW2_SCALES = 1
+
 EK_B_KN = 0
 EK_B_NK = 1
 
 EK_STATUS_WAIT_TIMEOUT = 1
 EK_STATUS_BAD_EXPERT = 2
 EK_STATUS_BAD_INDEX = 4
+EK_STATUS_BAD_SCALE = 8
 
 LIB_PATH = Path(__file__).with_name("_ek.so")
 
@@ -72,6 +75,8 @@ _SIGNATURES = {
                              _c_vp, _c_size, _c_vp]),
     "ek_quant_e4m3": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_quant_e4m3_kmajor": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_quant_e4m3_ex": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_quant_e4m3_kmajor_ex": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_gemm_noalloc": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _c_vp]),
     "ek_gemm_noalloc_max_scratch_bytes": (_c_size, []),
@@ -90,6 +95,8 @@ _SIGNATURES = {
     "ek_moe_combine": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_gate_up_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 7 + [_c_vp]),
     "ek_moe_down_fp8bs": (_c_int, [_c_vp] * 8 + [_c_int] * 9 + [_c_vp]),
+    "ek_moe_gate_up_fp8mx": (_c_int, [_c_vp] * 8 + [_c_int] * 7 + [_c_vp]),
+    "ek_moe_down_fp8mx": (_c_int, [_c_vp] * 8 + [_c_int] * 9 + [_c_vp]),
     "ek_moe_gather_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
     "ek_moe_gather_cols_f32": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
     "ek_moe_slot_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),

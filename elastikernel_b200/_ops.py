@@ -142,12 +142,14 @@ def gemm_fp8(a_q: torch.Tensor, w_q: torch.Tensor, a_scale: torch.Tensor, w_scal
     return out
 
 
-def quant_e4m3(x: torch.Tensor, block: tuple[int, int] = (1, 0)) -> tuple[torch.Tensor, torch.Tensor]:
+def quant_e4m3(x: torch.Tensor, block: tuple[int, int] = (1, 0), pow2: bool = False) -> tuple[torch.Tensor,
+                                                                                              torch.Tensor]:
     """e4m3 codes and fp32 scales (amax / 448 per block) of a bf16/fp32 [rows, cols] tensor.
 
     block = (1, 0): one scale per row; (1, 128): per 1 x 128 group;
     (br, bc): per br x bc block. Scales come back shaped [ceil(rows/br), ceil(cols/bc)]
-    (or [rows] for row-wise)."""
+    (or [rows] for row-wise). pow2=True rounds every scale up to a power of
+    two (the UE8M0 scale factors of the block-scaled GEMMs)."""
     dev = _require_cuda(x)
     if x.dtype not in (torch.bfloat16, torch.float32) or x.dim() != 2:
         raise RuntimeError("quant_e4m3 takes a 2-D bf16 or fp32 tensor")
@@ -162,15 +164,17 @@ def quant_e4m3(x: torch.Tensor, block: tuple[int, int] = (1, 0)) -> tuple[torch.
     else:
         scales = torch.empty((-(-rows // br), -(-cols // bc)), dtype=torch.float32, device=dev)
     with _on_device(dev):
-        check(lib().ek_quant_e4m3(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols, br, bc,
-                                  q.data_ptr(), scales.data_ptr(), current_stream_handle(dev)), "ek_quant_e4m3")
+        check(lib().ek_quant_e4m3_ex(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols, br, bc,
+                                     _lib.EK_QUANT_POW2_SCALES if pow2 else 0, q.data_ptr(), scales.data_ptr(),
+                                     current_stream_handle(dev)), "ek_quant_e4m3_ex")
     return q, scales
 
 
-def quant_e4m3_kmajor(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+def quant_e4m3_kmajor(x: torch.Tensor, pow2: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """e4m3 codes and 1 x 128 group scales of a bf16/fp32 [rows, cols] tensor, the
     scales K-block-major: [ceil(cols/128), rows] (the transpose of quant_e4m3's
-    (1, 128) scales, bit for bit). The FP8 block-scaled MoE GEMMs take this layout."""
+    (1, 128) scales, bit for bit). The FP8 block-scaled MoE GEMMs take this layout.
+    pow2=True: power-of-two scales, as quant_e4m3."""
     dev = _require_cuda(x)
     if x.dtype not in (torch.bfloat16, torch.float32) or x.dim() != 2:
         raise RuntimeError("quant_e4m3_kmajor takes a 2-D bf16 or fp32 tensor")
@@ -181,9 +185,9 @@ def quant_e4m3_kmajor(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     q = torch.empty((rows, cols), dtype=_FP8, device=dev)
     scales = torch.empty((-(-cols // 128), rows), dtype=torch.float32, device=dev)
     with _on_device(dev):
-        check(lib().ek_quant_e4m3_kmajor(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols,
-                                         q.data_ptr(), scales.data_ptr(), current_stream_handle(dev)),
-              "ek_quant_e4m3_kmajor")
+        check(lib().ek_quant_e4m3_kmajor_ex(x.data_ptr(), 0 if x.dtype == torch.bfloat16 else 3, rows, cols,
+                                            _lib.EK_QUANT_POW2_SCALES if pow2 else 0, q.data_ptr(),
+                                            scales.data_ptr(), current_stream_handle(dev)), "ek_quant_e4m3_kmajor_ex")
     return q, scales
 
 
@@ -398,25 +402,41 @@ def moe_down_packed(perm: dict, act: torch.Tensor, w2: torch.Tensor, topk_weight
     return y
 
 
-def quant_moe_weights_fp8(w1: torch.Tensor, w2: torch.Tensor, w3: torch.Tensor) -> dict:
+def quant_moe_weights_fp8(w1: torch.Tensor, w2: torch.Tensor, w3: torch.Tensor, pow2: bool = False) -> dict:
     """e4m3 expert weights with 128 x 128 fp32 block scales (DeepSeek style).
-    w1, w3 [E, I, H] and w2 [E, H, I] (bf16 or fp32); I and H multiples of 128."""
+    w1, w3 [E, I, H] and w2 [E, H, I] (bf16 or fp32); I and H multiples of 128.
+    pow2=True: power-of-two block scales; the layer then quantises its tokens
+    and activations the same way and runs the GEMMs whose tensor cores apply
+    the scales (ek_moe_*_fp8mx)."""
     E, I, H = w1.shape
     if I % 128 or H % 128:
         raise RuntimeError("block-scaled FP8 needs I and H multiples of 128")
-    out = {"E": E, "I": I, "H": H}
+    out = {"E": E, "I": I, "H": H, "pow2": bool(pow2)}
     for name, w, rows, cols in (("w1", w1, I, H), ("w3", w3, I, H), ("w2", w2, H, I)):
-        q, s = quant_e4m3(w.reshape(E * rows, cols).contiguous(), block=(128, 128))
+        q, s = quant_e4m3(w.reshape(E * rows, cols).contiguous(), block=(128, 128), pow2=pow2)
         out[name + "q"] = q.view(E, rows, cols)
         out[name + "s"] = s
     return out
 
 
+def _mx(qw: dict, mx: bool | None) -> bool:
+    """Whether the block-scaled GEMMs apply the scales in the tensor cores
+    (power-of-two scales) or scale each K block's product in the epilogue."""
+    pow2 = bool(qw.get("pow2", False))
+    if mx is None:
+        return pow2
+    if mx and not pow2:
+        raise RuntimeError("the tensor-core-scaled FP8 GEMMs need power-of-two scales (quant_moe_weights_fp8(pow2=True))")
+    return bool(mx)
+
+
 def moe_gate_up_fp8bs(perm: dict, xq: torch.Tensor, xs: torch.Tensor, qw: dict, num_sms: int | None = None,
-                      tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+                      tok_tile: int = 0, pair: int = -1, mx: bool | None = None) -> torch.Tensor:
     """Block-scaled FP8 gate/up (SwiGLU) over the packed layout; bf16 act [rows, I].
     xs: K-block-major token scales [H/128, rows] (quant_e4m3_kmajor).
-    tok_tile 0 and pair -1 let the library choose (CTA pairs for tiles of 128/256)."""
+    tok_tile 0 and pair -1 let the library choose (CTA pairs for tiles of 128/256).
+    mx (default: the weights' scale form) picks ek_moe_gate_up_fp8mx, whose
+    tensor cores apply power-of-two scales, over ek_moe_gate_up_fp8bs."""
     dev = _require_cuda(xq, xs)
     if perm["block_m"] != 1:
         raise RuntimeError("the FP8 block-scaled GEMMs take the packed layout (block_m=1)")
@@ -424,29 +444,30 @@ def moe_gate_up_fp8bs(perm: dict, xq: torch.Tensor, xs: torch.Tensor, qw: dict, 
     if xq.shape != (rows, H) or xs.shape != (H // 128, rows):
         raise RuntimeError("gate_up_fp8bs: activation shape mismatch")
     act = torch.empty((rows, I), dtype=torch.bfloat16, device=dev)
+    fn = lib().ek_moe_gate_up_fp8mx if _mx(qw, mx) else lib().ek_moe_gate_up_fp8bs
     with _on_device(dev):
-        check(lib().ek_moe_gate_up_fp8bs(xq.data_ptr(), xs.data_ptr(), qw["w1q"].data_ptr(), qw["w3q"].data_ptr(),
-                                         qw["w1s"].data_ptr(), qw["w3s"].data_ptr(), perm["expert_counts"].data_ptr(),
-                                         act.data_ptr(), rows, E, H, I, int(tok_tile), int(pair), int(num_sms or 0),
-                                         current_stream_handle(dev)), "ek_moe_gate_up_fp8bs")
+        check(fn(xq.data_ptr(), xs.data_ptr(), qw["w1q"].data_ptr(), qw["w3q"].data_ptr(), qw["w1s"].data_ptr(),
+                 qw["w3s"].data_ptr(), perm["expert_counts"].data_ptr(), act.data_ptr(), rows, E, H, I, int(tok_tile),
+                 int(pair), int(num_sms or 0), current_stream_handle(dev)), fn.__name__)
     return act
 
 
 def moe_down_fp8bs(perm: dict, aq: torch.Tensor, as_: torch.Tensor, qw: dict, topk_weights: torch.Tensor,
-                   num_sms: int | None = None, tok_tile: int = 0, pair: int = -1) -> torch.Tensor:
+                   num_sms: int | None = None, tok_tile: int = 0, pair: int = -1, mx: bool | None = None) -> torch.Tensor:
     """Block-scaled FP8 down projection with the routing weight, scattered to slots (bf16 [T*k, H]).
-    as_: K-block-major act scales [I/128, rows]."""
+    as_: K-block-major act scales [I/128, rows]. mx as for moe_gate_up_fp8bs."""
     dev = _require_cuda(aq, as_, topk_weights)
     rows, E, H, I = perm["max_rows"], qw["E"], qw["H"], qw["I"]
     T, k = perm["T"], perm["topk"]
     if aq.shape != (rows, I) or as_.shape != (I // 128, rows) or topk_weights.numel() != T * k:
         raise RuntimeError("down_fp8bs: shape mismatch")
     y = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    fn = lib().ek_moe_down_fp8mx if _mx(qw, mx) else lib().ek_moe_down_fp8bs
     with _on_device(dev):
-        check(lib().ek_moe_down_fp8bs(aq.data_ptr(), as_.data_ptr(), qw["w2q"].data_ptr(), qw["w2s"].data_ptr(),
-                                      perm["expert_counts"].data_ptr(), perm["sorted_slots"].data_ptr(),
-                                      topk_weights.data_ptr(), y.data_ptr(), rows, E, H, I, T, k, int(tok_tile),
-                                      int(pair), int(num_sms or 0), current_stream_handle(dev)), "ek_moe_down_fp8bs")
+        check(fn(aq.data_ptr(), as_.data_ptr(), qw["w2q"].data_ptr(), qw["w2s"].data_ptr(),
+                 perm["expert_counts"].data_ptr(), perm["sorted_slots"].data_ptr(), topk_weights.data_ptr(),
+                 y.data_ptr(), rows, E, H, I, T, k, int(tok_tile), int(pair), int(num_sms or 0),
+                 current_stream_handle(dev)), fn.__name__)
     return y
 
 
@@ -463,11 +484,12 @@ def fused_moe_fp8(hidden_states: torch.Tensor, gate_logits: torch.Tensor, qw: di
     if T == 0:
         return out if out is not None else torch.empty_like(hidden_states)
     ids, wts = moe_route(gate_logits, topk)
-    xq_tok, xs_tok = quant_e4m3(hidden_states, block=(1, 128))
+    pow2 = bool(qw.get("pow2", False))  # tokens and activations take the weights' scale form
+    xq_tok, xs_tok = quant_e4m3(hidden_states, block=(1, 128), pow2=pow2)
     perm = moe_permute(ids, qw["E"], x=xq_tok, block_m=1)
     xs = moe_gather_cols_f32(perm, xs_tok)
     act = moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=num_sms)
-    aq, as_ = quant_e4m3_kmajor(act)
+    aq, as_ = quant_e4m3_kmajor(act, pow2=pow2)
     y = moe_down_fp8bs(perm, aq, as_, qw, wts, num_sms=num_sms)
     return moe_combine(y, T, topk, out=out)
 

@@ -36,6 +36,15 @@
 //                  tile); weight tiles stream from HBM once per token tile, so
 //                  small token counts stay HBM-efficient, and large ones can
 //                  use the CTA pair.
+//
+// Block-scaled e4m3 (kMx, swapped schedule only): weights with 128 x 128 and
+// tokens with 1 x 128 power-of-two scales. The scales become UE8M0 scale
+// factors that the tensor cores apply themselves (kind::mxf8f6f4.block_scale),
+// so every K block accumulates into the same TMEM accumulator and the
+// epilogue runs once per unit. A scale-factor warp (warp 6) writes each
+// stage's factors into shared memory in the layout tcgen05.cp reads (per
+// 128-row block: byte 16a + 4b + j holds row a + 32b, K chunk j); the MMA
+// thread copies them into TMEM right before the stage's MMAs.
 #pragma once
 #include "ek_ptx.cuh"
 
@@ -57,9 +66,10 @@ constexpr int kMaxExpertsT = 256;  // experts per launch of the swapped schedule
 // split's "part written" flags ints [1024, 2048).
 constexpr int kGemmFlagOffset = 1024;
 
-template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false>
+template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false, bool kMx_ = false>
 struct GemmCfg {
   static constexpr bool kPair = kPair_;
+  static constexpr bool kMx = kMx_;  // block-scaled e4m3 (UE8M0 scale factors applied by the MMA)
   static constexpr int CTAS = kPair ? 2 : 1;
   static constexpr int BM = 128;                 // rows per CTA
   static constexpr int TILE_M = BM * CTAS;       // rows per work unit
@@ -82,17 +92,26 @@ struct GemmCfg {
   // slots / weights, and the gate exchange of the SwiGLU epilogue
   static constexpr int EXTRA_BYTES =
       kSwapped ? (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + 64 * 33 * 4 + 127) / 128 * 128 : 0;
+  // kMx scale factors per stage: A (512 B: 128 rows x 4 K chunks) and B
+  // (512 B per 128 tokens), and their TMEM columns (two buffers after the
+  // two accumulators)
+  static constexpr int SF_NB = (BN + 127) / 128;
+  static constexpr int SF_BYTES = kMx ? 512 * (1 + SF_NB) : 0;
+  static constexpr int SF_COLS = 4 + 4 * SF_NB;
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
-  static constexpr int STAGES_FIT = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES_FIT = SMEM_BUDGET / (STAGE_BYTES + SF_BYTES);
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
-                                 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr uint32_t IDESC = umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EXTRA_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int THREADS = 192;
+  static constexpr int TMEM_NEED = 2 * BN + (kMx ? 2 * SF_COLS : 0);
+  static constexpr int TMEM_COLS = (TMEM_NEED <= 32) ? 32 : (TMEM_NEED <= 64) ? 64 : (TMEM_NEED <= 128) ? 128
+                                 : (TMEM_NEED <= 256) ? 256 : 512;
+  static constexpr uint32_t IDESC = kMx ? umma_idesc_mx(TILE_M, BN)
+                                        : umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);
+  static constexpr int SMEM_BYTES = STAGES * (STAGE_BYTES + SF_BYTES) + EXTRA_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int THREADS = kMx ? 224 : 192;  // + the scale-factor warp
   static constexpr int EPI_WARPS = 4;
   static constexpr int CHUNK = BN < 32 ? BN : 32;  // TMEM columns per epilogue load
-  static_assert(kSwapped ? (BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256)
+  static_assert(kSwapped ? (BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256 ||
+                            (kPair && (BN == 160 || BN == 192)))
                          : (BN % 64 == 0 && BN <= 256),
                 "tile width");
   static_assert(BN_CTA % 8 == 0, "B tiles are whole 8-row swizzle atoms");
@@ -104,6 +123,7 @@ struct GemmCfg {
                 "the CTA-pair mode serves the dense, swapped and 256-row padded schedules");
   static_assert(!kSwapped || (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT), "swapped schedule epilogues");
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
+  static_assert(!kMx || (kF8 && kSwapped && TMEM_NEED <= 512), "block scaling: e4m3 swapped tiles up to 192 tokens");
 };
 
 struct GemmParams {
@@ -136,7 +156,21 @@ struct GemmParams {
   // split-K workspace
   float* ws_partial;
   int* ws_counters;
+  // block-scaled e4m3 (kMx): power-of-two fp32 scales, read as UE8M0 exponents
+  const float* sf_tok;    // token scales [K/128][M] (K-block-major)
+  const float* sf_w;      // weight block scales [weight rows / 128][K/128]
+  const float* sf_w2;     // SwiGLU: the w3 block scales (rows 64..127 of a unit)
+  int sf_ksb;             // K / 128
 };
+
+// UE8M0 exponent of a power-of-two fp32 scale; a scale that is not a normal
+// power of two sets EK_STATUS_BAD_SCALE (the kernel's result is then invalid).
+__device__ __forceinline__ uint32_t ue8m0_of(float s) {
+  const uint32_t b = __float_as_uint(s);
+  const uint32_t e = (b >> 23) & 0xFFu;
+  if ((b & 0x807FFFFFu) != 0u || e == 0u || e == 0xFFu) atomicOr(&g_ek_status, kStatusBadScale);
+  return e;
+}
 
 struct Unit {
   int tm, tn;       // tile coordinates
@@ -365,7 +399,7 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[32])
 }
 
 template <class Cfg>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmX, const GemmParams p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, UK = Cfg::UK, STAGES = Cfg::STAGES;
@@ -374,7 +408,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint8_t* sX = sB + STAGES * Cfg::B_BYTES;  // swapped-schedule tables
+  uint8_t* sSF = sB + STAGES * Cfg::B_BYTES;  // kMx scale-factor slots (one per stage)
+  uint8_t* sX = sSF + STAGES * Cfg::SF_BYTES;  // swapped-schedule tables
   uint64_t* bars = reinterpret_cast<uint64_t*>(sX + Cfg::EXTRA_BYTES);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
@@ -399,7 +434,8 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      // kMx: the producer's expect-tx arrival plus one per scale-factor warp of the pair
+      mbar_init(&full_bar[s], Cfg::kMx ? 1 + G : 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -520,6 +556,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int acc_i = 0;
+      uint32_t sf_seq = 0;  // kMx: K blocks issued (scale-factor TMEM buffer parity)
       bool ok = true;
       for (int u = unit0; u < nunits && ok; u += unit_step) {
         const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
@@ -537,6 +574,25 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+          if constexpr (Cfg::kMx) {
+            // this stage's scale factors into one of two TMEM buffers (the
+            // copies and the MMAs below run in issue order), then the four
+            // K = 32 steps of the 128-wide K block, step j using byte j
+            const uint32_t sf = tmem_base + 2 * BN + (uint32_t)(sf_seq & 1) * Cfg::SF_COLS;
+            ++sf_seq;
+            const uint32_t slot = smem_u32(sSF + stage * Cfg::SF_BYTES);
+#pragma unroll
+            for (int i = 0; i <= Cfg::SF_NB; ++i)
+              tmem_cp_32x128b_x4<Cfg::kPair>(sf + 4 * i, smem_desc_plain(slot + 512 * i, 512, 128));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+              const uint64_t bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
+              const uint32_t idk = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
+              umma_mx<Cfg::kPair>(d_tmem, ad, bd, idk, sf | ((uint32_t)k << 30), (sf + 4) | ((uint32_t)k << 30),
+                                  (kb > w.kb0 || k > 0) ? 1u : 0u);
+            }
+          } else {
 #pragma unroll
           for (int k = 0; k < BK / UK; ++k) {
             const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
@@ -550,6 +606,7 @@ __global__ void __launch_bounds__(192, 1)
               umma_pair<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
             else
               umma<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
+          }
           }
           if constexpr (Cfg::kPair)
             umma_commit_pair(&empty_bar[stage], 0x3);
@@ -577,6 +634,58 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain_bar, 0, &never);  // the leader's drain commit also arrives here
     }
     __syncwarp();
+  } else if (Cfg::kMx && warp == 6) {
+    if constexpr (Cfg::kMx) {
+    // ------------------------------------------------------------ scale factors (kMx)
+    // Per stage: the weight rows' factors (A) and the tile's token factors (B)
+    // in the tcgen05.cp layout; lane a writes the 16 bytes of rows a, a + 32,
+    // a + 64, a + 96 (four K chunks each, all equal: a scale covers 128 of K).
+    const uint32_t full_leader0 = Cfg::kPair ? mapa_shared(smem_u32(&full_bar[0]), 0) : 0u;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int u = unit0; u < nunits && ok; u += unit_step) {
+      const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
+      if (!w.valid) continue;
+      const int wb = w.a_row / 128;  // weight scale block row of this CTA's 128 (or 2 x 64) rows
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        // loads first, then the wait for the slot
+        const uint32_t ea = ue8m0_of(p.sf_w[(size_t)wb * p.sf_ksb + kb]) * 0x01010101u;
+        uint32_t eb = ea;
+        if constexpr (Cfg::kEpi == kEpiSwiGLUT) eb = ue8m0_of(p.sf_w2[(size_t)wb * p.sf_ksb + kb]) * 0x01010101u;
+        uint32_t tf[Cfg::SF_NB][4];
+#pragma unroll
+        for (int i = 0; i < Cfg::SF_NB; ++i) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int t = 128 * i + 32 * b + lane;  // MMA column = token tok0 + t
+            const int r = w.tok0 + t;
+            // columns past the unit's tokens multiply rows nobody stores: any factor (2^0)
+            tf[i][b] = (t < w.n_eff && r < w.row_end) ? ue8m0_of(p.sf_tok[(size_t)kb * p.M + r]) * 0x01010101u
+                                                       : 0x7F7F7F7Fu;
+          }
+        }
+        const bool got = mbar_wait(&empty_bar[stage], phase ^ 1, s_abort);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        uint8_t* slot = sSF + stage * Cfg::SF_BYTES;
+        // SwiGLU units hold [64 w1 rows | 64 w3 rows]: rows a and a + 32 are w1's, a + 64 and a + 96 w3's
+        *reinterpret_cast<uint4*>(slot + 16 * lane) = make_uint4(ea, ea, eb, eb);
+#pragma unroll
+        for (int i = 0; i < Cfg::SF_NB; ++i)
+          *reinterpret_cast<uint4*>(slot + 512 * (1 + i) + 16 * lane) = make_uint4(tf[i][0], tf[i][1], tf[i][2], tf[i][3]);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (Cfg::kPair && !leader)
+            mbar_arrive_cluster_release(full_leader0 + stage * 8);
+          else
+            mbar_arrive(&full_bar[stage]);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    __syncwarp();
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access

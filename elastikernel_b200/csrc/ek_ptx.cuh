@@ -24,6 +24,7 @@ enum StatusBits : int {
   kStatusWaitTimeout = 1,      // an mbarrier wait ran out of time
   kStatusBadExpert = 2,        // a grouped GEMM block named an expert out of range
   kStatusBadIndex = 4,         // a permutation index out of range
+  kStatusBadScale = 8,         // a block-scaled GEMM got a scale that is not a power of two
 };
 
 // A wait that has not completed after this many nanoseconds is treated as a
@@ -262,6 +263,70 @@ __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint
   }
 }
 
+// Block-scaled e4m3 MMA (kind::mxf8f6f4.block_scale, one UE8M0 scale factor
+// per 32 elements of K for every row of A and every column of B, read from
+// TMEM): D[tmem] (+)= (A * sfA) * (B * sfB)^T, K = 32 per instruction.
+// sfa / sfb are TMEM addresses whose top two bits select the byte of each
+// 32-bit TMEM cell (the scale-factor id, repeated in the instruction
+// descriptor). kPair: the CTA-pair form (M = 256), issued by the leader.
+template <bool kPair>
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  if constexpr (kPair) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+  }
+}
+
+// Copy 32 rows x 128 bits from shared memory (described by `sdesc`) into TMEM
+// at `taddr`, replicated into all four 32-lane quarters (.warpx4): row r goes
+// to lanes r, r + 32, r + 64, r + 96, columns taddr .. taddr + 3. Asynchronous
+// and ordered with the tcgen05.mma this thread issues afterwards; tracked by
+// tcgen05.commit. kPair: each CTA of the pair copies its own shared memory
+// into its own TMEM (issued by the leader).
+template <bool kPair>
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  if constexpr (kPair)
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+  else
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Shared-memory matrix descriptor without swizzle (sm_100 version bits):
+// 8-row x 16-byte core matrices of 128 contiguous bytes, `sbo` bytes between
+// consecutive 8-row groups, `lbo` between core matrices along the row.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100; layout type 0 = no swizzle
+  return d;
+}
+
+// Make this thread's ordinary shared-memory writes visible to the async proxy
+// (TMA, tcgen05.cp) before they are signalled to the thread that issues it.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Arrive on a barrier of another CTA of the cluster, releasing this thread's
+// prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -344,6 +409,14 @@ __host__ __device__ constexpr uint32_t umma_idesc(uint32_t ab_fmt, bool b_mn_maj
          | (0u << 15)                           // A K-major
          | ((b_mn_major ? 1u : 0u) << 16)       // B major
          | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Instruction descriptor of the block-scaled e4m3 MMA (kind::mxf8f6f4,
+// UE8M0 scale factors, f32 accumulate): A and B e4m3, K-major, N >> 3 at bit
+// 17, scale format UE8M0 at bit 23, M >> 4 at bit 24. The scale-factor ids
+// (bits 4-5 for B, 29-30 for A) are set per instruction.
+__host__ __device__ constexpr uint32_t umma_idesc_mx(uint32_t m, uint32_t n) {
+  return ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

@@ -7,6 +7,11 @@
 // An all-zero row / block gets scale 1 (its codes are all zero). The division
 // is IEEE fp32 and the conversion round-to-nearest-even with saturation, so
 // the result is bit-exact against a CPU restatement that does the same.
+//
+// Power-of-two scales (EK_QUANT_POW2_SCALES): the scale is amax / 448 rounded
+// up to the next power of two (unchanged if it is one), so x / scale is an
+// exact rescaling and the scale is a UE8M0 exponent that the block-scaled
+// tensor-core MMA applies itself; |x / scale| <= 448 still holds.
 #include <cuda_fp8.h>
 
 #include <algorithm>
@@ -28,6 +33,18 @@ __device__ __forceinline__ uint8_t to_e4m3(float v) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
 }
 
+// amax / 448 (1 for an all-zero block), rounded up to a power of two when pow2
+__device__ __forceinline__ float scale_for(float amax, int pow2) {
+  float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  if (pow2) {
+    uint32_t b = __float_as_uint(s);
+    if (b & 0x007FFFFFu) b = (b & 0x7F800000u) + 0x00800000u;  // next power of two up
+    if (b >= 0x7F800000u) b = 0x7F000000u;                    // stay finite (2^127)
+    s = __uint_as_float(b);
+  }
+  return s;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -36,7 +53,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // one warp per row
 __global__ void quant_rows_kernel(const void* __restrict__ x, int dt, int rows, int cols, uint8_t* __restrict__ q,
-                                  float* __restrict__ scales) {
+                                  float* __restrict__ scales, int pow2) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -44,14 +61,14 @@ __global__ void quant_rows_kernel(const void* __restrict__ x, int dt, int rows, 
   float amax = 0.f;
   for (int c = lane; c < cols; c += 32) amax = fmaxf(amax, fabsf(load_f(x, dt, base + c)));
   amax = warp_max(amax);
-  const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  const float s = scale_for(amax, pow2);
   for (int c = lane; c < cols; c += 32) q[base + c] = to_e4m3(load_f(x, dt, base + c) / s);
   if (lane == 0) scales[row] = s;
 }
 
 // one CTA (128 threads) per block_rows x block_cols block
 __global__ void quant_blocks_kernel(const void* __restrict__ x, int dt, int rows, int cols, int br, int bc,
-                                    uint8_t* __restrict__ q, float* __restrict__ scales) {
+                                    uint8_t* __restrict__ q, float* __restrict__ scales, int pow2) {
   const int nbc = (cols + bc - 1) / bc;
   const int bi = blockIdx.x / nbc, bj = blockIdx.x % nbc;
   const int r0 = bi * br, c0 = bj * bc;
@@ -74,7 +91,7 @@ __global__ void quant_blocks_kernel(const void* __restrict__ x, int dt, int rows
   }
   __syncthreads();
   amax = red[0];
-  const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  const float s = scale_for(amax, pow2);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int r = r0 + i / w, c = c0 + i % w;
     const size_t idx = (size_t)r * cols + c;
@@ -88,7 +105,7 @@ __global__ void quant_blocks_kernel(const void* __restrict__ x, int dt, int rows
 // the row length is a multiple of 4. Scales go to scales[row][group], or
 // K-block-major to scales[group][row] when kmajor is set.
 __global__ void quant_groups_kernel(const void* __restrict__ x, int dt, int rows, int cols, uint8_t* __restrict__ q,
-                                    float* __restrict__ scales, int kmajor) {
+                                    float* __restrict__ scales, int kmajor, int pow2) {
   const int groups = (cols + 127) / 128;
   const long long gid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -113,7 +130,7 @@ __global__ void quant_groups_kernel(const void* __restrict__ x, int dt, int rows
   }
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   amax = warp_max(amax);
-  const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  const float s = scale_for(amax, pow2);
   if ((cols & 3) == 0 && c0 + 3 < cols) {
     const uint32_t packed = (uint32_t)to_e4m3(v[0] / s) | ((uint32_t)to_e4m3(v[1] / s) << 8) |
                             ((uint32_t)to_e4m3(v[2] / s) << 16) | ((uint32_t)to_e4m3(v[3] / s) << 24);
@@ -203,7 +220,7 @@ __device__ __forceinline__ void unpack8(const Raw8<kF32>& r, float (&v)[8]) {
 template <int kU, bool kF32>
 __global__ void __launch_bounds__(256) quant_groups_vec_kernel(const void* __restrict__ x, int rows, int cols,
                                                                uint8_t* __restrict__ q, float* __restrict__ scales,
-                                                               int kmajor) {
+                                                               int kmajor, int pow2) {
   const int groups = (cols + 127) / 128;
   const unsigned parts = (unsigned)(groups + 2 * kU - 1) / (2 * kU);  // items per row
   const unsigned items = (unsigned)rows * parts;                       // < 2^31 (host check)
@@ -248,7 +265,7 @@ __global__ void __launch_bounds__(256) quant_groups_vec_kernel(const void* __res
       for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       if (c0 >= cols) continue;  // past the row (group >= groups)
       const int g = g0 + 2 * u;
-      const float s = amax > 0.f ? amax / kE4M3Max : 1.0f;
+      const float s = scale_for(amax, pow2);
       *reinterpret_cast<uint2*>(q + base + c0) = pack8_e4m3(v, s);
       if (hl == 0) scales[kmajor ? (size_t)g * rows + row : (size_t)row * groups + g] = s;
     }
@@ -256,7 +273,7 @@ __global__ void __launch_bounds__(256) quant_groups_vec_kernel(const void* __res
 }
 
 static int launch_groups_vec(const void* x, int dt, int rows, int cols, uint8_t* q, float* scales, int kmajor,
-                             cudaStream_t s) {
+                             int pow2, cudaStream_t s) {
   const long long groups = (cols + 127) / 128;
   const long long items = (long long)rows * ((groups + 2 * kGroupPairs - 1) / (2 * kGroupPairs));
   if (items >= (1ll << 30)) return set_error(EK_ERR_INVALID, "quant: too many rows (%d)", rows);
@@ -265,9 +282,9 @@ static int launch_groups_vec(const void* x, int dt, int rows, int cols, uint8_t*
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned blocks = (unsigned)std::max<long long>(std::min<long long>((items + 7) / 8, (long long)sms * 8), 1);
   if (dt == 0)
-    quant_groups_vec_kernel<kGroupPairs, false><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor);
+    quant_groups_vec_kernel<kGroupPairs, false><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor, pow2);
   else
-    quant_groups_vec_kernel<kGroupPairs, true><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor);
+    quant_groups_vec_kernel<kGroupPairs, true><<<blocks, 256, 0, s>>>(x, rows, cols, q, scales, kmajor, pow2);
   return EK_OK;
 }
 
@@ -275,7 +292,7 @@ static int launch_groups_vec(const void* x, int dt, int rows, int cols, uint8_t*
 // a CTA of 256 threads per block, each thread eight rows x eight consecutive
 // columns held in registers between the amax and the quantisation (one read).
 __global__ void quant_blocks128_vec_kernel(const void* __restrict__ x, int dt, int rows, int cols,
-                                           uint8_t* __restrict__ q, float* __restrict__ scales) {
+                                           uint8_t* __restrict__ q, float* __restrict__ scales, int pow2) {
   const int nbc = (cols + 127) / 128;
   const int bi = blockIdx.x / nbc, bj = blockIdx.x % nbc;
   const int cl = (threadIdx.x & 15) * 8;  // column within the block
@@ -302,7 +319,7 @@ __global__ void quant_blocks128_vec_kernel(const void* __restrict__ x, int dt, i
   float m = red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
-  const float s = m > 0.f ? m / kE4M3Max : 1.0f;
+  const float s = scale_for(m, pow2);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = bi * 128 + r0 + 16 * i;
@@ -318,58 +335,72 @@ using namespace ek;
 
 extern "C" {
 
-int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, void* q,
-                  float* scales, void* stream) {
+int ek_quant_e4m3_ex(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, int flags,
+                     void* q, float* scales, void* stream) {
   clear_error();
   if (!x || !q || !scales || rows < 0 || cols <= 0 || (x_dtype != 0 && x_dtype != 3))
     return set_error(EK_ERR_INVALID, "quant: bad arguments (x_dtype 0 = bf16, 3 = fp32)");
+  if (flags & ~EK_QUANT_POW2_SCALES) return set_error(EK_ERR_INVALID, "quant: unknown flags %#x", flags);
   if (rows == 0) return EK_OK;
+  const int pow2 = (flags & EK_QUANT_POW2_SCALES) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int br = block_rows, bc = block_cols;
   if (br == 1 && (bc <= 0 || bc >= cols)) {
     const long long threads = (long long)rows * 32;
     quant_rows_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
-                                                                      static_cast<uint8_t*>(q), scales);
+                                                                      static_cast<uint8_t*>(q), scales, pow2);
   } else if (br == 1 && bc == 128) {
     if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
-      const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales, 0, s);
+      const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales, 0, pow2, s);
       if (rc) return rc;
     } else {
       const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
       quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
-                                                                          static_cast<uint8_t*>(q), scales, 0);
+                                                                          static_cast<uint8_t*>(q), scales, 0, pow2);
     }
   } else if (br == 128 && bc == 128 && cols % 8 == 0 && aligned16(x) && aligned16(q)) {
     const long long blocks = (long long)((rows + 127) / 128) * ((cols + 127) / 128);
     if (blocks > 0x7fffffffLL) return set_error(EK_ERR_INVALID, "quant: too many blocks");
     quant_blocks128_vec_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, x_dtype, rows, cols, static_cast<uint8_t*>(q),
-                                                                scales);
+                                                                scales, pow2);
   } else if (br >= 1 && bc >= 1) {
     const long long blocks = (long long)((rows + br - 1) / br) * ((cols + bc - 1) / bc);
     if (blocks > 0x7fffffffLL) return set_error(EK_ERR_INVALID, "quant: too many blocks");
     quant_blocks_kernel<<<(unsigned)blocks, 128, 0, s>>>(x, x_dtype, rows, cols, br, bc, static_cast<uint8_t*>(q),
-                                                         scales);
+                                                         scales, pow2);
   } else {
     return set_error(EK_ERR_INVALID, "quant: bad block shape %d x %d", br, bc);
   }
   return check_cuda(cudaGetLastError(), "quant launch");
 }
 
-int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q, float* scales_t, void* stream) {
+int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, void* q,
+                  float* scales, void* stream) {
+  return ek_quant_e4m3_ex(x, x_dtype, rows, cols, block_rows, block_cols, 0, q, scales, stream);
+}
+
+int ek_quant_e4m3_kmajor_ex(const void* x, int x_dtype, int rows, int cols, int flags, void* q, float* scales_t,
+                            void* stream) {
   clear_error();
   if (!x || !q || !scales_t || rows < 0 || cols <= 0 || (x_dtype != 0 && x_dtype != 3))
     return set_error(EK_ERR_INVALID, "quant_kmajor: bad arguments (x_dtype 0 = bf16, 3 = fp32)");
+  if (flags & ~EK_QUANT_POW2_SCALES) return set_error(EK_ERR_INVALID, "quant_kmajor: unknown flags %#x", flags);
   if (rows == 0) return EK_OK;
+  const int pow2 = (flags & EK_QUANT_POW2_SCALES) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cols % 8 == 0 && aligned16(x) && aligned16(q)) {
-    const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1, s);
+    const int rc = launch_groups_vec(x, x_dtype, rows, cols, static_cast<uint8_t*>(q), scales_t, 1, pow2, s);
     if (rc) return rc;
   } else {
     const long long threads = (long long)rows * ((cols + 127) / 128) * 32;
     quant_groups_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, x_dtype, rows, cols,
-                                                                        static_cast<uint8_t*>(q), scales_t, 1);
+                                                                        static_cast<uint8_t*>(q), scales_t, 1, pow2);
   }
   return check_cuda(cudaGetLastError(), "quant_kmajor launch");
+}
+
+int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q, float* scales_t, void* stream) {
+  return ek_quant_e4m3_kmajor_ex(x, x_dtype, rows, cols, 0, q, scales_t, stream);
 }
 
 }  // extern "C"

@@ -105,10 +105,10 @@ class CudaEPOps:
         return _ops.moe_down(perm, act, w2, w_recv, num_sms=self.num_sms)
 
     # ---------------------------------------------------------------- FP8 dispatch
-    def quant_rows(self, x):
+    def quant_rows(self, x, pow2: bool = False):
         from . import _ops
 
-        return _ops.quant_e4m3(x, block=(1, 128))
+        return _ops.quant_e4m3(x, block=(1, 128), pow2=pow2)
 
     def gather_rows(self, perm, src):
         """Rows of `src` in the permutation's order (e.g. the scales of gathered FP8 rows)."""
@@ -135,7 +135,7 @@ class CudaEPOps:
         perm = _ops.moe_permute(local_ids.view(R, 1), qw["E"], x=xq_recv, block_m=1)
         xs = _ops.moe_gather_cols_f32(perm, xs_recv)  # K-block-major scales of the gathered rows
         act = _ops.moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=self.num_sms)
-        aq, as_ = _ops.quant_e4m3_kmajor(act)
+        aq, as_ = _ops.quant_e4m3_kmajor(act, pow2=bool(qw.get("pow2", False)))
         return _ops.moe_down_fp8bs(perm, aq, as_, qw, w_recv, num_sms=self.num_sms)
 
     def combine_rows(self, y_back, slot_row, T, topk):
@@ -199,7 +199,9 @@ class ExpertParallelMoE:
         dest = ops.dest_of(ids, self.experts_per_rank)
         xs = None
         if self.fp8:
-            x, xs = ops.quant_rows(x)  # e4m3 rows + 1 x 128 scales travel instead of bf16
+            # e4m3 rows + 1 x 128 scales travel instead of bf16 (power-of-two
+            # scales when the experts' GEMMs apply them in the tensor cores)
+            x, xs = (ops.quant_rows(x, pow2=True) if self.qw.get("pow2") else ops.quant_rows(x))
         perm = ops.permute_by_dest(dest, self.world, x)
         local_ids, row_w = ops.pack_meta(perm, ids, wts, self.experts_per_rank)
         counts = perm["expert_counts"].to(torch.int64)

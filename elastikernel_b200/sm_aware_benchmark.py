@@ -197,12 +197,15 @@ def run_layer(tokens: int, reps: int = 5, num_sms: int | None = None, layout: st
     torch.cuda.synchronize()
 
 
-def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256) -> None:
+def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256, pow2: bool = False, timed: bool = False) -> None:
     """Run the DeepSeek-V3-shaped e4m3 block-scaled MoE layer (top-8, H=7168,
-    I=2048) with all `experts` on this GPU a few times (for profilers)."""
+    I=2048) with all `experts` on this GPU a few times (for profilers).
+    pow2: power-of-two scales and the GEMMs whose tensor cores apply them.
+    timed: also print the layer's device time (CUDA events, L2 flushed)."""
     import torch
 
     from . import _ops
+    from .timing import time_on_stream
 
     dev = torch.device("cuda:0")
     E, k, H, I = experts, 8, 7168, 2048
@@ -213,9 +216,9 @@ def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256) -> None:
         w1 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         w3 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         w2 = (torch.randn((n, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        qs.append(_ops.quant_moe_weights_fp8(w1, w2, w3))
+        qs.append(_ops.quant_moe_weights_fp8(w1, w2, w3, pow2=pow2))
         del w1, w2, w3
-    qw = {"E": E, "I": I, "H": H}
+    qw = {"E": E, "I": I, "H": H, "pow2": pow2}
     for key in ("w1q", "w1s", "w3q", "w3s", "w2q", "w2s"):
         qw[key] = torch.cat([q[key] for q in qs], dim=0)
     del qs
@@ -224,6 +227,12 @@ def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256) -> None:
     for _ in range(reps):
         _ops.fused_moe_fp8(x, logits, qw, k)
     torch.cuda.synchronize()
+    if timed:
+        r = time_on_stream(lambda: _ops.fused_moe_fp8(x, logits, qw, k), reps=max(reps, 5))
+        flop = tokens * k * 6.0 * H * I
+        print(f"DSv3 FP8 layer T={tokens} E={E} scales={'pow2/tensor-core' if pow2 else 'fp32/epilogue'}: "
+              f"{r['mean_ms'] * 1e3:.1f} us mean, {r['median_ms'] * 1e3:.1f} us median, "
+              f"{flop / (r['mean_ms'] * 1e-3) / 1e12:.0f} TFLOP/s")
 
 
 HBM_SPEC_GBS = 8000.0  # B200 HBM3e spec-sheet bandwidth
@@ -313,6 +322,9 @@ def main():
     parser.add_argument("--layout", choices=["packed", "padded"], default="packed")
     parser.add_argument("--fp8-layer-tokens", type=int, default=0,
                         help="only run the DeepSeek-V3-shaped e4m3 MoE layer at this token count (for profiling)")
+    parser.add_argument("--pow2", action="store_true",
+                        help="--fp8-layer-tokens: power-of-two scales applied by the tensor cores")
+    parser.add_argument("--timed", action="store_true", help="--fp8-layer-tokens: print the layer's device time")
     parser.add_argument("--experts", type=int, default=256,
                         help="experts on this GPU for --fp8-layer-tokens / --stages-tokens")
     parser.add_argument("--stages-tokens", type=int, default=0,
@@ -330,7 +342,7 @@ def main():
     elif args.gemm_shape:
         run_gemm_shape(*args.gemm_shape, dtype=args.dtype, sm_count=args.sms, reps=args.reps)
     elif args.fp8_layer_tokens > 0:
-        run_layer_fp8(args.fp8_layer_tokens, args.reps, args.experts)
+        run_layer_fp8(args.fp8_layer_tokens, args.reps, args.experts, pow2=args.pow2, timed=args.timed)
     elif args.layer_tokens > 0:
         run_layer(args.layer_tokens, args.reps, layout=args.layout)
     elif args.all:

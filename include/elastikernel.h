@@ -55,6 +55,7 @@ int ek_device_status(int dev, int clear, int* status_out);
 #define EK_STATUS_WAIT_TIMEOUT 1
 #define EK_STATUS_BAD_EXPERT 2
 #define EK_STATUS_BAD_INDEX 4
+#define EK_STATUS_BAD_SCALE 8  /* a block-scaled (_fp8mx) GEMM got a scale that is not a power of two */
 
 /* --------------------------------------------------- green-context partitions
  * Replaces green_ctx.py (get_sm_alignment :46, get_total_sm_count :65,
@@ -173,6 +174,17 @@ int ek_quant_e4m3_kmajor(const void* x, int x_dtype, int rows, int cols, void* q
 int ek_quant_e4m3(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, void* q,
                   float* scales, void* stream);
 
+/* ek_quant_e4m3 / ek_quant_e4m3_kmajor with flags. EK_QUANT_POW2_SCALES
+ * rounds every scale up to the next power of two (amax / 448 unchanged if it
+ * is one), so x / scale is an exact rescaling and each scale is a UE8M0
+ * exponent: the form the block-scaled _fp8mx GEMMs take. No counterpart in
+ * the reference (it has no FP8 path). */
+#define EK_QUANT_POW2_SCALES 1
+int ek_quant_e4m3_ex(const void* x, int x_dtype, int rows, int cols, int block_rows, int block_cols, int flags,
+                     void* q, float* scales, void* stream);
+int ek_quant_e4m3_kmajor_ex(const void* x, int x_dtype, int rows, int cols, int flags, void* q, float* scales_t,
+                            void* stream);
+
 /* GEMM for callers that cannot allocate device memory. No counterpart in the
  * reference. Same arguments and result as ek_gemm, minus the workspace: the
  * scratch for split K-slices comes from a fixed 32 MiB device array inside
@@ -285,6 +297,23 @@ int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, 
                          const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
                          int E, int H, int I, int tok, int pair, int num_sms, void* stream);
 int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
+                      const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
+                      int E, int H, int I, int T, int topk, int tok, int pair, int num_sms, void* stream);
+
+/* The same two grouped GEMMs with the scales applied by the tensor cores
+ * (tcgen05.mma kind::mxf8f6f4.block_scale): every scale must be a power of
+ * two (ek_quant_e4m3_ex with EK_QUANT_POW2_SCALES), and is used as a UE8M0
+ * scale factor of each 32-element K chunk. The whole K reduction then
+ * accumulates in TMEM, with one epilogue per tile instead of one scaled
+ * accumulation per 128-wide K block. Same arguments and outputs as the
+ * _fp8bs entry points; token tiles 16/32/64/128 on one CTA, 128/160/192 on a
+ * CTA pair (tok 0 = choose). A scale that is not a normal power of two sets
+ * EK_STATUS_BAD_SCALE in the device status word. No counterpart in the
+ * reference (it has no FP8 path). */
+int ek_moe_gate_up_fp8mx(const void* xq, const float* x_scale, const void* w1q, const void* w3q,
+                         const float* w1_scale, const float* w3_scale, const int* expert_counts, void* act, int rows,
+                         int E, int H, int I, int tok, int pair, int num_sms, void* stream);
+int ek_moe_down_fp8mx(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
                       const int* expert_counts, const int* sorted_slots, const float* topk_weights, void* y, int rows,
                       int E, int H, int I, int T, int topk, int tok, int pair, int num_sms, void* stream);
 

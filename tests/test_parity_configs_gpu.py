@@ -239,9 +239,12 @@ def test_mixtral_layer_bench_shapes(cuda_dev, mixtral, T):
         assert err <= TOL, f"Mixtral T={T} layout={layout} on {sms} SMs: max rel err {err:.3e}"
 
 
-def test_dsv3_fp8_layer_e256_t4096(cuda_dev):
+@pytest.mark.parametrize("pow2", [False, True])
+def test_dsv3_fp8_layer_e256_t4096(cuda_dev, pow2):
     """The DeepSeek-V3-shaped FP8 layer at the bench's 1-GPU load: 256 experts,
-    4096 tokens, top-8 (CTA-pair token tiles of 160 at ~128 rows per expert)."""
+    4096 tokens, top-8 (CTA-pair token tiles at ~128 rows per expert), with
+    fp32 scales applied in the epilogue and with power-of-two scales applied
+    by the tensor cores."""
     from elastikernel_b200 import _ops
 
     E, k, H, I, T = 256, 8, 7168, 2048, 4096
@@ -251,11 +254,11 @@ def test_dsv3_fp8_layer_e256_t4096(cuda_dev):
         w1 = (torch.randn((32, I, H), device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
         w3 = (torch.randn((32, I, H), device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
         w2 = (torch.randn((32, H, I), device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
-        q = _ops.quant_moe_weights_fp8(w1, w2, w3)
+        q = _ops.quant_moe_weights_fp8(w1, w2, w3, pow2=pow2)
         for key in parts:
             parts[key].append(q[key])
         del w1, w2, w3, q
-    qw = {"E": E, "I": I, "H": H}
+    qw = {"E": E, "I": I, "H": H, "pow2": pow2}
     for key, lst in parts.items():
         qw[key] = torch.cat(lst, dim=0)
     del parts
@@ -270,7 +273,7 @@ def test_dsv3_fp8_layer_e256_t4096(cuda_dev):
 
     s = _sample(T, 48, seed=5)
     xs = x[s.tolist()].cpu()
-    xd = of8.dequant_blocks(*of8.quant_blocks(xs, 1, 128), 1, 128)  # the tokens as the kernels see them
+    xd = of8.dequant_blocks(*of8.quant_blocks(xs, 1, 128, pow2=pow2), 1, 128)  # the tokens as the kernels see them
     nI, nH = I // 128, H // 128
 
     def fetch(e):
@@ -280,11 +283,11 @@ def test_dsv3_fp8_layer_e256_t4096(cuda_dev):
         return w1e, w2e, w3e
 
     def act_q(a):  # the layer rounds its bf16 activations to e4m3 (1 x 128 groups) before the down GEMM
-        return of8.dequant_blocks(*of8.quant_blocks(torch.from_numpy(a).to(torch.bfloat16), 1, 128), 1, 128)
+        return of8.dequant_blocks(*of8.quant_blocks(torch.from_numpy(a).to(torch.bfloat16), 1, 128, pow2=pow2), 1, 128)
 
     ref, ref_q = om.moe_ref_by_expert(xd, ids_ref[s], wts_ref[s], E, fetch, act_quant=act_q)
     err = og.max_rel_err(out[s.tolist()], ref)
-    assert err <= TOL_FP8, f"DSv3 FP8 layer T=4096 E=256: max rel err {err:.3e}"
+    assert err <= TOL_FP8, f"DSv3 FP8 layer T=4096 E=256 pow2={pow2}: max rel err {err:.3e}"
     # against the reference that rounds the activations as the layer does, the
     # remaining difference is fp32 summation order and bf16 output rounding
     err_q = og.max_rel_err(out[s.tolist()], ref_q)
