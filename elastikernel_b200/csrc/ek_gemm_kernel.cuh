@@ -98,6 +98,8 @@ struct GemmCfg {
   static constexpr int SF_NB = (BN + 127) / 128;
   static constexpr int SF_BYTES = kMx ? 512 * (1 + SF_NB) : 0;
   static constexpr int SF_COLS = 4 + 4 * SF_NB;
+  static constexpr int SF_AHEAD = 6;  // K blocks of scale loads in flight ahead of the slot writes
+  static constexpr int SF_RELAY = 3;  // stages per cluster-scope release of the pair's relay warp
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / (STAGE_BYTES + SF_BYTES);
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
@@ -106,8 +108,10 @@ struct GemmCfg {
                                  : (TMEM_NEED <= 256) ? 256 : 512;
   static constexpr uint32_t IDESC = kMx ? umma_idesc_mx(TILE_M, BN)
                                         : umma_idesc(kElem == kBF16 ? 1u : 0u, kBMN, TILE_M, BN);
-  static constexpr int SMEM_BYTES = STAGES * (STAGE_BYTES + SF_BYTES) + EXTRA_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int THREADS = kMx ? 224 : 192;  // + the scale-factor warp
+  static constexpr int BAR_BYTES = kMx ? 512 : 256;  // barriers (+ the kMx relay barriers) and TMEM base
+  static constexpr int SMEM_BYTES = STAGES * (STAGE_BYTES + SF_BYTES) + EXTRA_BYTES + 1024 /*align*/ + BAR_BYTES;
+  // + the scale-factor warp; a CTA pair also has a relay warp (see the kernel)
+  static constexpr int THREADS = kMx ? (kPair ? 256 : 224) : 192;
   static constexpr int EPI_WARPS = 4;
   static constexpr int CHUNK = BN < 32 ? BN : 32;  // TMEM columns per epilogue load
   static_assert(kSwapped ? (BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256 ||
@@ -124,6 +128,7 @@ struct GemmCfg {
   static_assert(!kSwapped || (kEpi == kEpiSwiGLUT || kEpi == kEpiScatterT), "swapped schedule epilogues");
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(!kMx || (kF8 && kSwapped && TMEM_NEED <= 512), "block scaling: e4m3 swapped tiles up to 192 tokens");
+  static_assert(!kMx || SF_RELAY <= STAGES, "relay batch within the stage ring");
 };
 
 struct GemmParams {
@@ -416,7 +421,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* sf_ready = bars + 2 * STAGES + 5;  // kMx pair: [STAGES] scale factors written (local)
+  uint32_t* s_tmem_base = reinterpret_cast<uint32_t*>(bars + (Cfg::kMx ? 3 * STAGES + 5 : 2 * STAGES + 5));
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem_base + 1);
   volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem_base + 2);
   volatile int* s_ksplit = reinterpret_cast<volatile int*>(s_tmem_base + 3);
@@ -443,6 +449,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       mbar_init(&tempty_bar[b], Cfg::EPI_WARPS * G);  // one arrival per epilogue warp of the pair
     }
     mbar_init(drain_bar, 1);
+    if constexpr (Cfg::kMx)
+      for (int st = 0; st < STAGES; ++st) mbar_init(&sf_ready[st], 1);
     *s_abort = 0;
     *s_last = 0;
     fence_mbar_init();
@@ -640,48 +648,115 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     // Per stage: the weight rows' factors (A) and the tile's token factors (B)
     // in the tcgen05.cp layout; lane a writes the 16 bytes of rows a, a + 32,
     // a + 64, a + 96 (four K chunks each, all equal: a scale covers 128 of K).
+    // The scale loads run SF_AHEAD steps ahead of the slot writes (a register
+    // ring, indexed by the unrolled loop), so their latency overlaps the
+    // waits for free slots.
+    constexpr int D = Cfg::SF_AHEAD;
     const uint32_t full_leader0 = Cfg::kPair ? mapa_shared(smem_u32(&full_bar[0]), 0) : 0u;
+    uint32_t r_ea[D], r_eb[D], r_tf[D][Cfg::SF_NB][4];
+    int lu = unit0, lkb = 0;  // load cursor: the next (unit, K block) to load
+    Unit lw{};
+    if (lu < nunits) lw = decode_unit<Cfg>(p, lu, rows_rt, rank, xt);
+    // raw fp32 bits go into the ring; the UE8M0 conversion (and its check) happens
+    // when the slot is written, so the loads stay in flight until then
+    auto load_step = [&](uint32_t& ea, uint32_t& eb, uint32_t (&tf)[Cfg::SF_NB][4]) {
+      const int wb = lw.a_row / 128;  // weight scale block row of this CTA's 128 (or 2 x 64) rows
+      ea = __float_as_uint(p.sf_w[(size_t)wb * p.sf_ksb + lkb]);
+      eb = ea;
+      if constexpr (Cfg::kEpi == kEpiSwiGLUT) eb = __float_as_uint(p.sf_w2[(size_t)wb * p.sf_ksb + lkb]);
+#pragma unroll
+      for (int i = 0; i < Cfg::SF_NB; ++i) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int t = 128 * i + 32 * b + lane;  // MMA column = token tok0 + t
+          const int r = lw.tok0 + t;
+          // columns past the unit's tokens multiply rows nobody stores: any factor (2^0)
+          tf[i][b] = (t < lw.n_eff && r < lw.row_end) ? __float_as_uint(p.sf_tok[(size_t)lkb * p.M + r])
+                                                      : 0x3F800000u;
+        }
+      }
+      if (++lkb == p.k_blocks) {
+        lkb = 0;
+        lu += unit_step;
+        if (lu < nunits) lw = decode_unit<Cfg>(p, lu, rows_rt, rank, xt);
+      }
+    };
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (lu < nunits) load_step(r_ea[d], r_eb[d], r_tf[d]);
+    const int my_units = unit0 < nunits ? (nunits - 1 - unit0) / unit_step + 1 : 0;
+    const int steps = my_units * p.k_blocks;  // every unit of the swapped schedule is valid, unsplit
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int u = unit0; u < nunits && ok; u += unit_step) {
-      const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
-      if (!w.valid) continue;
-      const int wb = w.a_row / 128;  // weight scale block row of this CTA's 128 (or 2 x 64) rows
-      for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        // loads first, then the wait for the slot
-        const uint32_t ea = ue8m0_of(p.sf_w[(size_t)wb * p.sf_ksb + kb]) * 0x01010101u;
-        uint32_t eb = ea;
-        if constexpr (Cfg::kEpi == kEpiSwiGLUT) eb = ue8m0_of(p.sf_w2[(size_t)wb * p.sf_ksb + kb]) * 0x01010101u;
-        uint32_t tf[Cfg::SF_NB][4];
+    for (int g0 = 0; g0 < steps && ok; g0 += D) {
 #pragma unroll
-        for (int i = 0; i < Cfg::SF_NB; ++i) {
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int t = 128 * i + 32 * b + lane;  // MMA column = token tok0 + t
-            const int r = w.tok0 + t;
-            // columns past the unit's tokens multiply rows nobody stores: any factor (2^0)
-            tf[i][b] = (t < w.n_eff && r < w.row_end) ? ue8m0_of(p.sf_tok[(size_t)kb * p.M + r]) * 0x01010101u
-                                                       : 0x7F7F7F7Fu;
-          }
-        }
+      for (int d = 0; d < D; ++d) {
+        if (g0 + d >= steps) break;
         const bool got = mbar_wait(&empty_bar[stage], phase ^ 1, s_abort);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         uint8_t* slot = sSF + stage * Cfg::SF_BYTES;
         // SwiGLU units hold [64 w1 rows | 64 w3 rows]: rows a and a + 32 are w1's, a + 64 and a + 96 w3's
+        const uint32_t ea = ue8m0_of(__uint_as_float(r_ea[d])) * 0x01010101u;
+        const uint32_t eb = ue8m0_of(__uint_as_float(r_eb[d])) * 0x01010101u;
         *reinterpret_cast<uint4*>(slot + 16 * lane) = make_uint4(ea, ea, eb, eb);
 #pragma unroll
         for (int i = 0; i < Cfg::SF_NB; ++i)
-          *reinterpret_cast<uint4*>(slot + 512 * (1 + i) + 16 * lane) = make_uint4(tf[i][0], tf[i][1], tf[i][2], tf[i][3]);
+          *reinterpret_cast<uint4*>(slot + 512 * (1 + i) + 16 * lane) =
+              make_uint4(ue8m0_of(__uint_as_float(r_tf[d][i][0])) * 0x01010101u,
+                         ue8m0_of(__uint_as_float(r_tf[d][i][1])) * 0x01010101u,
+                         ue8m0_of(__uint_as_float(r_tf[d][i][2])) * 0x01010101u,
+                         ue8m0_of(__uint_as_float(r_tf[d][i][3])) * 0x01010101u);
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
+          // the peer of a pair hands the slot to its relay warp (below); the
+          // leader (or a single CTA) completes its own full barrier
           if (Cfg::kPair && !leader)
-            mbar_arrive_cluster_release(full_leader0 + stage * 8);
+            mbar_arrive(&sf_ready[stage]);
           else
             mbar_arrive(&full_bar[stage]);
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (lu < nunits) load_step(r_ea[d], r_eb[d], r_tf[d]);  // refill: the step D ahead
+      }
+    }
+    __syncwarp();
+    }
+  } else if (Cfg::kMx && Cfg::kPair && warp == 7) {
+    if constexpr (Cfg::kMx && Cfg::kPair) {
+    // ------------------------------------------------------------ relay (kMx pair, peer CTA)
+    // Signals the leader's full barrier once this CTA's scale factors are in
+    // place. A release at cluster scope costs about half a microsecond, so
+    // it is paid once per batch of SF_RELAY stages: wait until the batch's
+    // slots are written, one cluster-scope fence, then the batch's arrivals.
+    // Doing it here rather than in the scale-factor warp also keeps the fence
+    // from waiting for the scale loads that warp keeps in flight. A batch
+    // never exceeds the ring (SF_RELAY <= STAGES), so its slots' previous
+    // rounds were signalled by earlier batches: no wait here can block the
+    // MMA that would free them.
+    if (lane == 0 && !leader) {
+      constexpr int B = Cfg::SF_RELAY;
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full_bar[0]), 0);
+      const int my_units = unit0 < nunits ? (nunits - 1 - unit0) / unit_step + 1 : 0;
+      const int steps = my_units * p.k_blocks;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int g = 0; g < steps && ok; g += B) {
+        const int nb = min(B, steps - g);
+        int st = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < nb; ++i) {
+          if (!mbar_wait(&sf_ready[st], ph, s_abort)) { ok = false; break; }
+          if (++st == STAGES) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        fence_acq_rel_cluster();
+        for (int i = 0; i < nb; ++i) {
+          mbar_arrive_cluster(full_leader0 + stage * 8);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
       }
     }
     __syncwarp();

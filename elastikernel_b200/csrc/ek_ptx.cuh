@@ -321,6 +321,10 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Order this thread's prior memory accesses (and those it has acquired) before
+// its later ones at cluster scope.
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
 // Arrive on a barrier of another CTA of the cluster, releasing this thread's
 // prior writes at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t bar_cluster) {
