@@ -51,6 +51,9 @@ FLOP = 2.0 * M * N * K
 METRIC = "bf16 GEMM TFLOP/s per green-ctx partition (4096^3, 148-SM full device)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+# FP8 expert weights of the DeepSeek-V3-shaped layer: power-of-two scales
+# applied by the tensor cores (True) or fp32 scales applied per K block (False)
+FP8_POW2 = True
 # dense bf16 / fp16 MMA rate of one B200 SM per clock (tcgen05); e4m3 is twice it
 MMA_FLOP_PER_CLK_SM = 8192
 
@@ -382,14 +385,15 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
         w1 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         w3 = (torch.randn((n, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
         w2 = (torch.randn((n, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        q = _ops.quant_moe_weights_fp8(w1, w2, w3)
+        q = _ops.quant_moe_weights_fp8(w1, w2, w3, pow2=FP8_POW2)
         for key in parts:
             parts[key].append(q[key])
         del w1, w2, w3, q
-    qw = {"E": eg, "I": I, "H": H}
+    qw = {"E": eg, "I": I, "H": H, "pow2": FP8_POW2}
     for key, lst in parts.items():
         qw[key] = torch.cat(lst, dim=0)
     del parts
+    qw = _ops.stack_gate_up_planes(qw)  # w1 / w3 codes as two planes of one buffer
     gx = torch.Generator(device=dev).manual_seed(42 + rank)
     x = torch.randn((T, H), device=dev, generator=gx).to(torch.bfloat16)
     logits = torch.randn((T, E), device=dev, generator=gx)
@@ -448,6 +452,8 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
             "chunks": chunks, "phases_ms_unchunked": phases, "all_to_all": a2a,
             "ep_max_rel_err": err, "ep_parity_tol": 3e-2, "ep_max_rel_err_act_e4m3": err_q,
+            "fp8_scales": "power-of-two, applied by the tensor cores (kind::mxf8f6f4.block_scale)" if FP8_POW2
+            else "fp32, applied per 128-wide K block in the epilogue",
             "host_sync": "per-chunk count exchange read on the host (all-to-all split sizes)"}
 
 
@@ -485,7 +491,8 @@ def ep_parity(dev, x, logits, out, qw, E: int, k: int, world: int, rank: int, pe
     eg = E // world
     lo = rank * eg
     ids_local = np.where((ids >= lo) & (ids < lo + eg), ids - lo, -1)
-    xd = of8.dequant_blocks(*of8.quant_blocks(xs_all.cpu(), 1, 128), 1, 128)  # e4m3 rows, as dispatched
+    xd = of8.dequant_blocks(*of8.quant_blocks(xs_all.cpu(), 1, 128, pow2=bool(qw.get("pow2", False))), 1,
+                            128)  # e4m3 rows, as dispatched
     nI, nH = qw["I"] // 128, qw["H"] // 128
 
     def fetch(e):
@@ -494,9 +501,11 @@ def ep_parity(dev, x, logits, out, qw, E: int, k: int, world: int, rank: int, pe
         w2e = of8.dequant_block_rows(qw["w2q"][e].cpu(), qw["w2s"][e * nH:(e + 1) * nH].cpu().numpy())
         return w1e, w2e, w3e
 
+    pow2 = bool(qw.get("pow2", False))
+
     def act_q(a):  # the layer's e4m3 activations: bf16 act, 1 x 128 groups
         ab = torch.from_numpy(a).to(torch.bfloat16)
-        return of8.dequant_blocks(*of8.quant_blocks(ab, 1, 128), 1, 128)
+        return of8.dequant_blocks(*of8.quant_blocks(ab, 1, 128, pow2=pow2), 1, 128)
 
     plain, actq = om.moe_ref_by_expert(xd, ids_local, wts, eg, fetch, act_quant=act_q)
     part = torch.from_numpy(np.stack([plain, actq])).to(dev)
@@ -523,6 +532,11 @@ def moe_bench(dev, steps: int, hbm_gbs: float, peak_bf16_tflops: float, cpu: boo
     w1 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
     w3 = (torch.randn((E, I, H), device=dev, generator=g) * 0.02).to(torch.bfloat16)
     w2 = (torch.randn((E, H, I), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    # w1 and w3 as the two planes of one [2, E, I, H] tensor (a fused gate/up
+    # weight): the gate/up GEMMs then read a tile's [w1 | w3] rows in one TMA box
+    w13 = torch.stack([w1, w3])
+    del w1, w3
+    w1, w3 = w13[0], w13[1]
     res = []
     half_stream, half_sms = create_sm_partition(dev, 72)
     for T in [1, 16, 128, 1024, 4096]:

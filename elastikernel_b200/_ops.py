@@ -416,7 +416,23 @@ def quant_moe_weights_fp8(w1: torch.Tensor, w2: torch.Tensor, w3: torch.Tensor, 
         q, s = quant_e4m3(w.reshape(E * rows, cols).contiguous(), block=(128, 128), pow2=pow2)
         out[name + "q"] = q.view(E, rows, cols)
         out[name + "s"] = s
-    return out
+    return stack_gate_up_planes(out)
+
+
+def stack_gate_up_planes(qw: dict) -> dict:
+    """Store the e4m3 w1 and w3 codes as the two planes of one [2, E, I, H]
+    buffer (w1q / w3q become views of it). The gate/up GEMMs then load a
+    tile's [w1 rows | w3 rows] with one TMA box instead of two, which lets an
+    SM draw about twice the HBM bandwidth (the TMA engine keeps only a few
+    boxes in flight). Any layout stays correct; this one is faster. Call it
+    again after concatenating the codes of several quantised shards."""
+    w1q, w3q = qw["w1q"], qw["w3q"]
+    if w1q.shape != w3q.shape:
+        raise RuntimeError("w1q and w3q must have one shape")
+    planes = torch.stack([w1q, w3q])
+    qw = dict(qw)
+    qw["w1q"], qw["w3q"] = planes[0], planes[1]
+    return qw
 
 
 def _mx(qw: dict, mx: bool | None) -> bool:

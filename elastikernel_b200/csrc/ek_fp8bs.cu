@@ -137,6 +137,17 @@ int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, 
   if ((rc = make_tmap_2d(&ta, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
   if ((rc = make_tmap_2d(&tx, w3q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
   if ((rc = make_tmap_2d(&tb, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, rows, H, 128, t / ctas))) return rc;
+  uint64_t plane = 0;
+  bool planes = false;
+  CUtensorMap t3;
+  if (plane_stride(w1q, w3q, (uint64_t)E * I * H, &plane)) {
+    // w3q lies a fixed distance after w1q (e.g. two planes of one buffer): one
+    // 3-D box loads a unit's [64 w1 | 64 w3] weight rows
+    if (make_tmap_3d(&t3, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, 2, H, plane, 128, 64, 2) == EK_OK)
+      planes = true;
+    else
+      clear_error();
+  }
   Fp8BsParams P{};
   P.g.M = rows;
   P.g.N = I;
@@ -152,6 +163,10 @@ int ek_moe_gate_up_fp8bs(const void* xq, const float* x_scale, const void* w1q, 
   P.w_scale = w1_scale;
   P.w_scale2 = w3_scale;
   P.ksb = H / 128;
+  if (planes) {
+    ta = t3;
+    P.g.a_planes = 1;
+  }
   const int grid = std::max(1, S / ctas) * ctas;
   return launch_tok<kEpiSwiGLUT>(t, pr != 0, ta, tb, tx, P, grid, static_cast<cudaStream_t>(stream));
 }

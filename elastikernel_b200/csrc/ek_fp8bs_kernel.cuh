@@ -241,8 +241,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       if (fu < nunits) fw = decode_unit<Cfg>(p, fu, 0, rank, xt);
       auto prefetch_next = [&]() {
         if (fu >= nunits) return;
-        tma_prefetch_2d(&tmA, fkb * 128, fw.a_row);
-        if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_prefetch_2d(&tmX, fkb * 128, fw.a_row);
+        if (p.a_planes) {
+          tma_prefetch_3d(&tmA, fkb * 128, fw.a_row, 0);
+        } else {
+          tma_prefetch_2d(&tmA, fkb * 128, fw.a_row);
+          if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_prefetch_2d(&tmX, fkb * 128, fw.a_row);
+        }
         if (++fkb == KB) {
           fkb = 0;
           fu += unit_step;
@@ -262,14 +266,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           if constexpr (Cfg::kPair) {
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
             const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-            tma_load_2d_pair(a_dst, &tmA, fb, kb * 128, w.a_row);
-            if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * 128, w.a_row);
+            if (p.a_planes) {
+              tma_load_3d_pair(a_dst, &tmA, fb, kb * 128, w.a_row, 0);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, fb, kb * 128, w.a_row);
+              if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * 128, w.a_row);
+            }
             tma_load_2d_pair(b_dst, &tmB, fb, kb * 128, w.b_row);
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * 128, w.a_row);
-            if constexpr (Cfg::kEpi == kEpiSwiGLUT)
-              tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * 128, w.a_row);
+            if (p.a_planes) {
+              tma_load_3d(a_dst, &tmA, &full_bar[stage], kb * 128, w.a_row, 0);
+            } else {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * 128, w.a_row);
+              if constexpr (Cfg::kEpi == kEpiSwiGLUT)
+                tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * 128, w.a_row);
+            }
             tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * 128, w.b_row);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }

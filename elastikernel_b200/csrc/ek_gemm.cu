@@ -416,6 +416,18 @@ int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C
   if (rc) return rc;
 
   GemmParams prm{};
+  if (b_layout == EK_B_KN && N % 64 == 0) {
+    // one 3-D box per stage for all of the CTA's 64-column chunks of B (chunk
+    // stride 128 bytes along the row); the 2-D boxes above stay as fallback
+    CUtensorMap tb3;
+    if (make_tmap_3d(&tb3, B, tdt, 64, b_rows > 0 ? b_rows : K, N / 64, (uint64_t)N * es, 128, 64, 64,
+                     bn_cta / 64) == EK_OK) {
+      tb = tb3;
+      prm.b_chunks = 1;
+    } else {
+      clear_error();
+    }
+  }
   prm.M = M;
   prm.N = N;
   prm.K = K;

@@ -100,6 +100,7 @@ struct GemmCfg {
   static constexpr int SF_COLS = 4 + 4 * SF_NB;
   static constexpr int SF_AHEAD = 6;  // K blocks of scale loads in flight ahead of the slot writes
   static constexpr int SF_RELAY = 3;  // stages per cluster-scope release of the pair's relay warp
+  static constexpr int MX_PREFETCH = 16;  // kMx: K blocks of weight tiles prefetched into L2 ahead of the loads
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / (STAGE_BYTES + SF_BYTES);
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
@@ -161,6 +162,10 @@ struct GemmParams {
   // split-K workspace
   float* ws_partial;
   int* ws_counters;
+  // one 3-D box in place of two or more 2-D boxes per stage (make_tmap_3d):
+  int a_planes;   // SwiGLUT: tmA is [K, weight rows, 2 planes (w1, w3)]: one box = [w1 rows | w3 rows]
+  int b_planes;   // SwiGLU (one CTA): tmB is [K, weight rows, 2 planes]: one box = [w1 rows | w3 rows]
+  int b_chunks;   // MN-major B: tmB is [64 N, K, N / 64 chunks]: one box = every 64-column chunk of the stage
   // block-scaled e4m3 (kMx): power-of-two fp32 scales, read as UE8M0 exponents
   const float* sf_tok;    // token scales [K/128][M] (K-block-major)
   const float* sf_w;      // weight block scales [weight rows / 128][K/128]
@@ -507,11 +512,38 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // kMx: an L2 prefetch cursor MX_PREFETCH K blocks ahead of the loads.
+      // The weight tiles come from HBM; a prefetch holds no shared memory, so
+      // it deepens the stream past the stage ring, and the ring's loads then
+      // find their tiles in L2.
+      int fu = unit0, fkb = 0;
+      Unit fw{};
+      auto prefetch_next = [&]() {
+        if constexpr (Cfg::kMx) {
+          if (fu >= nunits) return;
+          if (p.a_planes) {
+            tma_prefetch_3d(&tmA, fkb * BK, fw.a_row, 0);
+          } else {
+            tma_prefetch_2d(&tmA, fkb * BK, fw.a_row);
+            if constexpr (Cfg::kEpi == kEpiSwiGLUT) tma_prefetch_2d(&tmX, fkb * BK, fw.a_row);
+          }
+          if (++fkb == p.k_blocks) {
+            fkb = 0;
+            fu += unit_step;
+            if (fu < nunits) fw = decode_unit<Cfg>(p, fu, rows_rt, rank, xt);
+          }
+        }
+      };
+      if constexpr (Cfg::kMx) {
+        if (fu < nunits) fw = decode_unit<Cfg>(p, fu, rows_rt, rank, xt);
+        for (int i = 0; i < Cfg::MX_PREFETCH; ++i) prefetch_next();
+      }
       for (int u = unit0; u < nunits && ok; u += unit_step) {
         const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
         if (!w.valid) continue;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) { ok = false; break; }
+          prefetch_next();
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
           if constexpr (Cfg::kPair) {
@@ -519,15 +551,23 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
             const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
             if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
-              tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
-              tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * BK, w.a_row);
+              if (p.a_planes) {
+                tma_load_3d_pair(a_dst, &tmA, fb, kb * BK, w.a_row, 0);
+              } else {
+                tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
+                tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * BK, w.a_row);
+              }
             } else {
               tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
             }
             if constexpr (Cfg::kBMN) {
+              if (p.b_chunks) {
+                tma_load_3d_pair(b_dst, &tmB, fb, 0, w.b_row + kb * BK, w.b_col / 64);
+              } else {
 #pragma unroll
-              for (int j = 0; j < Cfg::BN_CTA / 64; ++j)
-                tma_load_2d_pair(b_dst + j * (BK * 128), &tmB, fb, w.b_col + 64 * j, w.b_row + kb * BK);
+                for (int j = 0; j < Cfg::BN_CTA / 64; ++j)
+                  tma_load_2d_pair(b_dst + j * (BK * 128), &tmB, fb, w.b_col + 64 * j, w.b_row + kb * BK);
+              }
             } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
               // columns [0, BN/2) of the pair's tile come from rank 0 (w1), [BN/2, BN) from rank 1 (w3)
               tma_load_2d_pair(b_dst, leader ? &tmB : &tmX, fb, kb * BK, w.b_row);
@@ -537,18 +577,30 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], Cfg::TX_BYTES);
             if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
-              tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
-              tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * BK, w.a_row);
+              if (p.a_planes) {
+                tma_load_3d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row, 0);
+              } else {
+                tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
+                tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * BK, w.a_row);
+              }
             } else {
               tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
             }
             if constexpr (Cfg::kBMN) {
+              if (p.b_chunks) {
+                tma_load_3d(b_dst, &tmB, &full_bar[stage], 0, w.b_row + kb * BK, w.b_col / 64);
+              } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_2d(b_dst + j * (BK * 128), &tmB, &full_bar[stage], w.b_col + 64 * j, w.b_row + kb * BK);
+              }
             } else if constexpr (Cfg::kEpi == kEpiSwiGLU) {
-              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
-              tma_load_2d(b_dst + (BN / 2) * 128, &tmX, &full_bar[stage], kb * BK, w.b_row);
+              if (p.b_planes) {
+                tma_load_3d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row, 0);
+              } else {
+                tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
+                tma_load_2d(b_dst + (BN / 2) * 128, &tmX, &full_bar[stage], kb * BK, w.b_row);
+              }
             } else {
               tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * BK, w.b_row);
             }

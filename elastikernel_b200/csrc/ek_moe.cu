@@ -585,6 +585,18 @@ int ek_moe_gate_up(const void* x_perm, const void* w1, const void* w3, const int
   if ((rc = make_tmap_2d(&tb2, w3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, bn / 2)))
     return rc;
   GemmParams p{};
+  uint64_t plane = 0;
+  if (!pair && plane_stride(w1, w3, (uint64_t)E * I * H * 2, &plane)) {
+    // w3 lies a fixed distance after w1: one 3-D box loads the [w1 | w3] halves of a stage
+    CUtensorMap t3;
+    if (make_tmap_3d(&t3, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, 2, (uint64_t)H * 2, plane, 64,
+                     bn / 2, 2) == EK_OK) {
+      tb = t3;
+      p.b_planes = 1;
+    } else {
+      clear_error();
+    }
+  }
   p.M = max_rows;
   p.N = I;
   p.K = H;
@@ -697,6 +709,18 @@ int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, co
   if ((rc = make_tmap_2d(&tb, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, rows, (uint64_t)H * 2, 64, tok / ctas)))
     return rc;
   GemmParams p{};
+  uint64_t plane = 0;
+  if (plane_stride(w1, w3, (uint64_t)E * I * H * 2, &plane)) {
+    // w3 lies a fixed distance after w1: one 3-D box loads a unit's [64 w1 | 64 w3] weight rows
+    CUtensorMap t3;
+    if (make_tmap_3d(&t3, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, 2, (uint64_t)H * 2, plane, 64, 64,
+                     2) == EK_OK) {
+      ta = t3;
+      p.a_planes = 1;
+    } else {
+      clear_error();
+    }
+  }
   p.M = rows;
   p.N = I;
   p.K = H;

@@ -64,6 +64,35 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return EK_OK;
 }
 
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(driver_fn("cuTensorMapEncodeTiled", 12000));
+  });
+  if (!encode) return set_error(EK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver?)");
+  if (!aligned16(base) || (stride1_bytes & 15u) != 0 || (stride2_bytes & 15u) != 0)
+    return set_error(EK_ERR_INVALID, "3-D TMA operand must be 16-byte aligned with strides multiple of 16 bytes");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(EK_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return EK_OK;
+}
+
+bool plane_stride(const void* first, const void* second, uint64_t min_bytes, uint64_t* stride_out) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(first), b = reinterpret_cast<uintptr_t>(second);
+  if (b <= a || ((b - a) & 15u) != 0 || (b - a) < min_bytes || (b - a) >= (1ull << 40)) return false;
+  *stride_out = b - a;
+  return true;
+}
+
 int device_sm_count(int* out) {
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");

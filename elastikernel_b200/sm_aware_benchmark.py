@@ -222,6 +222,7 @@ def run_layer_fp8(tokens: int, reps: int = 3, experts: int = 256, pow2: bool = F
     for key in ("w1q", "w1s", "w3q", "w3s", "w2q", "w2s"):
         qw[key] = torch.cat([q[key] for q in qs], dim=0)
     del qs
+    qw = _ops.stack_gate_up_planes(qw)
     x = torch.randn((tokens, H), device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn((tokens, E), device=dev, generator=g)
     for _ in range(reps):

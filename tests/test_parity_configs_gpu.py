@@ -262,6 +262,7 @@ def test_dsv3_fp8_layer_e256_t4096(cuda_dev, pow2):
     for key, lst in parts.items():
         qw[key] = torch.cat(lst, dim=0)
     del parts
+    qw = _ops.stack_gate_up_planes(qw)
     gx = torch.Generator(device=cuda_dev).manual_seed(42)
     x = torch.randn((T, H), device=cuda_dev, generator=gx).to(torch.bfloat16)
     logits = torch.randn((T, E), device=cuda_dev, generator=gx)
