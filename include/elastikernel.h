@@ -229,7 +229,9 @@ int64_t ek_moe_max_padded_rows(int T, int topk, int E, int block_m);
  *   num_rows_padded[1]             padded rows in use
  *   expert_counts[E]               slots routed to each expert
  * If x != NULL (x is [T, H], element size elem_bytes) the rows are also
- * gathered: x_perm[r] = x[sorted_slots[r] / k], zero rows for padding.
+ * gathered: x_perm[r] = x[sorted_slots[r] / k] for every row holding a slot;
+ * padding rows are left unwritten (the GEMMs' outputs for them are never
+ * stored or read).
  * scratch: ek_moe_permute_scratch_bytes(T, topk, E) bytes of device memory
  * (no initial contents required). */
 size_t ek_moe_permute_scratch_bytes(int T, int topk, int E);

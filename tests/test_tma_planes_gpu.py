@@ -46,7 +46,10 @@ def test_bf16_gate_up_one_box_equals_two(cuda_dev, layout, tok, pair):
             perm = _ops.moe_permute(ids, E, x=x, block_m=128)
             outs.append(_ops.moe_gate_up(perm, a1, a3))
     torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1])
+    # rows that hold a routed slot (the padded layout's padding rows are never
+    # gathered, so their products are whatever the buffer held)
+    valid = perm["sorted_slots"] < T * k
+    assert torch.equal(outs[0][valid], outs[1][valid])
 
 
 @pytest.mark.parametrize("mx", [False, True])
