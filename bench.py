@@ -5,7 +5,9 @@ Headline (`value`): bf16 GEMM M = N = K = 4096 (the N=K=4096 wave-sweep's
 square point) on the full 148-SM device, TFLOP/s, whole job (sum over ranks;
 ranks are independent replicas, "weak" scaling). One step = one GEMM of
 synthetic N(0,1) inputs (seed 0) resident in HBM; the L2 is flushed (256 MB
-write) before every timed step, outside the timed events.
+write) before every timed step, outside the timed events. After the W
+warm-up steps and the clock sampler's start, about 30 ms of untimed steps
+bring the SM clock back up from idle before the K timed steps.
 
 Also on the same line:
 * e2e       the same metric through the public API (sm_aware_matmul.call_sm_aware)
@@ -20,6 +22,9 @@ Also on the same line:
 * moe_cpu   the reference's CPU MoE operator on the box's host cores
 * moe_ep    DeepSeek-V3-shaped FP8 expert-parallel layer: phases, NVLink
             bytes, and its output checked against the oracle on a token sample
+* triton_reference  the reference's own Triton GEMM (4096^3 fp16, autotuned as
+            the reference does) and MoE segment kernel on this GPU beside the
+            tcgen05 kernels (baseline/triton_comparator.py; N=1 only)
 * cpu_baseline  the reference's CPU GEMM (torch.matmul on CPU) on a bounded sample
 * summary   (the line's last key) the figures above in compact form
 
@@ -172,6 +177,27 @@ def barrier(world: int) -> None:
         import torch.distributed as dist
 
         dist.barrier()
+
+
+def settle(step_fn, flush, ms: float = 30.0) -> None:
+    """Untimed steps for about `ms` of GPU time right before a timed region.
+    The clock sampler's start-up leaves the GPU idle for a few tenths of a
+    second, and an idle B200 needs a few milliseconds under load to bring its
+    SM clock back up: without this the first timed steps of a short region
+    run at the lower clock."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    if flush is not None:
+        flush()
+    step_fn()
+    e.record()
+    torch.cuda.synchronize()
+    n = max(1, min(2000, int(ms / max(s.elapsed_time(e), 1e-3))))
+    for _ in range(n):
+        if flush is not None:
+            flush()
+        step_fn()
+    torch.cuda.synchronize()
 
 
 def timed_steps(step_fn, steps: int, flush) -> tuple[float, list]:
@@ -650,6 +676,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the partition sweep, MoE and CPU legs")
+    ap.add_argument("--triton-sms", default="16,32,64,96,132,148",
+                    help="partition sizes (comma list, '' for none) at which the reference's own Triton GEMM is "
+                         "timed beside the tcgen05 one; its MoE segment kernel runs at 64 SMs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local_rank = dist_env()
@@ -687,6 +716,7 @@ def main() -> None:
     # ---------------------------------------------------------------- device-resident timed region
     sampler = ClockSampler(dev)
     with sampler:
+        settle(lambda: smm.call_sm_aware(a, b), lambda: flush_l2(dev))
         barrier(world)
         torch.cuda.synchronize()
         ms, per = timed_steps(lambda: smm.call_sm_aware(a, b), args.steps, lambda: flush_l2(dev))
@@ -722,6 +752,8 @@ def main() -> None:
         extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
         extras["moe"] = moe_bench(dev, args.steps, hbm, peak_tf, cpu=(rank == 0 and world == 1))
         extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
+        if rank == 0 and world == 1 and args.triton_sms.strip():
+            extras["triton_reference"] = triton_reference(dev, [int(x) for x in args.triton_sms.split(",")])
         if rank == 0 and world == 1:
             extras["cpu_baseline"] = cpu_baseline_sample()
     if world > 1:
@@ -739,6 +771,7 @@ def main() -> None:
         "config": {"workload": "bf16 GEMM 4096x4096x4096 on the full 148-SM device (N=K=4096 wave sweep, "
                                "square point); replicas per GPU", "M": M, "N": N, "K": K,
                    "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) before every timed step",
+                   "clock_settle": "~30 ms of untimed steps between the clock sampler's start and the timed steps",
                    "schedule": {k: plan[k] for k in ("bn", "tail_split", "num_units", "grid",
                                                       "wave_efficiency")}},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": 2 * M * K * 2,
@@ -757,6 +790,25 @@ def main() -> None:
     line.update(extras)
     line["summary"] = summarize(line)  # last key: a driver that keeps the line's tail keeps this
     print(json.dumps(line), flush=True)
+
+
+def triton_reference(dev, sm_levels) -> dict:
+    """The reference's own Triton kernels on this GPU (GEMM 4096^3 fp16 per
+    partition, the MoE segment case at 64 SMs) beside the tcgen05 kernels;
+    unavailable when the reference package is not installed under
+    baseline/_ref."""
+    sys.path.insert(0, str(REPO / "baseline"))
+    try:
+        import triton_comparator as tc
+    finally:
+        sys.path.pop(0)
+    why = tc.available()
+    if why:
+        return {"unavailable": why}
+    try:
+        return tc.compare(dev, sm_levels=tuple(sm_levels), moe_levels=(64,))
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
 
 
 def summarize(line: dict) -> dict:
@@ -795,6 +847,16 @@ def summarize(line: dict) -> dict:
                         "phases_ms": ep["phases_ms_unchunked"],
                         "a2a_gbs": [ep["all_to_all"].get("dispatch_gbs_per_rank"),
                                     ep["all_to_all"].get("combine_gbs_per_rank")]}
+    tr = line.get("triton_reference")
+    if tr:
+        if "unavailable" in tr:
+            sm["triton_reference"] = tr["unavailable"]
+        else:
+            sm["triton_order"] = "SMs: reference Triton us, tcgen05 us, x speed-up (fp16 4096^3; moe: segment case)"
+            sm["triton_gemm"] = {str(r["actual_sm"]): [r["triton_us"], r["ek_us"], r["speedup_vs_triton"]]
+                                 for r in tr["gemm_4096_fp16"] if "error" not in r}
+            sm["triton_moe"] = {str(r["actual_sm"]): [r["triton_us"], r["ek_us"], r["speedup_vs_triton"]]
+                                for r in tr["moe_segment"] if "error" not in r}
     if "cpu_baseline" in line:
         sm["cpu_gemm_tflops"] = [line["cpu_baseline"]["value"], line["cpu_baseline"]["cores"]]
     return sm
