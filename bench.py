@@ -429,7 +429,9 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
     else:
         gemm_stream, gemm_sms = torch.cuda.current_stream(dev), total
         comm_stream, comm_sms = torch.cuda.Stream(dev), 0
-    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms))
+    # fixed-capacity exchanges: equal all-to-all splits known to the host, so
+    # nothing is read back between the routing and the combine
+    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto")
     # Two chunks let the dispatch / combine of one half overlap the expert
     # GEMMs of the other, but each chunk streams every local expert's weights
     # again: worth it only where the experts are compute-bound, i.e. with
@@ -467,6 +469,12 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
         for key, ph in (("dispatch", "dispatch"), ("combine", "combine_exchange")):
             t = phases.get(ph, 0.0)
             a2a[f"{key}_gbs_per_rank"] = round(prof[f"{key}_bytes"] / (t * 1e-3) / 1e9, 1) if t > 0 else None
+    from elastikernel_b200 import _lib
+
+    # overflow of a rank's capacity shows in the device status word (read, not cleared)
+    overflow = bool(_lib.device_status(dev.index if dev.index is not None else 0, clear=False)
+                    & _lib.EK_STATUS_CAPACITY)
+    overflow = bool(max_over_ranks(float(overflow), world))
     err, err_q = ep_parity(dev, x, logits, out, qw, E, k, world, rank)
     flop = T * k * 6.0 * H * I
     tf = flop / (ms * 1e-3) / 1e12
@@ -480,7 +488,9 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
             "ep_max_rel_err": err, "ep_parity_tol": 3e-2, "ep_max_rel_err_act_e4m3": err_q,
             "fp8_scales": "power-of-two, applied by the tensor cores (kind::mxf8f6f4.block_scale)" if FP8_POW2
             else "fp32, applied per 128-wide K block in the epilogue",
-            "host_sync": "per-chunk count exchange read on the host (all-to-all split sizes)"}
+            "host_sync": "none: fixed-capacity exchanges (equal all-to-all splits, padding rows on a dummy expert)",
+            "capacity_rows_per_rank": prof["capacity"], "rows_routed_per_rank": T * k,
+            "capacity_overflow": overflow}
 
 
 def ep_parity(dev, x, logits, out, qw, E: int, k: int, world: int, rank: int, per_rank: int = 32) -> float:

@@ -30,6 +30,7 @@ EK_STATUS_WAIT_TIMEOUT = 1
 EK_STATUS_BAD_EXPERT = 2
 EK_STATUS_BAD_INDEX = 4
 EK_STATUS_BAD_SCALE = 8
+EK_STATUS_CAPACITY = 16
 
 LIB_PATH = Path(__file__).with_name("_ek.so")
 
@@ -101,6 +102,8 @@ _SIGNATURES = {
     "ek_moe_gather_cols_f32": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_int, _c_vp, _c_vp]),
     "ek_moe_slot_rows": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),
     "ek_ep_pack_meta": (_c_int, [_c_vp, _c_int, _c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_ep_capacity_layout": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_vp,
+                                       _c_vp, _c_vp]),
     "ek_moe_combine_rows": (_c_int, [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_segment_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                      _c_vp]),

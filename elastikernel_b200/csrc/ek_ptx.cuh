@@ -25,6 +25,7 @@ enum StatusBits : int {
   kStatusBadExpert = 2,        // a grouped GEMM block named an expert out of range
   kStatusBadIndex = 4,         // a permutation index out of range
   kStatusBadScale = 8,         // a block-scaled GEMM got a scale that is not a power of two
+  kStatusCapacity = 16,        // an expert-parallel dispatch had more rows for a rank than its capacity
 };
 
 // A wait that has not completed after this many nanoseconds is treated as a

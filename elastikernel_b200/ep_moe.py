@@ -14,6 +14,16 @@ Eg = num_experts / world_size. One forward pass:
 5. send the rows back (all-to-all with the splits reversed);
 6. sum every token's k returned rows in choice order (ek_moe_combine_rows).
 
+Two ways to size the exchanges. By default the per-rank counts are
+exchanged and read on the host, which sizes both all-to-alls exactly. With
+``capacity`` set, every rank sends every other rank exactly ``capacity`` rows
+(padding rows carry a dummy expert id and are never computed), so the
+exchanges have equal splits the host knows in advance: nothing is read back
+and the layer can be captured in a CUDA graph. "auto" sizes the capacity for
+a uniform routing (mean + 6 standard deviations of a destination's count);
+slots past it are dropped and flagged in the device status word
+(EK_STATUS_CAPACITY).
+
 The reference has no multi-GPU path (its only parallelism is SM partitioning
 inside one GPU); this follows the expert-parallel MoE layout of the hot-path
 spec. The kernel steps go through an ``ops`` object: ``CudaEPOps`` (the
@@ -22,6 +32,7 @@ the same orchestration with a CPU implementation on gloo ranks).
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -34,9 +45,10 @@ class Dispatched:
 
     T: int
     topk: int
-    send_counts: list
-    recv_counts: list
-    slot_row: torch.Tensor  # [T*k] row of every slot in send order
+    send_counts: list | None  # exact exchanges: rows to / from every rank
+    recv_counts: list | None
+    slot_row: torch.Tensor  # [T*k] row of every slot in send order (-1: dropped)
+    capacity: int = 0  # fixed-capacity exchanges: rows per rank (0: exact)
 
 
 class CudaEPOps:
@@ -84,9 +96,59 @@ class CudaEPOps:
                                                    _ops.current_stream_handle(dev)), "ek_moe_slot_rows")
         return slot_row
 
-    def experts(self, x_recv, local_ids, w_recv, w1, w2, w3):
+    def capacity_layout(self, perm, ids, wts, experts_per_rank, world, capacity):
+        """Fixed-capacity send layout (ek_ep_capacity_layout): per capacity
+        row its slot, local expert id (experts_per_rank for padding) and
+        weight, and every slot's capacity row (-1 when dropped)."""
+        from . import _lib, _ops
+
+        dev = ids.device
+        n = ids.numel()
+        rows = world * capacity
+        out = {"slots": torch.empty(rows, dtype=torch.int32, device=dev),
+               "local_ids": torch.empty(rows, dtype=torch.int32, device=dev),
+               "weights": torch.empty(rows, dtype=torch.float32, device=dev),
+               "slot_row": torch.empty(n, dtype=torch.int32, device=dev),
+               "rows": torch.full((1,), rows, dtype=torch.int32, device=dev), "n": n, "topk": ids.shape[1]}
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_ep_capacity_layout(
+                perm["sorted_slots"].data_ptr(), perm["expert_counts"].data_ptr(), world, capacity, n, ids.data_ptr(),
+                wts.data_ptr(), experts_per_rank, out["slots"].data_ptr(), out["local_ids"].data_ptr(),
+                out["weights"].data_ptr(), out["slot_row"].data_ptr(), _ops.current_stream_handle(dev)),
+                "ek_ep_capacity_layout")
+        return out
+
+    def gather_capacity(self, cap, src):
+        """Rows of `src` (one per token) in the capacity layout; padding rows are left unwritten."""
+        from . import _lib, _ops
+
+        dev = src.device
+        rows = cap["slots"].numel()
+        dst = torch.empty((rows,) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
+        row_bytes = src[0].numel() * src.element_size()
+        with _ops._on_device(dev):
+            _lib.check(_lib.lib().ek_moe_gather_rows(cap["slots"].data_ptr(), cap["rows"].data_ptr(), rows, cap["n"],
+                                                     cap["topk"], src.data_ptr(), row_bytes, dst.data_ptr(),
+                                                     _ops.current_stream_handle(dev)), "ek_moe_gather_rows")
+        return dst
+
+    @staticmethod
+    def _local_permute(local_ids, E, x, block_m, dummy):
+        """Expert-major layout of the received rows. With `dummy`, ids equal to
+        E mark padding rows: they form an extra expert after the real ones,
+        which the GEMMs (given E experts) never reach."""
+        from . import _ops
+
+        R = local_ids.numel()
+        perm = _ops.moe_permute(local_ids.view(R, 1), E + 1 if dummy else E, x=x, block_m=block_m)
+        if dummy:
+            perm = dict(perm, E=E, expert_counts=perm["expert_counts"][:E])
+        return perm
+
+    def experts(self, x_recv, local_ids, w_recv, w1, w2, w3, dummy: bool = False):
         """Local experts on the received rows; row r of the result is
-        w_recv[r] * expert(local_ids[r])(x_recv[r])."""
+        w_recv[r] * expert(local_ids[r])(x_recv[r]) (rows of the dummy
+        expert, with `dummy`, are not computed)."""
         from . import _ops
 
         R = x_recv.shape[0]
@@ -96,8 +158,8 @@ class CudaEPOps:
         E = w1.shape[0]
         layout = _ops.moe_layout(int(self.num_sms or _ops._stream_sms(x_recv.device, _ops.current_stream_handle(
             x_recv.device))), E, R)
-        if layout == "packed":
-            perm = _ops.moe_permute(local_ids.view(R, 1), E, x=x_recv, block_m=1)
+        if layout == "packed" or dummy:
+            perm = self._local_permute(local_ids, E, x_recv, 1, dummy)
             act = _ops.moe_gate_up_packed(perm, w1, w3, num_sms=self.num_sms)
             return _ops.moe_down_packed(perm, act, w2, w_recv, num_sms=self.num_sms)
         perm = _ops.moe_permute(local_ids.view(R, 1), E, x=x_recv)
@@ -125,14 +187,14 @@ class CudaEPOps:
                        "ek_moe_gather_rows")
         return dst
 
-    def experts_fp8(self, xq_recv, xs_recv, local_ids, w_recv, qw):
+    def experts_fp8(self, xq_recv, xs_recv, local_ids, w_recv, qw, dummy: bool = False):
         """Local block-scaled FP8 experts on received e4m3 rows and their 1 x 128 scales."""
         from . import _ops
 
         R = xq_recv.shape[0]
         if R == 0:
             return torch.empty((0, qw["H"]), dtype=torch.bfloat16, device=xq_recv.device)
-        perm = _ops.moe_permute(local_ids.view(R, 1), qw["E"], x=xq_recv, block_m=1)
+        perm = self._local_permute(local_ids, qw["E"], xq_recv, 1, dummy)
         xs = _ops.moe_gather_cols_f32(perm, xs_recv)  # K-block-major scales of the gathered rows
         act = _ops.moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=self.num_sms)
         aq, as_ = _ops.quant_e4m3_kmajor(act, pow2=bool(qw.get("pow2", False)))
@@ -157,7 +219,8 @@ class ExpertParallelMoE:
     block-scaled form (_ops.quant_moe_weights_fp8), in which case the rows
     are dispatched as e4m3 with 1 x 128 scales (half the bytes of bf16)."""
 
-    def __init__(self, num_experts: int, topk: int, w1=None, w2=None, w3=None, group=None, ops=None, qw=None):
+    def __init__(self, num_experts: int, topk: int, w1=None, w2=None, w3=None, group=None, ops=None, qw=None,
+                 capacity=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -173,6 +236,25 @@ class ExpertParallelMoE:
         self.w1, self.w2, self.w3, self.qw = w1, w2, w3, qw
         self.ops = ops or CudaEPOps()
         self._marks = None  # (phase, CUDA event) pairs while profile_phases runs
+        if capacity is not None and capacity != "auto" and int(capacity) < 0:
+            raise ValueError("capacity must be None, 'auto' or a row count >= 0")
+        self.capacity = capacity  # None: exact exchanges (host read of the counts)
+
+    def capacity_rows(self, n_slots: int) -> int:
+        """Rows per destination rank of a fixed-capacity exchange of n_slots
+        slots: the given count, or for "auto" the mean of a uniform routing
+        plus 6 standard deviations of a destination's (binomial) count, plus
+        16, rounded up to 16 (one rank: exactly n_slots). Every rank must use
+        the same value, so with "auto" every rank passes the same number of
+        tokens."""
+        if self.capacity != "auto":
+            return int(self.capacity)
+        G = self.world
+        if G == 1:
+            return n_slots
+        m = n_slots / G
+        c = math.ceil(m + 6.0 * math.sqrt(m * (1.0 - 1.0 / G)) + 16)
+        return min(n_slots, -(-c // 16) * 16)
 
     def _mark(self, name: str) -> None:
         if self._marks is not None:
@@ -192,6 +274,8 @@ class ExpertParallelMoE:
     def dispatch(self, x, gate_logits):
         """Route, sort by destination and exchange rows + metadata.
         Returns (x_recv, local_ids_recv, w_recv, Dispatched)."""
+        if self.capacity is not None:
+            return self._dispatch_capacity(x, gate_logits)
         ops = self.ops
         T, H = x.shape
         self._mark("start")
@@ -231,10 +315,45 @@ class ExpertParallelMoE:
         self._mark("dispatch")
         return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, send_counts, recv_counts, slot_row)
 
+    def _dispatch_capacity(self, x, gate_logits):
+        """dispatch() with fixed-capacity exchanges: equal splits of
+        capacity rows per rank, no host read."""
+        ops = self.ops
+        T, H = x.shape
+        n = T * self.topk
+        C = self.capacity_rows(n)
+        self._mark("start")
+        ids, wts = ops.route(gate_logits, self.topk)
+        dest = ops.dest_of(ids, self.experts_per_rank)
+        xs = None
+        if self.fp8:
+            x, xs = (ops.quant_rows(x, pow2=True) if self.qw.get("pow2") else ops.quant_rows(x))
+        perm = ops.permute_by_dest(dest, self.world, None)  # the slot order only
+        cap = ops.capacity_layout(perm, ids, wts, self.experts_per_rank, self.world, C)
+        x_send = ops.gather_capacity(cap, x)
+        xs_send = ops.gather_capacity(cap, xs) if self.fp8 else None
+        self._mark("route_permute")
+        self._mark("count_exchange")  # nothing to exchange: the splits are fixed
+        x_recv = torch.empty_like(x_send)
+        if self.fp8:  # byte view: the exchange does not need to know the float8 type
+            self._a2a(x_recv.view(torch.uint8), x_send.view(torch.uint8), None, None)
+            xs_recv = torch.empty_like(xs_send)
+            self._a2a(xs_recv, xs_send, None, None)
+            x_recv = (x_recv, xs_recv)
+        else:
+            self._a2a(x_recv, x_send, None, None)
+        ids_recv = torch.empty_like(cap["local_ids"])
+        self._a2a(ids_recv, cap["local_ids"], None, None)
+        w_recv = torch.empty_like(cap["weights"])
+        self._a2a(w_recv, cap["weights"], None, None)
+        self._mark("dispatch")
+        return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, None, None, cap["slot_row"], capacity=C)
+
     def combine(self, y_local, d: Dispatched):
         n = d.T * d.topk
         self._mark("experts")
-        y_back = torch.empty((n, y_local.shape[1]), dtype=y_local.dtype, device=y_local.device)
+        rows = self.world * d.capacity if d.capacity else n
+        y_back = torch.empty((rows, y_local.shape[1]), dtype=y_local.dtype, device=y_local.device)
         self._a2a(y_back, y_local, d.send_counts, d.recv_counts)
         self._mark("combine_exchange")
         out = self.ops.combine_rows(y_back, d.slot_row, d.T, d.topk)
@@ -260,16 +379,22 @@ class ExpertParallelMoE:
             self._marks = None
         ms = {name: marks[i - 1][1].elapsed_time(ev) for i, (name, ev) in enumerate(marks) if i > 0}
         H = x.shape[1]
-        remote_send = sum(c for r, c in enumerate(d.send_counts) if r != self.rank)
-        remote_back = sum(c for r, c in enumerate(d.recv_counts) if r != self.rank)
+        if d.capacity:  # every rank sends and receives `capacity` rows per peer, padding included
+            remote_send = remote_back = (self.world - 1) * d.capacity
+            sent = received = self.world * d.capacity
+        else:
+            remote_send = sum(c for r, c in enumerate(d.send_counts) if r != self.rank)
+            remote_back = sum(c for r, c in enumerate(d.recv_counts) if r != self.rank)
+            sent, received = int(sum(d.send_counts)), int(sum(d.recv_counts))
         row_bytes = (H + (H // 128) * 4 if self.fp8 else 2 * H) + 8  # row (+ scales) + expert id + weight
         return {"out": out, "ms": ms, "dispatch_bytes": remote_send * row_bytes, "combine_bytes": remote_back * 2 * H,
-                "rows_sent": int(sum(d.send_counts)), "rows_received": int(sum(d.recv_counts))}
+                "rows_sent": sent, "rows_received": received, "capacity": d.capacity}
 
     def _experts(self, x_recv, ids_recv, w_recv):
+        kw = {"dummy": True} if self.capacity is not None else {}
         if self.fp8:
-            return self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw)
-        return self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3)
+            return self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw, **kw)
+        return self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3, **kw)
 
     def forward(self, x, gate_logits, chunks: int = 1, compute_stream=None, comm_stream=None):
         """The layer for this rank's tokens x [T, H] (router logits [T, E]).

@@ -56,6 +56,7 @@ int ek_device_status(int dev, int clear, int* status_out);
 #define EK_STATUS_BAD_EXPERT 2
 #define EK_STATUS_BAD_INDEX 4
 #define EK_STATUS_BAD_SCALE 8  /* a block-scaled (_fp8mx) GEMM got a scale that is not a power of two */
+#define EK_STATUS_CAPACITY 16  /* ek_ep_capacity_layout dropped slots past a rank's capacity */
 
 /* --------------------------------------------------- green-context partitions
  * Replaces green_ctx.py (get_sm_alignment :46, get_total_sm_count :65,
@@ -348,6 +349,22 @@ int ek_ep_pack_meta(const int* sorted_slots, int rows, const int* topk_ids, cons
                     int experts_per_rank, int* local_ids, float* weights_out, void* stream);
 int ek_moe_combine_rows(const void* y, const int* slot_row, void* out, int T, int topk, int H, int n_rows,
                         void* stream);
+
+/* Fixed-capacity dispatch layout: after ek_moe_permute by destination rank
+ * (block_m = 1; sorted_slots and the per-rank dest_counts on the device),
+ * lays the n_slots = T*k slots out as world blocks of `capacity` rows, so the
+ * row all-to-all has equal splits known to the host. For capacity row
+ * r = g*capacity + i: cap_slots[r] = the i-th slot bound for rank g (or
+ * n_slots when rank g has <= i slots), local_ids[r] = its expert id local to
+ * rank g (experts_per_rank, a dummy expert, for padding rows), weights_out[r]
+ * = its routing weight (0 for padding). slot_row[s] = the capacity row of
+ * slot s, or -1 when s is past its rank's capacity; such slots are dropped
+ * and EK_STATUS_CAPACITY is raised in the device status word. The token rows
+ * then go into the capacity layout with ek_moe_gather_rows(cap_slots, ...).
+ * world <= 1024. */
+int ek_ep_capacity_layout(const int* sorted_slots, const int* dest_counts, int world, int capacity, int n_slots,
+                          const int* topk_ids, const float* topk_weights, int experts_per_rank, int* cap_slots,
+                          int* local_ids, float* weights_out, int* slot_row, void* stream);
 
 /* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);

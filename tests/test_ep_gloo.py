@@ -4,9 +4,13 @@ The same ExpertParallelMoE dispatch / all-to-all / combine logic the GPU
 path runs, driven by an oracle-backed CPU implementation of the kernel steps,
 is checked against the single-process oracle with all experts: the
 bookkeeping (destination sort, split sizes, per-row metadata, return order,
-choice-order combine) must reproduce the MoE exactly. A second test makes one
-rank leave before the exchange and checks that the other rank gets an error
-instead of hanging (failure made on the host, no GPU involved).
+choice-order combine) must reproduce the MoE exactly, with exact exchanges
+and with fixed-capacity ones (equal splits, padding rows on a dummy
+expert; a capacity too small for the routing drops the slots past it and
+raises the overflow flag, and every token without a dropped slot is still
+exact). Another test makes one rank leave before the exchange and checks
+that the other rank gets an error instead of hanging (failure made on the
+host, no GPU involved).
 """
 from __future__ import annotations
 
@@ -28,6 +32,9 @@ E, K_TOP, H, I = 8, 2, 32, 48
 class CpuEPOps:
     """Oracle-backed CPU implementation of the kernel steps (test only)."""
 
+    def __init__(self):
+        self.dropped = set()  # slots a fixed-capacity layout dropped (the device status flag's stand-in)
+
     def route(self, logits, topk):
         ids, w = om.route_ref(logits.numpy(), topk)
         return torch.from_numpy(ids), torch.from_numpy(w)
@@ -40,7 +47,7 @@ class CpuEPOps:
         r = om.permute_ref(dest.numpy(), world, 1)
         slots = torch.from_numpy(r["sorted_slots"][: T * k].astype(np.int64))
         return {"sorted_slots": slots, "expert_counts": torch.from_numpy(r["expert_counts"]),
-                "x_perm": x[slots // k], "max_rows": T * k, "T": T, "topk": k}
+                "x_perm": None if x is None else x[slots // k], "max_rows": T * k, "T": T, "topk": k}
 
     def pack_meta(self, perm, ids, wts, experts_per_rank):
         s = perm["sorted_slots"]
@@ -52,17 +59,50 @@ class CpuEPOps:
         out[s] = torch.arange(s.numel())
         return out
 
-    def experts(self, x_recv, local_ids, w_recv, w1, w2, w3):
+    def capacity_layout(self, perm, ids, wts, experts_per_rank, world, capacity):
+        s = perm["sorted_slots"]
+        counts = perm["expert_counts"].tolist()
+        n = ids.numel()
+        rows = world * capacity
+        slots = torch.full((rows,), n, dtype=torch.int64)
+        local = torch.full((rows,), experts_per_rank, dtype=torch.int32)
+        w = torch.zeros(rows)
+        slot_row = torch.full((n,), -1, dtype=torch.int64)
+        start = 0
+        for g, c in enumerate(counts):
+            for i in range(c):
+                sl = int(s[start + i])
+                if i < capacity:
+                    r = g * capacity + i
+                    slots[r] = sl
+                    local[r] = int(ids.reshape(-1)[sl]) % experts_per_rank
+                    w[r] = float(wts.reshape(-1)[sl])
+                    slot_row[sl] = r
+                else:
+                    self.dropped.add(sl)
+            start += c
+        return {"slots": slots, "local_ids": local, "weights": w, "slot_row": slot_row, "n": n, "topk": ids.shape[1]}
+
+    def gather_capacity(self, cap, src):
+        dst = torch.zeros((cap["slots"].numel(),) + tuple(src.shape[1:]), dtype=src.dtype)
+        valid = cap["slots"] < cap["n"]
+        dst[valid] = src[cap["slots"][valid] // cap["topk"]]
+        return dst
+
+    def experts(self, x_recv, local_ids, w_recv, w1, w2, w3, dummy=False):
         y = torch.zeros((x_recv.shape[0], w2.shape[1]))
         for r in range(x_recv.shape[0]):
             e = int(local_ids[r])
+            if dummy and e == w1.shape[0]:
+                continue  # padding row
             h = x_recv[r].float()
             a = torch.nn.functional.silu(w1[e].float() @ h) * (w3[e].float() @ h)
             y[r] = float(w_recv[r]) * (w2[e].float() @ a)
         return y
 
     def combine_rows(self, y_back, slot_row, T, topk):
-        return y_back[slot_row.view(T, topk)].sum(dim=1)
+        r = slot_row.view(T, topk)
+        return (y_back[r.clamp_min(0)] * (r >= 0).unsqueeze(-1)).sum(dim=1)  # dropped slots add nothing
 
 
 def _free_port() -> int:
@@ -91,9 +131,12 @@ def _worker(rank, world, port, q, mode):
         w1, w2, w3 = _weights()
         eg = E // world
         sl = slice(rank * eg, (rank + 1) * eg)
-        moe = ExpertParallelMoE(E, K_TOP, w1[sl], w2[sl], w3[sl], ops=CpuEPOps())
+        ops = CpuEPOps()
+        capacity = {"capacity": "auto", "capacity_small": 3}.get(mode)
+        moe = ExpertParallelMoE(E, K_TOP, w1[sl], w2[sl], w3[sl], ops=ops, capacity=capacity)
         g = torch.Generator().manual_seed(100 + rank)
-        T = 17 + 5 * rank  # ragged token counts per rank
+        # ragged token counts per rank (a fixed capacity needs the same count everywhere)
+        T = 19 if capacity is not None else 17 + 5 * rank
         x = torch.randn((T, H), generator=g)
         logits = torch.randn((T, E), generator=g)
         if mode == "leave":
@@ -106,8 +149,15 @@ def _worker(rank, world, port, q, mode):
         # "chunked": the tokens go through in 3 chunks (ragged: T is not a multiple of 3)
         out = moe(x, logits, chunks=3) if mode == "chunked" else moe(x, logits)
         ref = om.moe_ref(x.numpy(), logits.numpy(), w1, w2, w3, K_TOP)
-        err = float(np.abs(out.numpy() - ref).max() / np.abs(ref).max())
-        q.put((rank, err))
+        if mode == "capacity_small":
+            # the slots this rank dropped belong to its own tokens; the others must be exact
+            hit = sorted({s // K_TOP for s in ops.dropped})
+            keep = np.setdiff1d(np.arange(T), hit)
+            err = float(np.abs(out.numpy()[keep] - ref[keep]).max() / np.abs(ref).max())
+            q.put((rank, (err, len(hit))))
+        else:
+            err = float(np.abs(out.numpy() - ref).max() / np.abs(ref).max())
+            q.put((rank, err))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent
         q.put((rank, "error: " + repr(e)[:200] + traceback.format_exc()[-300:]))
@@ -131,12 +181,24 @@ def _run(world, mode):
     return results
 
 
-@pytest.mark.parametrize("world,mode", [(2, "normal"), (4, "normal"), (2, "chunked")])
+@pytest.mark.parametrize("world,mode", [(2, "normal"), (4, "normal"), (2, "chunked"), (2, "capacity"),
+                                        (4, "capacity")])
 def test_ep_matches_single_process_oracle(world, mode):
     res = _run(world, mode)
     for rank, err in res.items():
         assert not isinstance(err, str), f"rank {rank}: {err}"
         assert err < 1e-5, f"rank {rank}: max rel err {err:.3e}"
+
+
+def test_ep_capacity_overflow_drops_and_flags():
+    """3 rows per destination for 19 tokens x 2 choices: most slots are
+    dropped; the tokens that kept all their slots are still exact."""
+    res = _run(2, "capacity_small")
+    for rank, v in res.items():
+        assert not isinstance(v, str), f"rank {rank}: {v}"
+        err, n_hit = v
+        assert n_hit > 0, "the small capacity should have dropped slots"
+        assert err < 1e-5, f"rank {rank}: max rel err {err:.3e} on the tokens that kept their slots"
 
 
 def test_ep_rank_leaving_is_an_error_not_a_hang():

@@ -4,6 +4,10 @@
   metadata packing, slot rows, indexed combine) around the local experts must
   reproduce the fused single-GPU layer, for bf16 and for e4m3 block-scaled
   experts with e4m3 dispatch;
+* fixed-capacity exchanges (equal splits, padding rows on a dummy expert)
+  give the exact exchange's result; a capacity too small for the routing
+  drops the slots past it, raises EK_STATUS_CAPACITY, and leaves every token
+  that kept its slots unchanged;
 * world size 2 (skipped with fewer GPUs): NCCL all-to-all over NVLink, each
   rank's EP output against the fused layer run with all experts on that rank.
 Tolerance: max|out - ref| / max|ref| <= 1e-2 (same kernels, same math).
@@ -67,6 +71,47 @@ def test_ep_world1_fp8(cuda_dev):
 
 
 @pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("capacity", ["auto", 333 * K_TOP + 37])
+def test_ep_world1_capacity(cuda_dev, fp8, capacity):
+    """Fixed-capacity exchanges ("auto": exactly the routed rows on one rank;
+    an explicit capacity above them: padding rows on the dummy expert)
+    against the exact exchanges."""
+    from elastikernel_b200 import _lib, _ops
+    from elastikernel_b200.ep_moe import ExpertParallelMoE
+
+    w1, w2, w3 = _weights(cuda_dev)
+    kw = {"qw": _ops.quant_moe_weights_fp8(w1, w2, w3, pow2=True)} if fp8 else {"w1": w1, "w2": w2, "w3": w3}
+    x, logits = _tokens(cuda_dev, 0, 333)
+    ref = ExpertParallelMoE(E, K_TOP, **kw)(x, logits)
+    _lib.device_status(0, clear=True)
+    out = ExpertParallelMoE(E, K_TOP, capacity=capacity, **kw)(x, logits)
+    st = _lib.device_status(0, clear=True)
+    assert st == 0, f"status {st:#x}"
+    assert max_rel_err(out, ref.float().cpu().numpy()) <= 1e-3
+
+
+def test_ep_world1_capacity_overflow_flags(cuda_dev):
+    """One rank, capacity 50 rows short of the T*k routed slots: the slots
+    are dropped in destination-sorted (slot index) order, so the tokens whose
+    k slots all lie below the capacity are unchanged; the status word says
+    slots were dropped."""
+    from elastikernel_b200 import _lib
+    from elastikernel_b200.ep_moe import ExpertParallelMoE
+
+    w1, w2, w3 = _weights(cuda_dev)
+    T = 333
+    C = T * K_TOP - 50
+    x, logits = _tokens(cuda_dev, 0, T)
+    ref = ExpertParallelMoE(E, K_TOP, w1, w2, w3)(x, logits)
+    _lib.device_status(0, clear=True)
+    out = ExpertParallelMoE(E, K_TOP, w1, w2, w3, capacity=C)(x, logits)
+    st = _lib.device_status(0, clear=True)
+    assert st & _lib.EK_STATUS_CAPACITY and not st & ~_lib.EK_STATUS_CAPACITY, f"status {st:#x}"
+    keep = C // K_TOP
+    assert max_rel_err(out[:keep], ref[:keep].float().cpu().numpy()) <= 1e-3
+
+
+@pytest.mark.parametrize("fp8", [False, True])
 def test_ep_world1_chunked_streams(cuda_dev, fp8):
     """Chunks pipelined over two green-context partitions (experts on the
     large one, routing / dispatch / combine on the small one) give the same
@@ -126,6 +171,12 @@ def _worker(rank, world, port, q):
         comp, comm = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         out8c = ExpertParallelMoE(E, K_TOP, qw=qw)(x, logits, chunks=2, compute_stream=comp, comm_stream=comm)
         err_fp8 = max(err_fp8, max_rel_err(out8c, ref8.float().cpu().numpy()))
+        # fixed-capacity exchanges (both ranks route the same number of tokens)
+        xc, lc = _tokens(dev, rank, 256)
+        outc = ExpertParallelMoE(E, K_TOP, qw=qw, capacity="auto")(xc, lc, chunks=2, compute_stream=comp,
+                                                                     comm_stream=comm)
+        refc = _ops.fused_moe_fp8(xc, lc, qw_all, K_TOP)
+        err_fp8 = max(err_fp8, max_rel_err(outc, refc.float().cpu().numpy()))
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
