@@ -583,11 +583,11 @@ def moe_bench(dev, steps: int, hbm_gbs: float, peak_bf16_tflops: float, cpu: boo
                 for _ in range(2):
                     _ops.fused_moe(x, logits, w1, w2, w3, k)
                 r = time_on_stream(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k), stream,
-                                   reps=max(3, steps // 2))
+                                   reps=max(3, steps // 2), warmup=2)
                 # the same layer replayed from a CUDA graph (no host work between its launches)
                 y = torch.empty((T, H), device=dev, dtype=torch.bfloat16)
                 cap = Captured(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k, out=y), stream)
-                rg = time_on_stream(cap, stream, reps=max(3, steps // 2))
+                rg = time_on_stream(cap, stream, reps=max(3, steps // 2), warmup=2)
                 del cap
                 ids, _ = _ops.moe_route(logits, k)
             hit = int(torch.unique(ids).numel())

@@ -86,6 +86,8 @@ _SIGNATURES = {
     "ek_moe_permute_scratch_bytes": (_c_size, [_c_int, _c_int, _c_int]),
     "ek_moe_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int,
                                 _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_moe_route_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
+                                      _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                 _c_int, _c_int, _c_int, _c_vp]),
     "ek_moe_down": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,

@@ -297,6 +297,47 @@ def moe_permute(topk_ids: torch.Tensor, num_experts: int, x: torch.Tensor | None
             "block_m": block_m}
 
 
+def moe_route_permute(gate_logits: torch.Tensor, topk: int, num_experts: int, x: torch.Tensor | None = None,
+                      block_m: int = BLOCK_M) -> tuple[torch.Tensor, torch.Tensor, dict]:
+    """moe_route then moe_permute (same outputs): ids, weights and the
+    permutation dict. Up to 128 slots the routing, the permutation and a
+    small row gather are one launch."""
+    dev = _require_cuda(gate_logits, x)
+    if gate_logits.dtype != torch.float32 or gate_logits.dim() != 2:
+        raise RuntimeError("gate_logits must be a 2-D float32 tensor")
+    _contig("gate_logits", gate_logits)
+    T, E_logits = gate_logits.shape
+    E = int(num_experts)
+    if E_logits != E:
+        raise RuntimeError("gate_logits must have one column per expert")
+    k = int(topk)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+    max_rows = int(lib().ek_moe_max_padded_rows(T, k, E, block_m))
+    sorted_slots = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    block_expert = torch.empty(max_rows // block_m, dtype=torch.int32, device=dev)
+    num_rows = torch.empty(1, dtype=torch.int32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    x_perm = None
+    H = es = 0
+    if x is not None:
+        _contig("x", x)
+        if x.dim() != 2 or x.shape[0] != T:
+            raise RuntimeError("x must be [T, H]")
+        H, es = x.shape[1], x.element_size()
+        x_perm = torch.empty((max_rows, H), dtype=x.dtype, device=dev)
+    scratch = torch.empty(int(lib().ek_moe_permute_scratch_bytes(T, k, E)), dtype=torch.uint8, device=dev)
+    with _on_device(dev):
+        check(lib().ek_moe_route_permute(gate_logits.data_ptr(), T, E, k, ids.data_ptr(), wts.data_ptr(), block_m,
+                                         sorted_slots.data_ptr(), block_expert.data_ptr(), num_rows.data_ptr(),
+                                         counts.data_ptr(), _ptr(x), H, es, _ptr(x_perm), scratch.data_ptr(),
+                                         current_stream_handle(dev)), "ek_moe_route_permute")
+    perm = {"sorted_slots": sorted_slots, "block_expert": block_expert, "num_rows_padded": num_rows,
+            "expert_counts": counts, "x_perm": x_perm, "max_rows": max_rows, "T": T, "topk": k, "E": E,
+            "block_m": block_m}
+    return ids, wts, perm
+
+
 def _check_bf16(name: str, t: torch.Tensor) -> None:
     if t.dtype != torch.bfloat16:
         raise RuntimeError(f"{name} must be bfloat16")
@@ -499,10 +540,9 @@ def fused_moe_fp8(hidden_states: torch.Tensor, gate_logits: torch.Tensor, qw: di
     T = hidden_states.shape[0]
     if T == 0:
         return out if out is not None else torch.empty_like(hidden_states)
-    ids, wts = moe_route(gate_logits, topk)
     pow2 = bool(qw.get("pow2", False))  # tokens and activations take the weights' scale form
     xq_tok, xs_tok = quant_e4m3(hidden_states, block=(1, 128), pow2=pow2)
-    perm = moe_permute(ids, qw["E"], x=xq_tok, block_m=1)
+    ids, wts, perm = moe_route_permute(gate_logits, topk, qw["E"], x=xq_tok, block_m=1)
     xs = moe_gather_cols_f32(perm, xs_tok)
     act = moe_gate_up_fp8bs(perm, perm["x_perm"], xs, qw, num_sms=num_sms)
     aq, as_ = quant_e4m3_kmajor(act, pow2=pow2)
@@ -595,14 +635,13 @@ def fused_moe(hidden_states: torch.Tensor, gate_logits: torch.Tensor, w1: torch.
     sms = int(num_sms) if num_sms else _stream_sms(dev, current_stream_handle(dev))
     if layout == "auto":
         layout = moe_layout(sms, w1.shape[0], T * topk)
-    ids, wts = moe_route(gate_logits, topk)
     if layout == "packed" and w1.shape[0] <= 256:
-        perm = moe_permute(ids, w1.shape[0], x=hidden_states, block_m=1)
+        ids, wts, perm = moe_route_permute(gate_logits, topk, w1.shape[0], x=hidden_states, block_m=1)
         act = moe_gate_up_packed(perm, w1, w3, num_sms=num_sms)
         y = moe_down_packed(perm, act, w2, wts, num_sms=num_sms)
     else:
-        perm = moe_permute(ids, w1.shape[0], x=hidden_states,
-                           block_m=padded_block_m(sms, w1.shape[0], T * topk))
+        ids, wts, perm = moe_route_permute(gate_logits, topk, w1.shape[0], x=hidden_states,
+                                           block_m=padded_block_m(sms, w1.shape[0], T * topk))
         act = moe_gate_up(perm, w1, w3, num_sms=num_sms)
         y = moe_down(perm, act, w2, wts, num_sms=num_sms)
     return moe_combine(y, T, topk, out=out)

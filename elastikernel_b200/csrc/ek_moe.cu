@@ -39,14 +39,16 @@ constexpr int kRouteMaxE = 256;   // logits per token held in registers: 8 per l
 constexpr int kRouteMaxK = 8;
 constexpr int kPermChunk = 1024;  // slots per permutation CTA
 constexpr int kPermMaxE = 1024;
+// up to this many slots the routing and the permutation run as one launch of
+// one CTA (decode sizes); past it the wide launches are faster (T = 128,
+// k = 2: 510 vs 506 us for the Mixtral layer)
+constexpr int kFrontMaxSlots = 128;
 
 // ------------------------------------------------------------------ routing
-__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int T, int E, int k,
-                                                    int* __restrict__ ids, float* __restrict__ wts) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const float* row = logits + (size_t)t * E;
+// One token's routing by one warp: logits row -> k expert ids and
+// renormalised weights (written by lane 0).
+__device__ __forceinline__ void route_token(const float* __restrict__ row, int E, int k, int lane,
+                                            int* __restrict__ ids_out, float* __restrict__ wts_out) {
   float v[kRouteMaxE / 32];
   float mx = -INFINITY;
 #pragma unroll
@@ -101,10 +103,18 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 #pragma unroll
     for (int j = 0; j < kRouteMaxK; ++j) {
       if (j >= k) break;
-      ids[(size_t)t * k + j] = sel[j];
-      wts[(size_t)t * k + j] = p[j] / psum;
+      ids_out[j] = sel[j];
+      wts_out[j] = p[j] / psum;
     }
   }
+}
+
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                                    int* __restrict__ ids, float* __restrict__ wts) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  route_token(logits + (size_t)t * E, E, k, lane, ids + (size_t)t * k, wts + (size_t)t * k);
 }
 
 // ------------------------------------------------------------------ permutation
@@ -125,12 +135,14 @@ __global__ void __launch_bounds__(kPermChunk) permute_count_kernel(const int* __
   for (int i = threadIdx.x; i < E; i += blockDim.x) chunk_counts[(size_t)blockIdx.x * E + i] = cnt[i];
 }
 
-__global__ void __launch_bounds__(kPermChunk)
-    permute_scatter_kernel(const int* __restrict__ ids, int n_slots, int E, int block_m,
-                           const int* __restrict__ chunk_counts, int n_chunks, int* __restrict__ sorted_slots,
-                           int* __restrict__ block_expert, int* __restrict__ num_rows_padded,
-                           int* __restrict__ expert_counts, int max_rows) {
-  extern __shared__ int sm[];
+// The stable scatter of chunk `chunk` (kPermChunk threads, `sm` = 35 E ints
+// of shared memory). chunk_counts == nullptr: a single chunk holds every slot
+// and counts them itself. Returns the padded row total (in every thread).
+__device__ __forceinline__ int permute_scatter_chunk(const int* __restrict__ ids, int n_slots, int E, int block_m,
+                                                     const int* __restrict__ chunk_counts, int n_chunks, int chunk,
+                                                     int* __restrict__ sorted_slots, int* __restrict__ block_expert,
+                                                     int* __restrict__ num_rows_padded,
+                                                     int* __restrict__ expert_counts, int max_rows, int* sm) {
   int* s_tot = sm;              // [E] slots per expert (all chunks)
   int* s_before = sm + E;       // [E] slots per expert in earlier chunks
   int* s_start = sm + 2 * E;    // [E] first padded row of each expert
@@ -147,14 +159,24 @@ __global__ void __launch_bounds__(kPermChunk)
   }
   for (int i = tid; i < 32 * E; i += blockDim.x) s_wcnt[i] = 0;
   __syncthreads();
-  const int n_counts = n_chunks * E;
+  if (chunk_counts == nullptr) {
+    if (tid < n_slots) {
+      const int e = ids[tid];
+      if (e >= 0 && e < E)
+        atomicAdd(&s_tot[e], 1);
+      else
+        atomicOr(&g_ek_status, kStatusBadIndex);
+    }
+  } else {
+    const int n_counts = n_chunks * E;
 #pragma unroll 4
-  for (int i = tid; i < n_counts; i += blockDim.x) {
-    const int v = __ldcg(chunk_counts + i);
-    if (v) {
-      const int c = i / E, e = i - c * E;
-      atomicAdd(&s_tot[e], v);
-      if (c < (int)blockIdx.x) atomicAdd(&s_before[e], v);
+    for (int i = tid; i < n_counts; i += blockDim.x) {
+      const int v = __ldcg(chunk_counts + i);
+      if (v) {
+        const int c = i / E, e = i - c * E;
+        atomicAdd(&s_tot[e], v);
+        if (c < chunk) atomicAdd(&s_before[e], v);
+      }
     }
   }
   __syncthreads();
@@ -187,8 +209,8 @@ __global__ void __launch_bounds__(kPermChunk)
   }
   __syncthreads();
 
-  if (blockIdx.x == 0) {
-    const int total = s_total;
+  const int total = s_total;
+  if (chunk == 0) {
     for (int e = tid; e < E; e += blockDim.x) expert_counts[e] = s_tot[e];
     if (tid == 0) *num_rows_padded = total;
     // sentinel in each expert's padding rows and past the used rows
@@ -215,7 +237,7 @@ __global__ void __launch_bounds__(kPermChunk)
 
   // stable rank of each slot inside this chunk: warp-level match, then the
   // counts of earlier warps
-  const int s = blockIdx.x * kPermChunk + tid;
+  const int s = chunk * kPermChunk + tid;
   int e = (s < n_slots) ? ids[s] : -1;
   const bool valid = (e >= 0 && e < E);
   if (!valid) e = -1;
@@ -229,6 +251,47 @@ __global__ void __launch_bounds__(kPermChunk)
     for (int w = 0; w < warp; ++w) pre += s_wcnt[w * E + e];
     dest = s_start[e] + s_before[e] + pre + rank_w;
     sorted_slots[dest] = s;
+  }
+  return total;
+}
+
+__global__ void __launch_bounds__(kPermChunk)
+    permute_scatter_kernel(const int* __restrict__ ids, int n_slots, int E, int block_m,
+                           const int* __restrict__ chunk_counts, int n_chunks, int* __restrict__ sorted_slots,
+                           int* __restrict__ block_expert, int* __restrict__ num_rows_padded,
+                           int* __restrict__ expert_counts, int max_rows) {
+  extern __shared__ int sm[];
+  permute_scatter_chunk(ids, n_slots, E, block_m, chunk_counts, n_chunks, (int)blockIdx.x, sorted_slots,
+                        block_expert, num_rows_padded, expert_counts, max_rows, sm);
+}
+
+// Small batches (T*k <= kPermChunk) in one CTA: routing (a warp per token),
+// the expert-sorted layout of the slots, and -- when the rows are few -- their
+// gather, with no launches in between. Same results as route_kernel +
+// permute_count/scatter_kernel + gather_rows_kernel.
+__global__ void __launch_bounds__(kPermChunk)
+    moe_front_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
+                     float* __restrict__ wts, int block_m, int* __restrict__ sorted_slots,
+                     int* __restrict__ block_expert, int* __restrict__ num_rows_padded,
+                     int* __restrict__ expert_counts, int max_rows, const uint8_t* __restrict__ x, int row_bytes,
+                     uint8_t* __restrict__ x_perm) {
+  extern __shared__ int sm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t = warp; t < T; t += kPermChunk / 32)
+    route_token(logits + (size_t)t * E, E, k, lane, ids + (size_t)t * k, wts + (size_t)t * k);
+  __syncthreads();  // the ids written above are read by other threads below
+  const int n_slots = T * k;
+  const int total = permute_scatter_chunk(ids, n_slots, E, block_m, nullptr, 1, 0, sorted_slots, block_expert,
+                                          num_rows_padded, expert_counts, max_rows, sm);
+  if (x == nullptr) return;
+  __syncthreads();  // sorted_slots complete
+  const int nvec = row_bytes / 16;
+  for (int r = warp; r < total; r += kPermChunk / 32) {
+    const int s = sorted_slots[r];
+    if (s < 0 || s >= n_slots) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(s / k) * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)r * row_bytes);
+    for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
   }
 }
 
@@ -550,6 +613,56 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
       expert_counts, (int)max_rows);
   rc = check_cuda(cudaGetLastError(), "permute scatter launch");
   if (rc || x == nullptr) return rc;
+  const int gather_blocks = (int)std::min<long long>((max_rows + 7) / 8, 148LL * 8);
+  gather_rows_kernel<<<std::max(gather_blocks, 1), 256, 0, s>>>(sorted_slots, num_rows_padded, (int)max_rows,
+                                                               (int)n_slots, topk, static_cast<const uint8_t*>(x),
+                                                               row_bytes, static_cast<uint8_t*>(x_perm));
+  return check_cuda(cudaGetLastError(), "row gather launch");
+}
+
+int ek_moe_route_permute(const float* logits, int T, int E, int topk, int* topk_ids, float* topk_weights,
+                         int block_m, int* sorted_slots, int* block_expert, int* num_rows_padded, int* expert_counts,
+                         const void* x, int H, int elem_bytes, void* x_perm, void* scratch, void* stream) {
+  clear_error();
+  const long long n_slots = (long long)T * topk;
+  if (T < 1 || n_slots > kFrontMaxSlots || E < 1 || E > kRouteMaxE || topk < 1 || topk > kRouteMaxK || topk > E ||
+      block_m < 1) {
+    // larger batches: the separate routing and permutation launches
+    int rc = ek_moe_route(logits, T, E, topk, topk_ids, topk_weights, stream);
+    if (rc) return rc;
+    return ek_moe_permute(topk_ids, T, topk, E, block_m, sorted_slots, block_expert, num_rows_padded, expert_counts,
+                          x, H, elem_bytes, x_perm, scratch, stream);
+  }
+  if (!logits || !topk_ids || !topk_weights || !sorted_slots || !block_expert || !num_rows_padded || !expert_counts)
+    return set_error(EK_ERR_INVALID, "route_permute: null pointer");
+  const int row_bytes = H * elem_bytes;
+  if (x) {
+    if (!x_perm || H <= 0 || elem_bytes <= 0 || row_bytes % 16 != 0 || !aligned16(x) || !aligned16(x_perm))
+      return set_error(EK_ERR_INVALID,
+                       "route_permute: gathered rows must be 16-byte multiples on 16-byte aligned buffers");
+  }
+  const int64_t max_rows = ek_moe_max_padded_rows(T, topk, E, block_m);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem_max = (3 * kPermMaxE + 32 * kPermMaxE) * (int)sizeof(int);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(moe_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max),
+                        "cudaFuncSetAttribute(front)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  // one CTA also gathers the rows while they are few (up to 256 KB); more
+  // rows go to the wide gather launch
+  const bool gather_here = x && n_slots * row_bytes <= (256 << 10);
+  const size_t smem = (size_t)(35 * E) * sizeof(int);
+  moe_front_kernel<<<1, kPermChunk, smem, s>>>(logits, T, E, topk, topk_ids, topk_weights, block_m, sorted_slots,
+                                                block_expert, num_rows_padded, expert_counts, (int)max_rows,
+                                                gather_here ? static_cast<const uint8_t*>(x) : nullptr, row_bytes,
+                                                static_cast<uint8_t*>(x_perm));
+  int rc = check_cuda(cudaGetLastError(), "route_permute launch");
+  if (rc || x == nullptr || gather_here) return rc;
   const int gather_blocks = (int)std::min<long long>((max_rows + 7) / 8, 148LL * 8);
   gather_rows_kernel<<<std::max(gather_blocks, 1), 256, 0, s>>>(sorted_slots, num_rows_padded, (int)max_rows,
                                                                (int)n_slots, topk, static_cast<const uint8_t*>(x),

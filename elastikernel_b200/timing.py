@@ -21,11 +21,16 @@ def flush_l2(device: torch.device | None = None) -> None:
     buf.zero_()
 
 
-def time_on_stream(fn, stream=None, reps: int | None = None, rep_ms: float = 50.0, flush: bool = True) -> dict:
+def time_on_stream(fn, stream=None, reps: int | None = None, rep_ms: float = 50.0, flush: bool = True,
+                   warmup: int = 0) -> dict:
     """Per-rep device time of fn() on `stream` (default: current stream).
 
     Each rep: flush L2 (untimed), record start, fn(), record end -- all on the
-    same stream. `reps` defaults to as many as fit in about rep_ms.
+    same stream. `reps` defaults to as many as fit in about rep_ms. `warmup`
+    untimed reps are queued right before the timed ones, with no host wait in
+    between: a GPU that idled while the host prepared the run (a synchronise,
+    a graph capture) brings its clock back up during them instead of during
+    the first timed rep.
     """
     stream = stream or torch.cuda.current_stream()
     with torch.cuda.stream(stream):
@@ -37,6 +42,10 @@ def time_on_stream(fn, stream=None, reps: int | None = None, rep_ms: float = 50.
             e.synchronize()
             one = max(s.elapsed_time(e), 1e-3)
             reps = int(max(5, min(200, rep_ms / one)))
+        for _ in range(warmup):
+            if flush:
+                flush_l2()
+            fn()
         pairs = []
         for _ in range(reps):
             if flush:

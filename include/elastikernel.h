@@ -240,6 +240,14 @@ int ek_moe_permute(const int* topk_ids, int T, int topk, int E, int block_m, int
                    int* block_expert, int* num_rows_padded, int* expert_counts, const void* x, int H,
                    int elem_bytes, void* x_perm, void* scratch, void* stream);
 
+/* ek_moe_route followed by ek_moe_permute, with the same outputs. Small
+ * batches (T*topk <= 128) run both, and the row gather while the rows are
+ * few, in one single-CTA launch (decode sizes are bound by launch latency);
+ * larger batches run the separate launches (scratch as for ek_moe_permute). */
+int ek_moe_route_permute(const float* logits, int T, int E, int topk, int* topk_ids, float* topk_weights,
+                         int block_m, int* sorted_slots, int* block_expert, int* num_rows_padded, int* expert_counts,
+                         const void* x, int H, int elem_bytes, void* x_perm, void* scratch, void* stream);
+
 /* Grouped gate/up GEMM with fused SiLU-and-multiply over the padded rows:
  *   act[r, n] = silu(x_perm[r] . w1[e, n]) * (x_perm[r] . w3[e, n]),
  * e = block_expert[r / block_m], for r < *num_rows_padded; w1, w3 are

@@ -76,6 +76,40 @@ def test_permute_bit_exact(cuda_dev, T, E, k):
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("T,E,k,block_m,H,dtype", [
+    (1, 8, 2, 1, 4096, torch.bfloat16),      # one launch, rows gathered in it
+    (16, 8, 2, 128, 4096, torch.bfloat16),   # one launch, 256 KB of rows gathered in it
+    (64, 8, 2, 1, 4096, torch.bfloat16),     # one launch, rows gathered by the wide gather
+    (16, 256, 8, 1, 7168, torch.uint8),      # 128 slots: the largest one-launch batch (e4m3 rows as bytes)
+    (3, 64, 6, 256, 0, None),                # no rows
+    (17, 256, 8, 1, 512, torch.bfloat16),    # 136 slots: the separate launches
+])
+def test_route_permute_matches_separate_launches(cuda_dev, T, E, k, block_m, H, dtype):
+    """ek_moe_route_permute against ek_moe_route + ek_moe_permute: every
+    output bit-identical, and the permutation against the oracle."""
+    from elastikernel_b200 import _ops
+
+    g = torch.Generator().manual_seed(T + 3 * E + k)
+    logits = torch.randn((T, E), generator=g).to(cuda_dev)
+    x = None
+    if dtype is not None:
+        x = (torch.randint(0, 255, (T, H), generator=g, dtype=torch.uint8) if dtype == torch.uint8
+             else torch.randn((T, H), generator=g).to(dtype)).to(cuda_dev)
+    ids, wts, perm = _ops.moe_route_permute(logits, k, E, x=x, block_m=block_m)
+    ids2, wts2 = _ops.moe_route(logits, k)
+    perm2 = _ops.moe_permute(ids2, E, x=x, block_m=block_m)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids2) and torch.equal(wts, wts2)
+    for key in ("sorted_slots", "block_expert", "num_rows_padded", "expert_counts"):
+        assert torch.equal(perm[key], perm2[key]), key
+    ref = om.permute_ref(ids.cpu().numpy(), E, block_m)
+    np.testing.assert_array_equal(perm["sorted_slots"].cpu().numpy(), ref["sorted_slots"])
+    if x is not None:
+        n = int(perm["num_rows_padded"].item())
+        used = perm["sorted_slots"][:n] < T * k  # padding rows are not gathered
+        assert torch.equal(perm["x_perm"][:n][used], perm2["x_perm"][:n][used])
+
+
 @pytest.mark.parametrize("T,k,H", [(4096, 8, 7168), (333, 2, 4096), (1, 1, 8), (64, 12, 520)])
 def test_combine_bit_exact(cuda_dev, T, k, H):
     """Top-k combine: fp32 sum in choice order, one bf16 rounding (k = 12
