@@ -49,7 +49,7 @@ class GemmPlan(ctypes.Structure):
         ("num_tiles", _c_int), ("num_dp_tiles", _c_int), ("tail_split", _c_int),
         ("num_units", _c_int), ("grid", _c_int), ("num_sms", _c_int), ("waves", _c_int),
         ("wave_efficiency", ctypes.c_double), ("est_us", ctypes.c_double),
-        ("workspace_bytes", _c_size),
+        ("workspace_bytes", _c_size), ("cluster_split", _c_int),
     ]
 
     def as_dict(self) -> dict:

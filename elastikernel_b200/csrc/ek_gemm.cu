@@ -11,7 +11,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
+#include "ek_gemm_csplit.cuh"
 #include "ek_gemm_kernel.cuh"
 #include "ek_internal.h"
 
@@ -47,6 +49,12 @@ struct Machine {
   double red_gbs_per_sm = 45;
   double red_fixed_us = 2.5;     // partial stores drained, ticket, barriers
   double launch_us = 2.0;        // fixed launch + prologue cost
+  // Cluster split: the first stage's latency is not hidden (every CTA runs
+  // one short slice), then two cluster barriers and a reduction that reads
+  // 128 x bn fp32 per CTA over distributed shared memory.
+  double csplit_fill_us = 1.0;
+  double csplit_fixed_us = 1.0;
+  double dsmem_gbs_per_sm = 120;
 };
 
 struct Candidate {
@@ -106,6 +114,82 @@ Candidate evaluate(int M, int N, int K, int S, int dtype, int pair, int bn, int 
   return best;
 }
 
+// Cluster split of every tile over cs CTAs (ek_gemm_csplit.cuh), one wave:
+// the busiest CTA streams its 1/cs of K, then the cluster reduces through
+// distributed shared memory. max_clusters: clusters of cs CTAs the device
+// holds at once (0: not offered).
+Candidate evaluate_csplit(int M, int N, int K, int dtype, int bn, int cs, int max_clusters) {
+  Machine mc;
+  Candidate c{0, bn, 1, 0, 0, 1e30, 0};
+  const int es = elem_bytes(dtype);
+  const int bk = 128 / es;
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int kb = (K + bk - 1) / bk;
+  if (max_clusters <= 0 || tiles > max_clusters || kb / cs < 2) return c;
+  const double flops_clk = dtype == EK_DTYPE_E4M3 ? mc.f8_flops_clk : mc.f16_flops_clk;
+  const double mma_clk = 128.0 * bn * bk * 2.0 / flops_clk;
+  const double feed_clk = (128.0 + double(bn)) * 128.0 / mc.feed_bytes_clk;
+  const double t_kb_us = std::max(mma_clk, feed_clk) / (mc.clk_ghz * 1e3);
+  const int slice_kb = (kb + cs - 1) / cs;
+  const double red_us = mc.csplit_fixed_us + 128.0 * bn * 4.0 / (mc.dsmem_gbs_per_sm * 1e3);
+  const double grid = double(tiles) * cs;
+  const double unique = (double(M) * K + double(K) * N) * es + double(M) * N * 2;
+  const double t_hbm = unique / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
+  c.est_us = std::max(slice_kb * t_kb_us + mc.csplit_fill_us, t_hbm) + red_us + mc.launch_us;
+  c.eff = double(kb) / (double(slice_kb) * cs);
+  return c;
+}
+
+// Clusters of cs CTAs (cs = 2, 4, 8) of the cluster-split kernel that the
+// current device holds at once, when num_sms is its full SM count; 0 when the
+// query is not possible (no device) or num_sms is a partition. Queried once
+// per device.
+int csplit_max_clusters(int num_sms, int cs) {
+  static std::mutex mu;
+  static int cached[64][3];
+  static int device_sms[64];
+  static bool done[64] = {false};
+  const int idx = cs == 2 ? 0 : cs == 4 ? 1 : cs == 8 ? 2 : -1;
+  if (idx < 0) return 0;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    using Cfg = GemmCfg<256, kBF16, false, kEpiStore, kSchedDense>;
+    const int smem = CsplitLayout<Cfg>::SMEM_BYTES;
+    int nsm = 0;
+    bool ok = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+              cudaFuncSetAttribute(gemm_csplit_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+                  cudaSuccess;
+    const int sizes[3] = {2, 4, 8};
+    for (int i = 0; i < 3; ++i) {
+      int n = 0;
+      if (ok) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(sizes[i] * 64, 1, 1);
+        cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = sizes[i];
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_csplit_kernel<Cfg>, &cfg) != cudaSuccess) n = 0;
+      }
+      cached[dev][i] = n;
+    }
+    (void)cudaGetLastError();
+    device_sms[dev] = nsm;
+    done[dev] = true;
+  }
+  return num_sms == device_sms[dev] ? cached[dev][idx] : 0;
+}
+
 }  // namespace
 
 static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layout, int force_bn, int force_split,
@@ -152,19 +236,59 @@ static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layo
   // pair modes first: on a near tie the 2-SM tile streams fewer bytes per SM
   static const Mode kModes[] = {{1, 256}, {1, 128}, {0, 256}, {0, 192}, {0, 128}, {0, 64}};
   Candidate best{0, 0, 1, 0, 0, 1e30, 0};
-  for (const Mode& m : kModes) {
-    // force_bn > 0: one CTA per 128 x force_bn tile; < 0: a CTA pair per 256 x -force_bn tile
-    if (force_bn > 0 && (m.pair || m.bn != force_bn)) continue;
-    if (force_bn < 0 && (!m.pair || m.bn != -force_bn)) continue;
-    if (m.pair && S < 2) continue;
-    Candidate c = evaluate(M, N, K, S, dtype, m.pair, m.bn, force_split);
-    if (c.est_us < best.est_us * 0.98) best = c;
+  if (force_split >= 0) {
+    for (const Mode& m : kModes) {
+      // force_bn > 0: one CTA per 128 x force_bn tile; < 0: a CTA pair per 256 x -force_bn tile
+      if (force_bn > 0 && (m.pair || m.bn != force_bn)) continue;
+      if (force_bn < 0 && (!m.pair || m.bn != -force_bn)) continue;
+      if (m.pair && S < 2) continue;
+      Candidate c = evaluate(M, N, K, S, dtype, m.pair, m.bn, force_split);
+      if (c.est_us < best.est_us * 0.98) best = c;
+    }
   }
-  if (best.bn == 0)
+  // The cluster split (fewer tiles than SMs): taken when its estimate beats
+  // the persistent schedule's by 2 %, or when force_split < 0 asks for it.
+  int best_cs = 0;
+  if (force_split <= 0 && force_bn >= 0) {
+    for (int cs : {2, 4, 8}) {
+      if (force_split < 0 && cs != -force_split) continue;
+      for (int bn : {256, 128}) {
+        if (force_bn > 0 && bn != force_bn) continue;
+        Candidate c = evaluate_csplit(M, N, K, dtype, bn, cs, csplit_max_clusters(S, cs));
+        if (c.est_us < best.est_us * 0.98 || (force_split < 0 && best_cs == 0 && c.est_us < 1e29)) {
+          best = c;
+          best_cs = cs;
+        }
+      }
+    }
+  }
+  if (best.bn == 0 || best.est_us >= 1e29)
     return set_error(EK_ERR_INVALID, "no tile width matches force_bn=%d force_split=%d", force_bn, force_split);
   const int es = elem_bytes(dtype);
-  const int ctas = best.pair ? 2 : 1;
   ek_gemm_plan p{};
+  if (best_cs > 0) {
+    p.bm = 128;
+    p.bn = best.bn;
+    p.bk = 128 / es;
+    p.cta_pair = 0;
+    p.tiles_m = (M + 127) / 128;
+    p.tiles_n = (N + best.bn - 1) / best.bn;
+    p.k_blocks = (K + p.bk - 1) / p.bk;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.tail_split = 1;
+    p.num_dp_tiles = p.num_tiles;
+    p.num_units = p.num_tiles * best_cs;
+    p.grid = p.num_units;
+    p.num_sms = S;
+    p.waves = 1;
+    p.wave_efficiency = best.eff;
+    p.est_us = best.est_us;
+    p.workspace_bytes = 0;
+    p.cluster_split = best_cs;
+    *out = p;
+    return EK_OK;
+  }
+  const int ctas = best.pair ? 2 : 1;
   p.bm = 128 * ctas;
   p.bn = best.bn;
   p.bk = 128 / es;
@@ -222,9 +346,46 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
   }
 }
 
+template <class Cfg>
+int launch_csplit(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid, int cs,
+                  cudaStream_t stream) {
+  constexpr int smem = CsplitLayout<Cfg>::SMEM_BYTES;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
+  if (!attr_done[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_csplit_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                        "cudaFuncSetAttribute(cluster split)");
+    if (rc) return rc;
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, gemm_csplit_kernel<Cfg>, ta, tb, prm), "cluster-split gemm launch");
+}
+
 template <int kElem, bool kBMN, int kEpi>
 int launch_mode(int pair, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid,
-                cudaStream_t stream) {
+                cudaStream_t stream, int cs = 0) {
+  if (cs > 1) {
+    if (cs != 2 && cs != 4 && cs != 8) return set_error(EK_ERR_INVALID, "cluster split of %d CTAs", cs);
+    switch (bn) {
+      case 128: return launch_csplit<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, cs, stream);
+      case 256: return launch_csplit<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, cs, stream);
+    }
+    return set_error(EK_ERR_UNSUPPORTED, "cluster split with bn=%d not built", bn);
+  }
   if (pair) {
     switch (bn) {
       case 128: return launch_cfg<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense, true>>(ta, tb, prm, grid, stream);
@@ -446,14 +607,17 @@ int launch_dense(const ek_gemm_plan& plan, const void* A, const void* B, void* C
     prm.ws_counters = static_cast<int*>(workspace);
     prm.ws_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kGemmTicketBytes);
   }
+  const int cs = plan.cluster_split;
   if (dtype == EK_DTYPE_E4M3)
-    return launch_mode<kE4M3, false, kEpiRowColScale>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
+    return launch_mode<kE4M3, false, kEpiRowColScale>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s, cs);
   if (dtype == EK_DTYPE_BF16) {
-    if (b_layout == EK_B_KN) return launch_mode<kBF16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
-    return launch_mode<kBF16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
+    if (b_layout == EK_B_KN)
+      return launch_mode<kBF16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s, cs);
+    return launch_mode<kBF16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s, cs);
   }
-  if (b_layout == EK_B_KN) return launch_mode<kFP16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
-  return launch_mode<kFP16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s);
+  if (b_layout == EK_B_KN)
+    return launch_mode<kFP16, true, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s, cs);
+  return launch_mode<kFP16, false, kEpiStore>(plan.cta_pair, plan.bn, ta, tb, prm, plan.grid, s, cs);
 }
 
 }  // namespace ek

@@ -128,7 +128,7 @@ int register_status_reader(status_reader_fn fn) {
 
 extern "C" {
 
-int ek_abi_version(void) { return 100; }
+int ek_abi_version(void) { return 101; }
 
 const char* ek_last_error(void) { return ek::t_last_error.c_str(); }
 

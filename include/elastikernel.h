@@ -123,12 +123,20 @@ typedef struct ek_gemm_plan {
   double wave_efficiency;  /* useful K-steps / (grid * K-steps of busiest CTA)   */
   double est_us;           /* model estimate of the kernel time                  */
   size_t workspace_bytes;  /* scratch the schedule needs (split partials)        */
+  int cluster_split;       /* > 1: K split over a thread-block cluster of this  */
+                           /* many CTAs per 128 x bn tile, reduced through      */
+                           /* distributed shared memory (no workspace); grid =  */
+                           /* num_tiles * cluster_split; 0 = persistent schedule */
 } ek_gemm_plan;
 
 /* Plan a GEMM C[M,N] = A[M,K] * B on num_sms SMs (num_sms > 0 required here).
  * force_bn pins the tile: > 0 one CTA per 128 x force_bn tile (64/128/192/256),
  * < 0 a CTA pair per 256 x -force_bn tile (128/256), 0 = choose.
- * force_split > 0 pins the tail split (0 = choose). */
+ * force_split > 0 pins the tail split of the persistent schedule, < 0 the
+ * cluster split (-force_split = 2, 4 or 8 CTAs per tile; bn 128 or 256),
+ * 0 = choose. The cluster split is offered on a device's full SM count only
+ * (cluster placement inside a green-context partition is not known) and
+ * when every cluster fits on the device at once. */
 int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,
                       ek_gemm_plan* out);
 

@@ -33,7 +33,7 @@ def test_library_loads_and_exports_header_symbols():
     missing = [s for s in syms if getattr(L, s, None) is None]
     assert not missing, f"symbols declared in the header but not exported: {missing}"
     assert set(syms) <= set(_lib.exported_symbols()), "binding table lacks header symbols"
-    assert L.ek_abi_version() == 100
+    assert L.ek_abi_version() == 101
 
 
 @pytest.fixture()
