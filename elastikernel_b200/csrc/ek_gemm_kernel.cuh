@@ -91,7 +91,7 @@ struct GemmCfg {
   // extra shared memory of the swapped schedule: expert prefixes, per-token
   // slots / weights, and the gate exchange of the SwiGLU epilogue
   static constexpr int EXTRA_BYTES =
-      kSwapped ? (2 * (kMaxExpertsT + 1) * 4 + BN * 8 + 64 * 33 * 4 + 127) / 128 * 128 : 0;
+      kSwapped ? (2 * (kMaxExpertsT + 1) * 4 + ((BN + 31) / 32 * 32) * 8 + 64 * 33 * 4 + 127) / 128 * 128 : 0;
   // kMx scale factors per stage: A (512 B: 128 rows x 4 K chunks) and B
   // (512 B per 128 tokens), and their TMEM columns (two buffers after the
   // two accumulators)
@@ -432,9 +432,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   volatile int* s_last = reinterpret_cast<volatile int*>(s_tmem_base + 2);
   volatile int* s_ksplit = reinterpret_cast<volatile int*>(s_tmem_base + 3);
   ExpertTables xt{reinterpret_cast<int*>(sX), reinterpret_cast<int*>(sX) + (kMaxExpertsT + 1)};
-  int* s_slot = reinterpret_cast<int*>(sX) + 2 * (kMaxExpertsT + 1);  // [BN]
-  float* s_wt = reinterpret_cast<float*>(s_slot + BN);                 // [BN]
-  float* s_xg = s_wt + BN;                                             // [64][33]
+  // per-token tables of the swapped epilogues, one entry per TMEM column the
+  // 32-column epilogue chunks read (BN rounded up to a whole chunk)
+  constexpr int BN_CH = (BN + 31) / 32 * 32;
+  int* s_slot = reinterpret_cast<int*>(sX) + 2 * (kMaxExpertsT + 1);  // [BN_CH]
+  float* s_wt = reinterpret_cast<float*>(s_slot + BN_CH);              // [BN_CH]
+  float* s_xg = s_wt + BN_CH;                                          // [64][33]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -837,7 +840,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const uint32_t aphase = (acc_i >> 1) & 1;
       if constexpr (Cfg::kEpi == kEpiScatterT) {
         // slot and routing weight of every token column of this unit
-        for (int t = epi_tid; t < BN; t += 128) {
+        for (int t = epi_tid; t < BN_CH; t += 128) {  // columns past the unit's tokens get slot -1
           const int tr = w.tok0 + t;
           int slot = -1;
           float wt = 0.f;
