@@ -391,7 +391,7 @@ def fp8_bench(dev, peak_bf16_tflops: float, steps: int) -> dict:
             "fp8_peak_tflops": peak_fp8, "peak_note": "2 x measured bf16 burst", "results": res}
 
 
-def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: int = 0) -> dict:
+def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: int = 0) -> dict:
     """DeepSeek-V3-shaped expert-parallel MoE: 256 experts, top-8 softmax
     routing, H=7168, I=2048, e4m3 experts with 128 x 128 block scales, 4096
     tokens per rank, 256/world experts per rank, e4m3 dispatch over NCCL
@@ -431,32 +431,45 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
         comm_stream, comm_sms = torch.cuda.Stream(dev), 0
     # fixed-capacity exchanges: equal all-to-all splits known to the host, so
     # nothing is read back between the routing and the combine
-    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto")
-    # Two chunks let the dispatch / combine of one half overlap the expert
-    # GEMMs of the other, but each chunk streams every local expert's weights
-    # again: worth it only where the experts are compute-bound, i.e. with
-    # ~1024+ tokens per local expert (8 GPUs: 4096 * 8 * 8 / 256 = 1024).
-    if chunks <= 0:
-        chunks = 2 if T * k * world // E >= 1024 else 1
+    # the equal-split exchanges go through an NCCL communicator driven on the
+    # communication partition's stream, so their kernels stay on its 32 SMs
+    stream_a2a = None
+    if world > 1:
+        from elastikernel_b200.nccl_stream import StreamAllToAll
 
-    def layer():
-        return moe(x, logits, chunks=chunks, compute_stream=gemm_stream, comm_stream=comm_stream)
-
+        stream_a2a = StreamAllToAll()
+    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto", stream_a2a=stream_a2a)
+    # Expert groups (N > 1): each rank's experts in 2 groups; a group's
+    # exchanges run on the 32-SM partition (NCCL driven on its stream) while
+    # another group's GEMMs run in the 116-SM partition, and every expert
+    # still streams its weights once. The ungrouped layer (routing, exchanges
+    # and the experts' 116-CTA GEMMs one after another on a full-device
+    # stream) is timed beside it.
+    if groups <= 0:
+        groups = 2 if world > 1 else 1
     main = torch.cuda.Stream(dev)
-    with torch.cuda.stream(main):
-        for _ in range(2):
-            layer()
-        torch.cuda.synchronize()
-        barrier(world)
-        reps = max(3, steps // 10)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(main)
-        for _ in range(reps):
-            out = layer()
-        e.record(main)
-        torch.cuda.synchronize()
-    ms = max_over_ranks(s.elapsed_time(e) / reps, world)
-    # phase split of one unchunked layer (device time between phase events on
+
+    def time_layer(gr):
+        def layer():
+            return moe(x, logits, groups=gr, compute_stream=gemm_stream, comm_stream=comm_stream)
+
+        with torch.cuda.stream(main):
+            for _ in range(2):
+                layer()
+            torch.cuda.synchronize()
+            barrier(world)
+            reps = max(3, steps // 10)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(main)
+            for _ in range(reps):
+                y = layer()
+            e.record(main)
+            torch.cuda.synchronize()
+        return max_over_ranks(s.elapsed_time(e) / reps, world), y
+
+    ms, out = time_layer(groups)
+    ms_ungrouped = time_layer(1)[0] if groups > 1 else ms
+    # phase split of one ungrouped layer (device time between phase events on
     # the experts' partition stream; NCCL inside the same timeline)
     barrier(world)
     with torch.cuda.stream(gemm_stream):
@@ -476,6 +489,9 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
                     & _lib.EK_STATUS_CAPACITY)
     overflow = bool(max_over_ranks(float(overflow), world))
     err, err_q = ep_parity(dev, x, logits, out, qw, E, k, world, rank)
+    if stream_a2a is not None:
+        barrier(world)
+        stream_a2a.close()
     flop = T * k * 6.0 * H * I
     tf = flop / (ms * 1e-3) / 1e12
     peak_fp8 = 2.0 * peak_bf16_tflops
@@ -484,7 +500,11 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, chunks: i
             "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
             "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms, "comm_partition_sms": comm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
-            "chunks": chunks, "phases_ms_unchunked": phases, "all_to_all": a2a,
+            "expert_groups": groups, "ms_per_layer_ungrouped": round(ms_ungrouped, 3),
+            "placement": ("experts in the 116-SM green context, exchanges on the 32-SM one, overlapped group by "
+                          "group" if groups > 1 else "routing, exchanges and the experts' 116-CTA GEMMs in turn on "
+                          "a full-device stream"),
+            "phases_ms_ungrouped": phases, "all_to_all": a2a,
             "ep_max_rel_err": err, "ep_parity_tol": 3e-2, "ep_max_rel_err_act_e4m3": err_q,
             "fp8_scales": "power-of-two, applied by the tensor cores (kind::mxf8f6f4.block_scale)" if FP8_POW2
             else "fp32, applied per 128-wide K block in the epilogue",
@@ -854,7 +874,8 @@ def summarize(line: dict) -> dict:
         sm["moe_ep"] = {"n_gpus": ep["n_gpus"], "ms": ep["ms_per_layer"], "tokens_per_s": ep["tokens_per_s"],
                         "pct_fp8_peak_scaled": ep["pct_fp8_peak_scaled"], "gemm_sms": ep["gemm_partition_sms"],
                         "ep_max_rel_err": [ep["ep_max_rel_err"], ep.get("ep_max_rel_err_act_e4m3")],
-                        "phases_ms": ep["phases_ms_unchunked"],
+                        "expert_groups": ep["expert_groups"], "ms_ungrouped": ep.get("ms_per_layer_ungrouped"),
+                        "phases_ms_ungrouped": ep["phases_ms_ungrouped"],
                         "a2a_gbs": [ep["all_to_all"].get("dispatch_gbs_per_rank"),
                                     ep["all_to_all"].get("combine_gbs_per_rank")]}
     tr = line.get("triton_reference")

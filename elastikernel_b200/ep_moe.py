@@ -220,7 +220,7 @@ class ExpertParallelMoE:
     are dispatched as e4m3 with 1 x 128 scales (half the bytes of bf16)."""
 
     def __init__(self, num_experts: int, topk: int, w1=None, w2=None, w3=None, group=None, ops=None, qw=None,
-                 capacity=None):
+                 capacity=None, stream_a2a=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -239,17 +239,23 @@ class ExpertParallelMoE:
         if capacity is not None and capacity != "auto" and int(capacity) < 0:
             raise ValueError("capacity must be None, 'auto' or a row count >= 0")
         self.capacity = capacity  # None: exact exchanges (host read of the counts)
+        # nccl_stream.StreamAllToAll: equal-split exchanges launched on the
+        # current stream (e.g. a communication partition's) instead of the
+        # process group's internal one
+        self.stream_a2a = stream_a2a
 
-    def capacity_rows(self, n_slots: int) -> int:
-        """Rows per destination rank of a fixed-capacity exchange of n_slots
-        slots: the given count, or for "auto" the mean of a uniform routing
-        plus 6 standard deviations of a destination's (binomial) count, plus
-        16, rounded up to 16 (one rank: exactly n_slots). Every rank must use
-        the same value, so with "auto" every rank passes the same number of
+    def capacity_rows(self, n_slots: int, groups: int = 1) -> int:
+        """Rows per destination of a fixed-capacity exchange of n_slots slots,
+        the destinations being the ranks (groups = 1) or the (expert group,
+        rank) pairs of a grouped layer: the given count (split evenly over the
+        groups), or for "auto" the mean of a uniform routing plus 6 standard
+        deviations of a destination's (binomial) count, plus 16, rounded up
+        to 16 (a single destination: exactly n_slots). Every rank must use the
+        same value, so with "auto" every rank passes the same number of
         tokens."""
         if self.capacity != "auto":
-            return int(self.capacity)
-        G = self.world
+            return -(-int(self.capacity) // groups)
+        G = self.world * groups
         if G == 1:
             return n_slots
         m = n_slots / G
@@ -267,6 +273,8 @@ class ExpertParallelMoE:
         if self.world == 1:
             out.copy_(inp)
             return out
+        if self.stream_a2a is not None and out_splits is None and in_splits is None and out.is_cuda:
+            return self.stream_a2a.all_to_all(out, inp)
         dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
                                group=self.group)
         return out
@@ -349,6 +357,138 @@ class ExpertParallelMoE:
         self._mark("dispatch")
         return x_recv, ids_recv, w_recv, Dispatched(T, self.topk, None, None, cap["slot_row"], capacity=C)
 
+    # ---------------------------------------------------------------- expert groups
+    def _dispatch_groups(self, x, gate_logits, groups: int):
+        """Routing and the fixed-capacity send layout of a grouped layer. The
+        local experts of every rank are split into `groups` contiguous groups;
+        the slots are laid out by (group, destination rank), group-major, so
+        group g's rows for all ranks are one block of world * Cg rows that one
+        equal-split all-to-all moves. Done by renaming expert l of rank r to
+        g * (world * eg) + r * eg + l % eg (g = l // eg, eg experts per
+        group) and laying out by "rank" = id // eg over world * groups
+        destinations: the local ids that arrive are l % eg, the expert's index
+        inside its group. Returns the send tensors (rows, scales or None,
+        local ids, weights), the slots' layout rows and Cg."""
+        ops = self.ops
+        T = x.shape[0]
+        n = T * self.topk
+        W, epr = self.world, self.experts_per_rank
+        eg = epr // groups
+        Cg = self.capacity_rows(n, groups)
+        ids, wts = ops.route(gate_logits, self.topk)
+        r = torch.div(ids, epr, rounding_mode="floor")
+        loc = ids - r * epr
+        g = torch.div(loc, eg, rounding_mode="floor")
+        vids = (g * (W * eg) + r * eg + (loc - g * eg)).to(ids.dtype).contiguous()
+        xs = None
+        if self.fp8:
+            x, xs = (ops.quant_rows(x, pow2=True) if self.qw.get("pow2") else ops.quant_rows(x))
+        perm = ops.permute_by_dest(ops.dest_of(vids, eg), W * groups, None)
+        cap = ops.capacity_layout(perm, vids, wts, eg, W * groups, Cg)
+        x_send = ops.gather_capacity(cap, x)
+        xs_send = ops.gather_capacity(cap, xs) if self.fp8 else None
+        return (x_send, xs_send, cap["local_ids"], cap["weights"]), cap["slot_row"], Cg
+
+    def _exchange_group(self, send, g: int, rows_g: int):
+        """All-to-all of group g's block of the send layout (equal splits)."""
+        sl = slice(g * rows_g, (g + 1) * rows_g)
+        x_send, xs_send, ids_send, w_send = send
+        xb = x_send[sl]
+        x_recv = torch.empty_like(xb)
+        if self.fp8:  # byte view: the exchange does not need to know the float8 type
+            self._a2a(x_recv.view(torch.uint8), xb.view(torch.uint8), None, None)
+            xs_recv = torch.empty_like(xs_send[sl])
+            self._a2a(xs_recv, xs_send[sl], None, None)
+            x_recv = (x_recv, xs_recv)
+        else:
+            self._a2a(x_recv, xb, None, None)
+        ids_recv = torch.empty_like(ids_send[sl])
+        self._a2a(ids_recv, ids_send[sl], None, None)
+        w_recv = torch.empty_like(w_send[sl])
+        self._a2a(w_recv, w_send[sl], None, None)
+        return x_recv, ids_recv, w_recv
+
+    def _group_weights(self, a: int, b: int):
+        """The weights of local experts [a, b): views, e4m3 codes with their
+        128 x 128 block scales (rows of the scale grids), or bf16 tensors."""
+        if not self.fp8:
+            return self.w1[a:b], self.w2[a:b], self.w3[a:b]
+        q = dict(self.qw)
+        for name, rows in (("w1", q["I"]), ("w3", q["I"]), ("w2", q["H"])):
+            q[name + "q"] = self.qw[name + "q"][a:b]
+            q[name + "s"] = self.qw[name + "s"][a * (rows // 128):b * (rows // 128)]
+        q["E"] = b - a
+        return q
+
+    def _group_experts(self, recv, a: int, b: int):
+        x_recv, ids_recv, w_recv = recv
+        if self.fp8:
+            return self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self._group_weights(a, b),
+                                        dummy=True)
+        return self.ops.experts(x_recv, ids_recv, w_recv, *self._group_weights(a, b), dummy=True)
+
+    def _forward_groups(self, x, gate_logits, groups: int, compute=None, comm=None):
+        """The layer with the local experts in `groups` groups. With CUDA
+        streams the routing and every exchange run on `comm`, the expert
+        GEMMs on `compute`: group g+1's rows travel while group g computes,
+        and group g's results travel back while group g+1 computes. Each
+        expert still sees all its rows in one GEMM, so no weight is streamed
+        twice (token chunks would stream every expert's weights once per
+        chunk). Without streams the same steps run in order."""
+        import contextlib
+
+        piped = x.is_cuda and compute is not None and comm is not None
+        on = (lambda st: torch.cuda.stream(st)) if piped else (lambda st: contextlib.nullcontext())
+        T = x.shape[0]
+        eg = self.experts_per_rank // groups
+        # routing and the send layout on the caller's stream (nothing else runs
+        # yet, so they get every SM the caller's stream has)
+        send, slot_row, Cg = self._dispatch_groups(x, gate_logits, groups)
+        rows_g = self.world * Cg
+        if piped:
+            cur = torch.cuda.current_stream(x.device)
+            comm.wait_stream(cur)
+            compute.wait_stream(cur)
+            for t in send:
+                if t is not None:
+                    t.record_stream(comm)  # made on the caller's stream, sent from the comm stream
+        with on(comm):
+            recvs = []
+            for g in range(groups):
+                recv = self._exchange_group(send, g, rows_g)
+                ev = None
+                if piped:
+                    ev = torch.cuda.Event()
+                    ev.record(comm)
+                recvs.append((recv, ev))
+        ys = []
+        for g, (recv, ev) in enumerate(recvs):
+            with on(compute):
+                if piped:
+                    compute.wait_event(ev)
+                    xr, ids_r, w_r = recv
+                    for t in (xr if isinstance(xr, tuple) else (xr,)) + (ids_r, w_r):
+                        t.record_stream(compute)  # made on the comm stream, read here
+                y = self._group_experts(recv, g * eg, (g + 1) * eg)
+                ev_y = None
+                if piped:
+                    ev_y = torch.cuda.Event()
+                    ev_y.record(compute)
+                ys.append((y, ev_y))
+        with on(comm):
+            y0 = ys[0][0]
+            y_back = torch.empty((groups * rows_g, y0.shape[1]), dtype=y0.dtype, device=y0.device)
+            for g, (y, ev_y) in enumerate(ys):
+                if piped:
+                    comm.wait_event(ev_y)
+                    y.record_stream(comm)  # made on the compute stream, sent from here
+                self._a2a(y_back[g * rows_g:(g + 1) * rows_g], y, None, None)
+        if piped:
+            cur.wait_stream(comm)
+            y_back.record_stream(cur)  # made on the comm stream, read here
+        # each token's k rows summed on the caller's stream, every SM again
+        return self.ops.combine_rows(y_back, slot_row, T, self.topk)
+
     def combine(self, y_local, d: Dispatched):
         n = d.T * d.topk
         self._mark("experts")
@@ -396,8 +536,13 @@ class ExpertParallelMoE:
             return self.ops.experts_fp8(x_recv[0], x_recv[1], ids_recv, w_recv, self.qw, **kw)
         return self.ops.experts(x_recv, ids_recv, w_recv, self.w1, self.w2, self.w3, **kw)
 
-    def forward(self, x, gate_logits, chunks: int = 1, compute_stream=None, comm_stream=None):
+    def forward(self, x, gate_logits, chunks: int = 1, compute_stream=None, comm_stream=None, groups: int = 1):
         """The layer for this rank's tokens x [T, H] (router logits [T, E]).
+
+        groups > 1 (fixed-capacity exchanges only; a divisor of the experts
+        per rank) splits each rank's experts into that many groups and
+        pipelines the exchanges of one group with the expert GEMMs of another
+        (_forward_groups); every rank must use the same value.
 
         chunks > 1 splits the tokens into that many contiguous chunks and
         pipelines them: with CUDA streams given (the expert GEMMs on
@@ -409,6 +554,13 @@ class ExpertParallelMoE:
         unchunked layer: every token's rows are computed and summed the same
         way whichever chunk carries them."""
         T = x.shape[0]
+        groups = int(groups)
+        if groups > 1:
+            if self.capacity is None:
+                raise ValueError("expert groups need fixed-capacity exchanges (capacity='auto' or a row count)")
+            if self.experts_per_rank % groups != 0:
+                raise ValueError(f"{groups} groups do not split {self.experts_per_rank} experts per rank")
+            return self._forward_groups(x, gate_logits, groups, compute_stream, comm_stream)
         chunks = max(1, min(int(chunks), T))
         if chunks == 1:
             x_recv, ids_recv, w_recv, d = self.dispatch(x, gate_logits)

@@ -51,7 +51,8 @@ def test_summary_is_compact_and_complete():
                                             for t in (1, 16, 128, 1024, 4096)]}}
     ep = {"n_gpus": 8, "ms_per_layer": 5.9, "tokens_per_s": 5.5e6, "pct_fp8_peak_scaled": 19.4,
           "gemm_partition_sms": 116, "ep_max_rel_err": 0.011, "ep_max_rel_err_act_e4m3": 0.004,
-          "phases_ms_unchunked": {k: 0.123 for k in ("route_permute", "count_exchange", "dispatch", "experts",
+          "expert_groups": 4,
+          "phases_ms_ungrouped": {k: 0.123 for k in ("route_permute", "count_exchange", "dispatch", "experts",
                                                     "combine_exchange", "final_combine")},
           "all_to_all": {"dispatch_gbs_per_rank": 300.1, "combine_gbs_per_rank": 310.2}}
     line = {"value": 1331.57, "roofline": {"frac": 0.798}, "e2e": {"value": 101.0}, "clocks": {"sm_mhz": 1965.0},

@@ -132,7 +132,8 @@ def _worker(rank, world, port, q, mode):
         eg = E // world
         sl = slice(rank * eg, (rank + 1) * eg)
         ops = CpuEPOps()
-        capacity = {"capacity": "auto", "capacity_small": 3}.get(mode)
+        groups = int(mode[6:]) if mode.startswith("groups") else 1
+        capacity = "auto" if groups > 1 else {"capacity": "auto", "capacity_small": 3}.get(mode)
         moe = ExpertParallelMoE(E, K_TOP, w1[sl], w2[sl], w3[sl], ops=ops, capacity=capacity)
         g = torch.Generator().manual_seed(100 + rank)
         # ragged token counts per rank (a fixed capacity needs the same count everywhere)
@@ -147,7 +148,13 @@ def _worker(rank, world, port, q, mode):
                 q.join_thread()  # the message must reach the parent before the hard exit
                 os._exit(0)  # leaves between steps, without cleanup
         # "chunked": the tokens go through in 3 chunks (ragged: T is not a multiple of 3)
-        out = moe(x, logits, chunks=3) if mode == "chunked" else moe(x, logits)
+        # "groupsN": each rank's experts in N groups, exchanged group by group
+        if mode == "chunked":
+            out = moe(x, logits, chunks=3)
+        elif groups > 1:
+            out = moe(x, logits, groups=groups)
+        else:
+            out = moe(x, logits)
         ref = om.moe_ref(x.numpy(), logits.numpy(), w1, w2, w3, K_TOP)
         if mode == "capacity_small":
             # the slots this rank dropped belong to its own tokens; the others must be exact
@@ -182,7 +189,7 @@ def _run(world, mode):
 
 
 @pytest.mark.parametrize("world,mode", [(2, "normal"), (4, "normal"), (2, "chunked"), (2, "capacity"),
-                                        (4, "capacity")])
+                                        (4, "capacity"), (2, "groups2"), (2, "groups4"), (4, "groups2")])
 def test_ep_matches_single_process_oracle(world, mode):
     res = _run(world, mode)
     for rank, err in res.items():

@@ -132,6 +132,32 @@ def test_ep_world1_chunked_streams(cuda_dev, fp8):
     assert max_rel_err(out, ref.float().cpu().numpy()) <= 1e-3
 
 
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("groups", [2, 4])
+def test_ep_world1_expert_groups_streams(cuda_dev, fp8, groups):
+    """Expert groups pipelined over two green-context partitions (each group's
+    exchange on the small one, its GEMMs on the large one) give the layer of
+    the ungrouped forward, to fp32-sum-order tolerance (the groups run the same
+    per-row math on the same rows)."""
+    from elastikernel_b200 import _ops
+    from elastikernel_b200.ep_moe import CudaEPOps, ExpertParallelMoE
+    from elastikernel_b200.green_ctx import create_disjoint_partitions
+
+    w1, w2, w3 = _weights(cuda_dev)
+    (comm, _), (comp, comp_sms) = create_disjoint_partitions(cuda_dev, [32, 112])
+    kw = ({"qw": _ops.quant_moe_weights_fp8(w1, w2, w3, pow2=True)} if fp8
+          else {"w1": w1, "w2": w2, "w3": w3})
+    moe = ExpertParallelMoE(E, K_TOP, ops=CudaEPOps(num_sms=comp_sms), capacity="auto", **kw)
+    x, logits = _tokens(cuda_dev, 0, 333)
+    ref = moe(x, logits)
+    out = moe(x, logits, groups=groups, compute_stream=comp, comm_stream=comm)
+    out_seq = moe(x, logits, groups=groups)  # the same steps on one stream
+    torch.cuda.synchronize()
+    assert out.shape == ref.shape
+    assert max_rel_err(out, ref.float().cpu().numpy()) <= 1e-3
+    assert torch.equal(out, out_seq)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -177,6 +203,35 @@ def _worker(rank, world, port, q):
                                                                      comm_stream=comm)
         refc = _ops.fused_moe_fp8(xc, lc, qw_all, K_TOP)
         err_fp8 = max(err_fp8, max_rel_err(outc, refc.float().cpu().numpy()))
+        # expert groups: each group's rows and results cross NVLink while another group computes
+        outg = ExpertParallelMoE(E, K_TOP, qw=qw, capacity="auto")(xc, lc, groups=2, compute_stream=comp,
+                                                                     comm_stream=comm)
+        err_fp8 = max(err_fp8, max_rel_err(outg, refc.float().cpu().numpy()))
+        # the equal-split exchanges on a communication partition's own stream
+        # (an NCCL communicator driven directly): the same bytes as
+        # all_to_all_single, and the same grouped layer
+        from elastikernel_b200.green_ctx import create_disjoint_partitions
+        from elastikernel_b200.nccl_stream import StreamAllToAll
+
+        (p_comm, _), (p_comp, p_sms) = create_disjoint_partitions(dev, [32], with_remainder=True)
+        sa = StreamAllToAll()
+        inp = torch.randn(world * 4099, device=dev)
+        want = torch.empty_like(inp)
+        dist.all_to_all_single(want, inp)
+        got = torch.empty_like(inp)
+        with torch.cuda.stream(p_comm):
+            sa.all_to_all(got, inp)
+        p_comm.synchronize()
+        if not torch.equal(got, want):
+            raise AssertionError("StreamAllToAll differs from all_to_all_single")
+        from elastikernel_b200.ep_moe import CudaEPOps
+
+        outs = ExpertParallelMoE(E, K_TOP, qw=qw, capacity="auto", ops=CudaEPOps(num_sms=p_sms), stream_a2a=sa)(
+            xc, lc, groups=2, compute_stream=p_comp, comm_stream=p_comm)
+        err_fp8 = max(err_fp8, max_rel_err(outs, refc.float().cpu().numpy()))
+        torch.cuda.synchronize()
+        dist.barrier()
+        sa.close()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
