@@ -51,6 +51,7 @@ struct Fp8BsCfg {
   static constexpr bool kPair = kPair_;
   static constexpr int CTAS = kPair ? 2 : 1;
   static constexpr int BM = 128;
+  static constexpr int WROWS = 128;  // weight rows per CTA (one MMA row block)
   static constexpr int TILE_M = 128 * CTAS;
   static constexpr int BN = BN_;
   static constexpr int BN_CTA = BN_ / CTAS;

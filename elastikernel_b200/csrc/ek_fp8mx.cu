@@ -59,8 +59,19 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx, 
 }
 
 template <int kEpi>
-int launch_tok(int tok, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx,
+int launch_tok(int tok, bool pair, bool wide, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx,
                const GemmParams& p, int grid, cudaStream_t s) {
+  if (pair && wide) {
+    switch (tok) {
+      case 128:
+        return launch<GemmCfg<128, kE4M3, false, kEpi, kSchedExperts, true, true, true>>(ta, tb, tx, p, grid, s);
+      case 160:
+        return launch<GemmCfg<160, kE4M3, false, kEpi, kSchedExperts, true, true, true>>(ta, tb, tx, p, grid, s);
+      case 192:
+        return launch<GemmCfg<192, kE4M3, false, kEpi, kSchedExperts, true, true, true>>(ta, tb, tx, p, grid, s);
+    }
+    return set_error(EK_ERR_INVALID, "fp8 mx wide pair token tile must be 128, 160 or 192 (got %d)", tok);
+  }
   if (pair) {
     switch (tok) {
       case 128: return launch<GemmCfg<128, kE4M3, false, kEpi, kSchedExperts, true, true>>(ta, tb, tx, p, grid, s);
@@ -103,6 +114,25 @@ void tiles(long long rows, int E, int S, int force_tok, int force_pair, bool pai
   *pair = pr;
 }
 
+// Wide weight tiles (256 rows per CTA of a pair, GemmCfg kWideA): force 2
+// = wide, 1 = normal pair, otherwise chosen where they measured faster: the
+// gate/up GEMM (`auto_ok`; 56 K blocks per unit at H = 7168 amortise the
+// epilogue that the single TMEM buffer no longer hides) from ~192 routed rows
+// per expert (DeepSeek-V3 shapes, 116-148 SMs: 256 rows 2015 -> 1844 us,
+// 1024 rows 1621 -> 1415 us; at 128 rows 2085 -> 2363 us), and only while the
+// wide schedule still has a unit for every SM. The down projection (16 K
+// blocks per unit) measured slower wide at every load.
+bool wide_tiles(long long rows, int E, int S, int tok, int pair, int force, int wrows_per_expert, int rows_per_pair,
+                bool auto_ok) {
+  if (!pair || wrows_per_expert % rows_per_pair != 0) return false;
+  if (force == 2) return true;
+  if (force == 1 || !auto_ok) return false;
+  const long long used = std::max<long long>(1, std::min<long long>(E, rows));
+  if (rows < 192 * used) return false;
+  const long long tiles = std::max<long long>(used, (rows + tok - 1) / tok);
+  return tiles * (wrows_per_expert / rows_per_pair) >= S;
+}
+
 }  // namespace
 }  // namespace ek
 
@@ -125,19 +155,22 @@ int ek_moe_gate_up_fp8mx(const void* xq, const float* x_scale, const void* w1q, 
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   int t = 0, pr = 0;
-  tiles(rows, E, S, tok, pair, true, &t, &pr);
+  tiles(rows, E, S, tok, pair == 2 ? 1 : pair, true, &t, &pr);
   const int ctas = pr ? 2 : 1;
+  // features per CTA: 64 ([64 w1 | 64 w3] rows), or 128 with wide tiles
+  const bool wide = wide_tiles(rows, E, S, t, pr, pair, I, 256, true);
+  const int fpc = wide ? 128 : 64;
   CUtensorMap ta, tx, tb;
-  if ((rc = make_tmap_2d(&ta, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
-  if ((rc = make_tmap_2d(&tx, w3q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, 64))) return rc;
+  if ((rc = make_tmap_2d(&ta, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, fpc))) return rc;
+  if ((rc = make_tmap_2d(&tx, w3q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, H, 128, fpc))) return rc;
   if ((rc = make_tmap_2d(&tb, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, rows, H, 128, t / ctas))) return rc;
   uint64_t plane = 0;
   bool planes = false;
   CUtensorMap t3;
   if (plane_stride(w1q, w3q, (uint64_t)E * I * H, &plane)) {
     // w3q lies a fixed distance after w1q (e.g. two planes of one buffer): one
-    // 3-D box loads a unit's [64 w1 | 64 w3] weight rows
-    if (make_tmap_3d(&t3, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, 2, H, plane, 128, 64, 2) == EK_OK)
+    // 3-D box loads a unit's [fpc w1 | fpc w3] weight rows
+    if (make_tmap_3d(&t3, w1q, CU_TENSOR_MAP_DATA_TYPE_UINT8, H, (uint64_t)E * I, 2, H, plane, 128, fpc, 2) == EK_OK)
       planes = true;
     else
       clear_error();
@@ -152,7 +185,7 @@ int ek_moe_gate_up_fp8mx(const void* xq, const float* x_scale, const void* w1q, 
   p.num_experts = E;
   p.expert_counts = expert_counts;
   p.w_rows_per_expert = I;
-  p.feat_tiles = I / (64 * ctas);
+  p.feat_tiles = I / (fpc * ctas);
   p.sf_tok = x_scale;
   p.sf_w = w1_scale;
   p.sf_w2 = w3_scale;
@@ -162,7 +195,7 @@ int ek_moe_gate_up_fp8mx(const void* xq, const float* x_scale, const void* w1q, 
     p.a_planes = 1;
   }
   const int grid = std::max(1, S / ctas) * ctas;
-  return launch_tok<kEpiSwiGLUT>(t, pr != 0, ta, tb, tx, p, grid, static_cast<cudaStream_t>(stream));
+  return launch_tok<kEpiSwiGLUT>(t, pr != 0, wide, ta, tb, tx, p, grid, static_cast<cudaStream_t>(stream));
 }
 
 int ek_moe_down_fp8mx(const void* aq, const float* a_scale, const void* w2q, const float* w2_scale,
@@ -181,10 +214,13 @@ int ek_moe_down_fp8mx(const void* aq, const float* a_scale, const void* w2q, con
   if (rc) return rc;
   // a pair tile covers 256 output features, so H must divide into them
   int t = 0, pr = 0;
-  tiles(rows, E, S, tok, pair, H % 256 == 0, &t, &pr);
+  tiles(rows, E, S, tok, pair == 2 ? 1 : pair, H % 256 == 0, &t, &pr);
   const int ctas = pr ? 2 : 1;
+  // output features per CTA: 128, or 256 with wide tiles
+  const bool wide = wide_tiles(rows, E, S, t, pr, pair, H, 512, false);
+  const int fpc = wide ? 256 : 128;
   CUtensorMap ta, tb;
-  if ((rc = make_tmap_2d(&ta, w2q, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, (uint64_t)E * H, I, 128, 128))) return rc;
+  if ((rc = make_tmap_2d(&ta, w2q, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, (uint64_t)E * H, I, 128, fpc))) return rc;
   if ((rc = make_tmap_2d(&tb, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, I, rows, I, 128, t / ctas))) return rc;
   GemmParams p{};
   p.M = rows;
@@ -196,7 +232,7 @@ int ek_moe_down_fp8mx(const void* aq, const float* a_scale, const void* w2q, con
   p.num_experts = E;
   p.expert_counts = expert_counts;
   p.w_rows_per_expert = H;
-  p.feat_tiles = H / (128 * ctas);
+  p.feat_tiles = H / (fpc * ctas);
   p.sorted_slots = sorted_slots;
   p.slot_weights = topk_weights;
   p.num_slots = T * topk;
@@ -205,7 +241,7 @@ int ek_moe_down_fp8mx(const void* aq, const float* a_scale, const void* w2q, con
   p.sf_w2 = w2_scale;
   p.sf_ksb = I / 128;
   const int grid = std::max(1, S / ctas) * ctas;
-  return launch_tok<kEpiScatterT>(t, pr != 0, ta, tb, ta, p, grid, static_cast<cudaStream_t>(stream));
+  return launch_tok<kEpiScatterT>(t, pr != 0, wide, ta, tb, ta, p, grid, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -66,12 +66,20 @@ constexpr int kMaxExpertsT = 256;  // experts per launch of the swapped schedule
 // split's "part written" flags ints [1024, 2048).
 constexpr int kGemmFlagOffset = 1024;
 
-template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false, bool kMx_ = false>
+template <int BN_, int kElem_, bool kBMN_, int kEpi_, int kSched_, bool kPair_ = false, bool kMx_ = false,
+          bool kWideA_ = false>
 struct GemmCfg {
   static constexpr bool kPair = kPair_;
   static constexpr bool kMx = kMx_;  // block-scaled e4m3 (UE8M0 scale factors applied by the MMA)
+  // kWideA (block-scaled swapped pair tiles): 256 weight rows per CTA, two
+  // MMAs per K step sharing the stage's token rows, two accumulators in one
+  // TMEM buffer. Each token row loaded then meets twice the weight rows, so
+  // the token tile is re-read half as often per weight byte streamed.
+  static constexpr bool kWideA = kWideA_;
   static constexpr int CTAS = kPair ? 2 : 1;
-  static constexpr int BM = 128;                 // rows per CTA
+  static constexpr int BM = 128;                 // rows per CTA (per MMA)
+  static constexpr int A_HALVES = kWideA ? 2 : 1;
+  static constexpr int WROWS = BM * A_HALVES;    // weight rows per CTA (kWideA: two MMA row blocks)
   static constexpr int TILE_M = BM * CTAS;       // rows per work unit
   static constexpr int BN = BN_;                 // columns per work unit
   static constexpr int BN_CTA = BN / CTAS;       // B rows (K-major) / columns (MN-major) loaded per CTA
@@ -84,7 +92,7 @@ struct GemmCfg {
   static constexpr int ES = kF8 ? 1 : 2;   // bytes per element
   static constexpr int BK = 128 / ES;      // one 128-byte swizzle row of K
   static constexpr int UK = 32 / ES;       // K of one MMA instruction
-  static constexpr int A_BYTES = BM * 128;
+  static constexpr int A_BYTES = WROWS * 128;
   static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES * CTAS;  // bytes that complete one stage of the pair
@@ -96,14 +104,16 @@ struct GemmCfg {
   // (512 B per 128 tokens), and their TMEM columns (two buffers after the
   // two accumulators)
   static constexpr int SF_NB = (BN + 127) / 128;
-  static constexpr int SF_BYTES = kMx ? 512 * (1 + SF_NB) : 0;
-  static constexpr int SF_COLS = 4 + 4 * SF_NB;
+  static constexpr int SF_BYTES = kMx ? 512 * (A_HALVES + SF_NB) : 0;
+  static constexpr int SF_COLS = 4 * A_HALVES + 4 * SF_NB;
   static constexpr int SF_AHEAD = 6;  // K blocks of scale loads in flight ahead of the slot writes
   static constexpr int SF_RELAY = 3;  // stages per cluster-scope release of the pair's relay warp
   static constexpr int MX_PREFETCH = 16;  // kMx: K blocks of weight tiles prefetched into L2 ahead of the loads
   static constexpr int SMEM_BUDGET = 220 * 1024 - EXTRA_BYTES;
   static constexpr int STAGES_FIT = SMEM_BUDGET / (STAGE_BYTES + SF_BYTES);
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
+  // two accumulator buffers of BN columns, or (kWideA) one buffer of two
+  // accumulators, then two scale-factor buffers
   static constexpr int TMEM_NEED = 2 * BN + (kMx ? 2 * SF_COLS : 0);
   static constexpr int TMEM_COLS = (TMEM_NEED <= 32) ? 32 : (TMEM_NEED <= 64) ? 64 : (TMEM_NEED <= 128) ? 128
                                  : (TMEM_NEED <= 256) ? 256 : 512;
@@ -130,6 +140,7 @@ struct GemmCfg {
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(!kMx || (kF8 && kSwapped && TMEM_NEED <= 512), "block scaling: e4m3 swapped tiles up to 192 tokens");
   static_assert(!kMx || SF_RELAY <= STAGES, "relay batch within the stage ring");
+  static_assert(!kWideA || (kMx && kPair), "wide weight tiles: block-scaled CTA-pair swapped tiles");
 };
 
 struct GemmParams {
@@ -332,11 +343,13 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int rows
     w.b_row = w.tok0 + rank * (w.n_eff / Cfg::CTAS);
     w.b_col = 0;
     if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
-      // 64 features per CTA: rows [64 of w1 | 64 of w3]
-      w.c_col = f * 64 * Cfg::CTAS + rank * 64;
+      // 64 features per CTA: rows [64 of w1 | 64 of w3]; kWideA: 128
+      // features, rows [128 of w1 | 128 of w3]
+      constexpr int FPC = Cfg::WROWS / 2;  // features per CTA
+      w.c_col = f * FPC * Cfg::CTAS + rank * FPC;
       w.a_row = e * p.w_rows_per_expert + w.c_col;
     } else {
-      w.c_col = f * Cfg::TILE_M + rank * Cfg::BM;
+      w.c_col = f * Cfg::WROWS * Cfg::CTAS + rank * Cfg::WROWS;
       w.a_row = e * p.w_rows_per_expert + w.c_col;
     }
   }
@@ -558,7 +571,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                 tma_load_3d_pair(a_dst, &tmA, fb, kb * BK, w.a_row, 0);
               } else {
                 tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
-                tma_load_2d_pair(a_dst + 64 * 128, &tmX, fb, kb * BK, w.a_row);
+                tma_load_2d_pair(a_dst + (Cfg::WROWS / 2) * 128, &tmX, fb, kb * BK, w.a_row);
               }
             } else {
               tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, w.a_row);
@@ -584,7 +597,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                 tma_load_3d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row, 0);
               } else {
                 tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
-                tma_load_2d(a_dst + 64 * 128, &tmX, &full_bar[stage], kb * BK, w.a_row);
+                tma_load_2d(a_dst + (Cfg::WROWS / 2) * 128, &tmX, &full_bar[stage], kb * BK, w.a_row);
               }
             } else {
               tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * BK, w.a_row);
@@ -624,8 +637,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       for (int u = unit0; u < nunits && ok; u += unit_step) {
         const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
         if (!w.valid) continue;
-        const int buf = acc_i & 1;
-        const uint32_t aphase = (acc_i >> 1) & 1;
+        // kWideA: one buffer holding both accumulators (columns [0, BN) and [BN, 2 BN))
+        const int buf = Cfg::kWideA ? 0 : (acc_i & 1);
+        const uint32_t aphase = Cfg::kWideA ? (acc_i & 1) : ((acc_i >> 1) & 1);
         if (!mbar_wait(&tempty_bar[buf], aphase ^ 1, s_abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
@@ -641,19 +655,26 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             // this stage's scale factors into one of two TMEM buffers (the
             // copies and the MMAs below run in issue order), then the four
             // K = 32 steps of the 128-wide K block, step j using byte j
+            // factor columns: A row block(s) first (4 each), then the tokens'
             const uint32_t sf = tmem_base + 2 * BN + (uint32_t)(sf_seq & 1) * Cfg::SF_COLS;
             ++sf_seq;
             const uint32_t slot = smem_u32(sSF + stage * Cfg::SF_BYTES);
+            constexpr int AH = Cfg::A_HALVES;
 #pragma unroll
-            for (int i = 0; i <= Cfg::SF_NB; ++i)
+            for (int i = 0; i < AH + Cfg::SF_NB; ++i)
               tmem_cp_32x128b_x4<Cfg::kPair>(sf + 4 * i, smem_desc_plain(slot + 512 * i, 512, 128));
+            const uint32_t sfb = sf + 4 * AH;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
               const uint64_t bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
               const uint32_t idk = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
-              umma_mx<Cfg::kPair>(d_tmem, ad, bd, idk, sf | ((uint32_t)k << 30), (sf + 4) | ((uint32_t)k << 30),
-                                  (kb > w.kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < AH; ++h) {
+                // kWideA: weight rows [128 h, 128 h + 128) of the stage into accumulator h
+                const uint64_t ad = umma_desc_sw128(a0 + h * (Cfg::BM * 128) + k * 32, 16, 1024);
+                umma_mx<Cfg::kPair>(d_tmem + h * BN, ad, bd, idk, (sf + 4 * h) | ((uint32_t)k << 30),
+                                    sfb | ((uint32_t)k << 30), (kb > w.kb0 || k > 0) ? 1u : 0u);
+              }
             }
           } else {
 #pragma unroll
@@ -718,7 +739,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int wb = lw.a_row / 128;  // weight scale block row of this CTA's 128 (or 2 x 64) rows
       ea = __float_as_uint(p.sf_w[(size_t)wb * p.sf_ksb + lkb]);
       eb = ea;
-      if constexpr (Cfg::kEpi == kEpiSwiGLUT) eb = __float_as_uint(p.sf_w2[(size_t)wb * p.sf_ksb + lkb]);
+      if constexpr (Cfg::kEpi == kEpiSwiGLUT)
+        eb = __float_as_uint(p.sf_w2[(size_t)wb * p.sf_ksb + lkb]);  // the w3 rows' block
+      else if constexpr (Cfg::kWideA)
+        eb = __float_as_uint(p.sf_w[(size_t)(wb + 1) * p.sf_ksb + lkb]);  // the second 128-row block
 #pragma unroll
       for (int i = 0; i < Cfg::SF_NB; ++i) {
 #pragma unroll
@@ -751,13 +775,19 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         const bool got = mbar_wait(&empty_bar[stage], phase ^ 1, s_abort);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
         uint8_t* slot = sSF + stage * Cfg::SF_BYTES;
-        // SwiGLU units hold [64 w1 rows | 64 w3 rows]: rows a and a + 32 are w1's, a + 64 and a + 96 w3's
+        // SwiGLU units hold [64 w1 rows | 64 w3 rows]: rows a and a + 32 are w1's, a + 64 and a + 96 w3's.
+        // kWideA: two 128-row blocks, [128 w1 | 128 w3] rows (or two row blocks of w2), one factor each.
         const uint32_t ea = ue8m0_of(__uint_as_float(r_ea[d])) * 0x01010101u;
         const uint32_t eb = ue8m0_of(__uint_as_float(r_eb[d])) * 0x01010101u;
-        *reinterpret_cast<uint4*>(slot + 16 * lane) = make_uint4(ea, ea, eb, eb);
+        if constexpr (Cfg::kWideA) {
+          *reinterpret_cast<uint4*>(slot + 16 * lane) = make_uint4(ea, ea, ea, ea);
+          *reinterpret_cast<uint4*>(slot + 512 + 16 * lane) = make_uint4(eb, eb, eb, eb);
+        } else {
+          *reinterpret_cast<uint4*>(slot + 16 * lane) = make_uint4(ea, ea, eb, eb);
+        }
 #pragma unroll
         for (int i = 0; i < Cfg::SF_NB; ++i)
-          *reinterpret_cast<uint4*>(slot + 512 * (1 + i) + 16 * lane) =
+          *reinterpret_cast<uint4*>(slot + 512 * (Cfg::A_HALVES + i) + 16 * lane) =
               make_uint4(ue8m0_of(__uint_as_float(r_tf[d][i][0])) * 0x01010101u,
                          ue8m0_of(__uint_as_float(r_tf[d][i][1])) * 0x01010101u,
                          ue8m0_of(__uint_as_float(r_tf[d][i][2])) * 0x01010101u,
@@ -836,8 +866,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     for (int u = unit0; u < nunits; u += unit_step) {
       const Unit w = decode_unit<Cfg>(p, u, rows_rt, rank, xt);
       if (!w.valid) continue;
-      const int buf = acc_i & 1;
-      const uint32_t aphase = (acc_i >> 1) & 1;
+      const int buf = Cfg::kWideA ? 0 : (acc_i & 1);
+      const uint32_t aphase = Cfg::kWideA ? (acc_i & 1) : ((acc_i >> 1) & 1);
       if constexpr (Cfg::kEpi == kEpiScatterT) {
         // slot and routing weight of every token column of this unit
         for (int t = epi_tid; t < BN_CH; t += 128) {  // columns past the unit's tokens get slot -1
@@ -862,7 +892,58 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int row = w.a_row + row_in_tile;
       const bool row_ok = row < w.row_end;
 
-      if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
+      if constexpr (Cfg::kWideA && Cfg::kEpi == kEpiSwiGLUT) {
+        // accumulator 0 (columns [0, BN)): x.w1 for this CTA's 128 features,
+        // accumulator 1 (columns [BN, 2 BN)): x.w3 for the same features, in
+        // the same TMEM lanes: gate and up meet in one thread
+        constexpr int CH = Cfg::CHUNK;
+        const int col = w.c_col + row_in_tile;
+        const int nch = (w.n_eff + CH - 1) / CH;
+        __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld_chunk<Cfg>(t_row + c * CH, rg);
+          tmem_ld_chunk<Cfg>(t_row + BN + c * CH, ru);
+          tmem_ld_wait(rg);
+          reg_dep(ru);
+          if (c == nch - 1) release_tmem(buf);
+          if (col < p.N) {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) {
+              const int tr = w.tok0 + c * CH + t;
+              if (tr < w.row_end)
+                outp[(size_t)tr * p.ldc + col] = __float2bfloat16_rn(silu_f(__uint_as_float(rg[t])) *
+                                                                     __uint_as_float(ru[t]));
+            }
+          }
+        }
+      } else if constexpr (Cfg::kWideA && Cfg::kEpi == kEpiScatterT) {
+        // accumulator h holds output features [c_col + 128 h, c_col + 128 h + 128)
+        constexpr int CH = Cfg::CHUNK;
+        const int nch = (w.n_eff + CH - 1) / CH;
+        __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int col = w.c_col + h * Cfg::BM + row_in_tile;
+#pragma unroll 1
+          for (int c = 0; c < nch; ++c) {
+            uint32_t r[32];
+            tmem_ld_chunk<Cfg>(t_row + h * BN + c * CH, r);
+            tmem_ld_wait(r);
+            if (h == 1 && c == nch - 1) release_tmem(buf);
+            if (col < p.N) {
+#pragma unroll
+              for (int t = 0; t < CH; ++t) {
+                const int slot = s_slot[c * CH + t];
+                if (slot >= 0)
+                  outp[(size_t)slot * p.ldc + col] = __float2bfloat16_rn(__uint_as_float(r[t]) * s_wt[c * CH + t]);
+              }
+            }
+          }
+        }
+        named_bar_sync(1, 128);  // s_slot / s_wt are rewritten for the next unit
+      } else if constexpr (Cfg::kEpi == kEpiSwiGLUT) {
         // TMEM rows 0..63: x.w1 for 64 features, rows 64..127: x.w3 for the
         // same features; columns: tokens. Gate rows hand their values over
         // through shared memory, up rows combine and store.

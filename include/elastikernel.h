@@ -326,7 +326,12 @@ int ek_moe_down_fp8bs(const void* aq, const float* a_scale, const void* w2q, con
  * accumulates in TMEM, with one epilogue per tile instead of one scaled
  * accumulation per 128-wide K block. Same arguments and outputs as the
  * _fp8bs entry points; token tiles 16/32/64/128 on one CTA, 128/160/192 on a
- * CTA pair (tok 0 = choose). A scale that is not a normal power of two sets
+ * CTA pair (tok 0 = choose). pair: -1 choose, 0 one CTA, 1 a CTA pair with
+ * 128 weight rows per CTA, 2 a CTA pair with 256 weight rows per CTA (two
+ * accumulators share each stage's token rows, which halves the token
+ * re-reads per weight byte; needs I % 256 == 0 for gate/up, H % 512 == 0 for
+ * down; chosen by -1 for gate/up from ~192 routed rows per expert). A scale
+ * that is not a normal power of two sets
  * EK_STATUS_BAD_SCALE in the device status word. No counterpart in the
  * reference (it has no FP8 path). */
 int ek_moe_gate_up_fp8mx(const void* xq, const float* x_scale, const void* w1q, const void* w3q,

@@ -85,10 +85,12 @@ def test_pow2_quantisation_matches_oracle(cuda_dev):
 
 @pytest.mark.parametrize("tok,pair,E", [(16, 0, 16), (32, 0, 16), (64, 0, 16), (128, 0, 16), (128, 0, 4),
                                         (128, 1, 16), (128, 1, 4), (160, 1, 16), (160, 1, 4), (192, 1, 16),
-                                        (192, 1, 4)])
+                                        (192, 1, 4), (128, 2, 16), (160, 2, 4), (192, 2, 16), (192, 2, 4)])
 def test_fp8mx_gemms_token_tiles(cuda_dev, tok, pair, E):
     """Every token tile; E=4 puts ~300 tokens on each expert, so every expert
-    spans several token tiles."""
+    spans several token tiles. pair=2: the wide pair tiles (256 weight rows
+    per CTA, two accumulators), against the epilogue-scaled kernel's pair
+    tile and the oracle."""
     from elastikernel_b200 import _ops
 
     T, H, I, k = 300, 512, 256, 4
@@ -98,9 +100,10 @@ def test_fp8mx_gemms_token_tiles(cuda_dev, tok, pair, E):
     xq, xs = _ops.quant_e4m3_kmajor(perm["x_perm"], pow2=True)
     outs = {}
     for mx in (True, False):
-        act = _ops.moe_gate_up_fp8bs(perm, xq, xs, qw, tok_tile=tok, pair=pair, mx=mx)
+        pr = pair if mx else min(pair, 1)
+        act = _ops.moe_gate_up_fp8bs(perm, xq, xs, qw, tok_tile=tok, pair=pr, mx=mx)
         aq, as_ = _ops.quant_e4m3_kmajor(act, pow2=True)
-        y = _ops.moe_down_fp8bs(perm, aq, as_, qw, wts, tok_tile=tok, pair=pair, mx=mx)
+        y = _ops.moe_down_fp8bs(perm, aq, as_, qw, wts, tok_tile=tok, pair=pr, mx=mx)
         outs[mx] = (act, _ops.moe_combine(y, T, k))
     torch.cuda.synchronize()
     # the two kernels on the same quantised inputs: the same math, another summation order
