@@ -620,7 +620,9 @@ def moe_bench(dev, steps: int, hbm_gbs: float, peak_bf16_tflops: float, cpu: boo
                         "tokens_per_s": round(T / t_s, 1), "tflops": round(flop / t_s / 1e12, 1),
                         "experts_hit": hit, "pct_roofline_time": round(100 * t_floor / t_s, 1),
                         "graph_us": round(rg["mean_ms"] * 1e3, 1), "graph_tokens_per_s": round(T / tg_s, 1),
-                        "graph_pct_roofline_time": round(100 * t_floor / tg_s, 1)})
+                        "graph_pct_roofline_time": round(100 * t_floor / tg_s, 1),
+                        "eager_reps_us": [round(v * 1e3) for v in r["all_ms"]],
+                        "graph_reps_us": [round(v * 1e3) for v in rg["all_ms"]]})
     out = {"config": "Mixtral E=8 k=2 H=4096 I=14336 bf16, weights N(0,0.02); us = eager launches from "
                      "Python, graph_us = the layer replayed from a CUDA graph; roofline = max(tensor at the "
                      "measured bf16 burst x SMs/148, expert weights at the measured HBM rate)",
@@ -706,6 +708,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the partition sweep, MoE and CPU legs")
+    ap.add_argument("--legs", default="partitions,fp8,moe,moe_ep,triton,cpu",
+                    help="comma list of the extra legs to run (default: all)")
     ap.add_argument("--triton-sms", default="16,32,64,96,132,148",
                     help="partition sizes (comma list, '' for none) at which the reference's own Triton GEMM is "
                          "timed beside the tcgen05 one; its MoE segment kernel runs at 64 SMs")
@@ -777,15 +781,19 @@ def main() -> None:
             traffic = None
 
     extras = {}
-    if not args.no_extras:
+    legs = set() if args.no_extras else {v.strip() for v in args.legs.split(",")}
+    if "partitions" in legs:
         extras["partitions"] = partition_sweep(dev, peak_tf, args.steps, hbm)
+    if "fp8" in legs:
         extras["fp8"] = fp8_bench(dev, peak_tf, args.steps)
-        extras["moe"] = moe_bench(dev, args.steps, hbm, peak_tf, cpu=(rank == 0 and world == 1))
+    if "moe" in legs:
+        extras["moe"] = moe_bench(dev, args.steps, hbm, peak_tf, cpu=(rank == 0 and world == 1 and "cpu" in legs))
+    if "moe_ep" in legs:
         extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
-        if rank == 0 and world == 1 and args.triton_sms.strip():
-            extras["triton_reference"] = triton_reference(dev, [int(x) for x in args.triton_sms.split(",")])
-        if rank == 0 and world == 1:
-            extras["cpu_baseline"] = cpu_baseline_sample()
+    if "triton" in legs and rank == 0 and world == 1 and args.triton_sms.strip():
+        extras["triton_reference"] = triton_reference(dev, [int(x) for x in args.triton_sms.split(",")])
+    if "cpu" in legs and rank == 0 and world == 1:
+        extras["cpu_baseline"] = cpu_baseline_sample()
     if world > 1:
         import torch.distributed as dist
 
