@@ -433,12 +433,19 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
     # nothing is read back between the routing and the combine
     # the equal-split exchanges go through an NCCL communicator driven on the
     # communication partition's stream, so their kernels stay on its 32 SMs
-    stream_a2a = None
+    # The grouped layer's exchanges go by copy engines straight into the
+    # peers' IPC-mapped receive buffers (no NCCL, no SM); the ungrouped
+    # layer's through an NCCL communicator driven on the communication
+    # partition's stream.
+    stream_a2a = p2p = None
     if world > 1:
         from elastikernel_b200.nccl_stream import StreamAllToAll
+        from elastikernel_b200.p2p_exchange import P2PAllToAll
 
         stream_a2a = StreamAllToAll()
-    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto", stream_a2a=stream_a2a)
+        p2p = P2PAllToAll()
+    moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto", stream_a2a=stream_a2a,
+                            p2p=p2p)
     # Expert groups (N > 1): each rank's experts in 2 groups; a group's
     # exchanges run on the 32-SM partition (NCCL driven on its stream) while
     # another group's GEMMs run in the 116-SM partition, and every expert
@@ -467,7 +474,15 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
             torch.cuda.synchronize()
         return max_over_ranks(s.elapsed_time(e) / reps, world), y
 
-    ms, out = time_layer(groups)
+    exchange = "copy engines into IPC-mapped buffers" if (p2p is not None and groups > 1) else "NCCL"
+    try:
+        ms, out = time_layer(groups)
+    except RuntimeError as err:  # the copy-engine path could not map the peers' buffers: NCCL instead
+        if p2p is None:
+            raise
+        moe.p2p = None
+        exchange = f"NCCL (copy-engine exchange unavailable: {str(err)[:160]})"
+        ms, out = time_layer(groups)
     ms_ungrouped = time_layer(1)[0] if groups > 1 else ms
     # phase split of one ungrouped layer (device time between phase events on
     # the experts' partition stream; NCCL inside the same timeline)
@@ -492,6 +507,8 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
     if stream_a2a is not None:
         barrier(world)
         stream_a2a.close()
+    if moe.p2p is not None:
+        moe.p2p.close()
     flop = T * k * 6.0 * H * I
     tf = flop / (ms * 1e-3) / 1e12
     peak_fp8 = 2.0 * peak_bf16_tflops
@@ -500,7 +517,7 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
             "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
             "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms, "comm_partition_sms": comm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
-            "expert_groups": groups, "ms_per_layer_ungrouped": round(ms_ungrouped, 3),
+            "expert_groups": groups, "exchange": exchange, "ms_per_layer_ungrouped": round(ms_ungrouped, 3),
             "placement": ("experts in the 116-SM green context, exchanges on the 32-SM one, overlapped group by "
                           "group" if groups > 1 else "routing, exchanges and the experts' 116-CTA GEMMs in turn on "
                           "a full-device stream"),

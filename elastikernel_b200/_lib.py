@@ -86,6 +86,13 @@ _SIGNATURES = {
     "ek_moe_permute_scratch_bytes": (_c_size, [_c_int, _c_int, _c_int]),
     "ek_moe_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int,
                                 _c_int, _c_vp, _c_vp, _c_vp]),
+    "ek_p2p_mem_base": (_c_int, [_c_vp, ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(_c_size)]),
+    "ek_p2p_ipc_handle": (_c_int, [_c_vp, _c_vp]),
+    "ek_p2p_ipc_open": (_c_int, [_c_vp, ctypes.POINTER(_c_vp)]),
+    "ek_p2p_ipc_close": (_c_int, [_c_vp]),
+    "ek_p2p_copy": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
+    "ek_p2p_signal": (_c_int, [ctypes.POINTER(_c_vp), _c_int, _c_int, _c_vp]),
+    "ek_p2p_wait": (_c_int, [_c_vp, _c_int, _c_int, _c_vp]),
     "ek_moe_route_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
                                       _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,

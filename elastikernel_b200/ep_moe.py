@@ -220,7 +220,7 @@ class ExpertParallelMoE:
     are dispatched as e4m3 with 1 x 128 scales (half the bytes of bf16)."""
 
     def __init__(self, num_experts: int, topk: int, w1=None, w2=None, w3=None, group=None, ops=None, qw=None,
-                 capacity=None, stream_a2a=None):
+                 capacity=None, stream_a2a=None, p2p=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -243,6 +243,9 @@ class ExpertParallelMoE:
         # current stream (e.g. a communication partition's) instead of the
         # process group's internal one
         self.stream_a2a = stream_a2a
+        # p2p_exchange.P2PAllToAll: the grouped layer's equal-split exchanges
+        # by copy engines into IPC-mapped receive buffers (no NCCL, no SM)
+        self.p2p = p2p
 
     def capacity_rows(self, n_slots: int, groups: int = 1) -> int:
         """Rows per destination of a fixed-capacity exchange of n_slots slots,
@@ -389,24 +392,25 @@ class ExpertParallelMoE:
         xs_send = ops.gather_capacity(cap, xs) if self.fp8 else None
         return (x_send, xs_send, cap["local_ids"], cap["weights"]), cap["slot_row"], Cg
 
+    def _xchg(self, inp, key):
+        """Equal-split all-to-all of `inp`: through the copy-engine exchange
+        when one is configured, else into a new tensor over NCCL."""
+        if self.p2p is not None and self.world > 1 and inp.is_cuda:
+            return self.p2p.all_to_all(inp, key)
+        out = torch.empty_like(inp)
+        self._a2a(out, inp, None, None)
+        return out
+
     def _exchange_group(self, send, g: int, rows_g: int):
         """All-to-all of group g's block of the send layout (equal splits)."""
         sl = slice(g * rows_g, (g + 1) * rows_g)
         x_send, xs_send, ids_send, w_send = send
         xb = x_send[sl]
-        x_recv = torch.empty_like(xb)
         if self.fp8:  # byte view: the exchange does not need to know the float8 type
-            self._a2a(x_recv.view(torch.uint8), xb.view(torch.uint8), None, None)
-            xs_recv = torch.empty_like(xs_send[sl])
-            self._a2a(xs_recv, xs_send[sl], None, None)
-            x_recv = (x_recv, xs_recv)
+            x_recv = (self._xchg(xb.view(torch.uint8), ("x", g)).view(xb.dtype), self._xchg(xs_send[sl], ("xs", g)))
         else:
-            self._a2a(x_recv, xb, None, None)
-        ids_recv = torch.empty_like(ids_send[sl])
-        self._a2a(ids_recv, ids_send[sl], None, None)
-        w_recv = torch.empty_like(w_send[sl])
-        self._a2a(w_recv, w_send[sl], None, None)
-        return x_recv, ids_recv, w_recv
+            x_recv = self._xchg(xb, ("x", g))
+        return x_recv, self._xchg(ids_send[sl], ("ids", g)), self._xchg(w_send[sl], ("w", g))
 
     def _group_weights(self, a: int, b: int):
         """The weights of local experts [a, b): views, e4m3 codes with their
@@ -475,14 +479,21 @@ class ExpertParallelMoE:
                     ev_y = torch.cuda.Event()
                     ev_y.record(compute)
                 ys.append((y, ev_y))
+        use_p2p = self.p2p is not None and self.world > 1 and x.is_cuda
         with on(comm):
             y0 = ys[0][0]
-            y_back = torch.empty((groups * rows_g, y0.shape[1]), dtype=y0.dtype, device=y0.device)
+            shape = (groups * rows_g, y0.shape[1])
+            y_back = None if use_p2p else torch.empty(shape, dtype=y0.dtype, device=y0.device)
             for g, (y, ev_y) in enumerate(ys):
                 if piped:
                     comm.wait_event(ev_y)
                     y.record_stream(comm)  # made on the compute stream, sent from here
-                self._a2a(y_back[g * rows_g:(g + 1) * rows_g], y, None, None)
+                if use_p2p:  # every group's results land in one buffer, group after group
+                    self.p2p.all_to_all(y, ("y", groups), part=g, parts=groups)
+                else:
+                    self._a2a(y_back[g * rows_g:(g + 1) * rows_g], y, None, None)
+            if use_p2p:
+                y_back = self.p2p.buffer_view(("y", groups), y0.dtype, shape)
         if piped:
             cur.wait_stream(comm)
             y_back.record_stream(cur)  # made on the comm stream, read here

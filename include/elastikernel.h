@@ -387,6 +387,27 @@ int ek_ep_capacity_layout(const int* sorted_slots, const int* dest_counts, int w
                           const int* topk_ids, const float* topk_weights, int experts_per_rank, int* cap_slots,
                           int* local_ids, float* weights_out, int* slot_row, void* stream);
 
+/* Peer-to-peer exchange primitives (expert-parallel all-to-all over NVLink
+ * without NCCL; no counterpart in the reference, which has no multi-GPU
+ * path). ek_p2p_mem_base: the base address and size of the device allocation
+ * holding ptr (cuMemGetAddressRange). ek_p2p_ipc_handle: the 64-byte CUDA IPC
+ * handle of an allocation base. ek_p2p_ipc_open / _close: map / unmap another
+ * process's allocation on the current device (peer access enabled on
+ * demand). ek_p2p_copy: cudaMemcpyAsync device to device on `stream` (the
+ * copy engines; dst may be a peer mapping). ek_p2p_signal: after the work
+ * queued before it on `stream`, store `value` into each of the n int flags
+ * (peer mappings allowed) with system-scope release. ek_p2p_wait: on
+ * `stream`, wait until each of the n local int flags holds a value >= `value`
+ * (system-scope acquire; bounded: after 2 s EK_STATUS_WAIT_TIMEOUT is raised
+ * and the wait ends). n <= 64. */
+int ek_p2p_mem_base(const void* ptr, unsigned long long* base, size_t* size);
+int ek_p2p_ipc_handle(const void* base, void* handle_out);
+int ek_p2p_ipc_open(const void* handle, void** ptr);
+int ek_p2p_ipc_close(void* ptr);
+int ek_p2p_copy(void* dst, const void* src, size_t bytes, void* stream);
+int ek_p2p_signal(void* const* flags, int n, int value, void* stream);
+int ek_p2p_wait(const int* flags, int n, int value, void* stream);
+
 /* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);
 

@@ -158,6 +158,12 @@ def test_ep_world1_expert_groups_streams(cuda_dev, fp8, groups):
     assert torch.equal(out, out_seq)
 
 
+def _lib_status(dev) -> int:
+    from elastikernel_b200 import _lib
+
+    return _lib.device_status(dev.index if dev.index is not None else 0, clear=True)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -232,6 +238,41 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         dist.barrier()
         sa.close()
+        # the copy-engine exchange: the same bytes as all_to_all_single (three
+        # calls of one key: both buffers and a reuse), a multi-part key, and
+        # the grouped layer over it
+        from elastikernel_b200.p2p_exchange import P2PAllToAll
+
+        px = P2PAllToAll()
+        for rep in range(3):
+            inp = torch.randn(world * 4096, device=dev) + rep
+            want = torch.empty_like(inp)
+            dist.all_to_all_single(want, inp)
+            p_comm.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(p_comm):
+                got = px.all_to_all(inp, "probe").clone()
+            p_comm.synchronize()
+            if not torch.equal(got, want):
+                raise AssertionError(f"P2PAllToAll differs from all_to_all_single (call {rep})")
+        parts = [torch.randn(world * 512, device=dev) for _ in range(3)]
+        for i, t in enumerate(parts):
+            px.all_to_all(t, "multi", part=i, parts=3)
+        torch.cuda.synchronize()
+        whole = px.buffer_view("multi", torch.float32, (3, world * 512))
+        for i, t in enumerate(parts):
+            want = torch.empty_like(t)
+            dist.all_to_all_single(want, t)
+            if not torch.equal(whole[i], want):
+                raise AssertionError(f"P2PAllToAll part {i} differs")
+        moe_p = ExpertParallelMoE(E, K_TOP, qw=qw, capacity="auto", ops=CudaEPOps(num_sms=p_sms), p2p=px)
+        for _ in range(3):  # the arenas' two buffers, then the first again
+            outp = moe_p(xc, lc, groups=2, compute_stream=p_comp, comm_stream=p_comm)
+            err_fp8 = max(err_fp8, max_rel_err(outp, refc.float().cpu().numpy()))
+        torch.cuda.synchronize()
+        st = _lib_status(dev)
+        if st:
+            raise AssertionError(f"device status {st} after the copy-engine exchanges")
+        px.close()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
