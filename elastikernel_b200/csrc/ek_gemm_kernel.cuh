@@ -140,7 +140,7 @@ struct GemmCfg {
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(!kMx || (kF8 && kSwapped && TMEM_NEED <= 512), "block scaling: e4m3 swapped tiles up to 192 tokens");
   static_assert(!kMx || SF_RELAY <= STAGES, "relay batch within the stage ring");
-  static_assert(!kWideA || (kMx && kPair), "wide weight tiles: block-scaled CTA-pair swapped tiles");
+  static_assert(!kWideA || (kSwapped && kPair), "wide weight tiles: CTA-pair swapped tiles");
 };
 
 struct GemmParams {
@@ -679,17 +679,21 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           } else {
 #pragma unroll
           for (int k = 0; k < BK / UK; ++k) {
-            const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
             uint64_t bd;
             if constexpr (Cfg::kBMN)
               bd = umma_desc_sw128(b0 + k * UK * 128, BK * 128, 1024);
             else
               bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
             const uint32_t acc = (kb > w.kb0 || k > 0) ? 1u : 0u;
-            if constexpr (Cfg::kPair)
-              umma_pair<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
-            else
-              umma<Cfg::kF8>(d_tmem, ad, bd, idesc, acc);
+#pragma unroll
+            for (int h = 0; h < Cfg::A_HALVES; ++h) {
+              // kWideA: weight rows [128 h, 128 h + 128) of the stage into accumulator h
+              const uint64_t ad = umma_desc_sw128(a0 + h * (Cfg::BM * 128) + k * 32, 16, 1024);
+              if constexpr (Cfg::kPair)
+                umma_pair<Cfg::kF8>(d_tmem + h * BN, ad, bd, idesc, acc);
+              else
+                umma<Cfg::kF8>(d_tmem + h * BN, ad, bd, idesc, acc);
+            }
           }
           }
           if constexpr (Cfg::kPair)

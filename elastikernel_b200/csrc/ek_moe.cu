@@ -504,6 +504,30 @@ int launch_packed_tok(int tok, const CUtensorMap& ta, const CUtensorMap& tb, con
   return set_error(EK_ERR_INVALID, "token tile must be 16, 32, 64, 128 or 256 (got %d)", tok);
 }
 
+// Wide CTA-pair tiles for the packed gate/up GEMM (GemmCfg kWideA: 256
+// weight rows per CTA, two accumulators sharing the token rows, so the token
+// tile is re-read half as often per weight byte), taken only when pair = 2
+// asks for them: in bf16 the Mixtral-shaped loads measured slightly slower
+// with them (T = 1024: 555 -> 567 us, T = 2048: 912 -> 939 us on 148 SMs;
+// the kernel sits at the tensor/HBM ridge there and the single TMEM buffer
+// leaves the epilogue unhidden), unlike the e4m3 gate/up at expert-parallel
+// loads, where the token re-reads dominate.
+bool packed_wide(int tok, int pr, int pair, int I, bool split) {
+  return pair == 2 && pr && !split && (tok == 128 || tok == 256) && I % 256 == 0;
+}
+
+template <int kEpi>
+int launch_packed_wide(int tok, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tx,
+                       const GemmParams& p, int grid, cudaStream_t s) {
+  switch (tok) {
+    case 128:
+      return launch_grouped<GemmCfg<128, kBF16, false, kEpi, kSchedExperts, true, false, true>>(ta, tb, tx, p, grid, s);
+    case 256:
+      return launch_grouped<GemmCfg<256, kBF16, false, kEpi, kSchedExperts, true, false, true>>(ta, tb, tx, p, grid, s);
+  }
+  return set_error(EK_ERR_INVALID, "wide token tile must be 128 or 256 (got %d)", tok);
+}
+
 // Expected 128-row blocks of the padded layout for n_slots (token, choice)
 // slots over E experts: every used expert adds at most one partial block.
 int est_mblocks(long long n_slots, int E, int max_mblocks) {
@@ -812,21 +836,28 @@ int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, co
   int rc = resolve_num_sms(num_sms, stream, &S);
   if (rc) return rc;
   int tok = 0, pr = 0;
-  packed_tiles(rows, E, S, tok_tile, pair, &tok, &pr);
+  packed_tiles(rows, E, S, tok_tile, pair == 2 ? 1 : pair, &tok, &pr);
   const int ctas = pr ? 2 : 1;
+  const size_t need = split_workspace_bytes(rows, H, I);
+  const int ft_normal = (I + 64 * ctas - 1) / (64 * ctas);
+  const bool may_split = need > 0 && workspace != nullptr && workspace_bytes >= need && aligned16(workspace) &&
+                         split_expected(rows, E, tok, ctas, S, ft_normal, (H + 63) / 64);
+  // features per CTA: 64 ([64 w1 | 64 w3] weight rows), or 128 with wide tiles
+  const bool wide = packed_wide(tok, pr, pair, I, may_split);
+  const int fpc = wide ? 128 : 64;
   CUtensorMap ta, tx, tb;
-  if ((rc = make_tmap_2d(&ta, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, 64)))
+  if ((rc = make_tmap_2d(&ta, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, fpc)))
     return rc;
-  if ((rc = make_tmap_2d(&tx, w3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, 64)))
+  if ((rc = make_tmap_2d(&tx, w3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, (uint64_t)H * 2, 64, fpc)))
     return rc;
   if ((rc = make_tmap_2d(&tb, x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, rows, (uint64_t)H * 2, 64, tok / ctas)))
     return rc;
   GemmParams p{};
   uint64_t plane = 0;
   if (plane_stride(w1, w3, (uint64_t)E * I * H * 2, &plane)) {
-    // w3 lies a fixed distance after w1: one 3-D box loads a unit's [64 w1 | 64 w3] weight rows
+    // w3 lies a fixed distance after w1: one 3-D box loads a unit's [fpc w1 | fpc w3] weight rows
     CUtensorMap t3;
-    if (make_tmap_3d(&t3, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, 2, (uint64_t)H * 2, plane, 64, 64,
+    if (make_tmap_3d(&t3, w1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, (uint64_t)E * I, 2, (uint64_t)H * 2, plane, 64, fpc,
                      2) == EK_OK) {
       ta = t3;
       p.a_planes = 1;
@@ -843,10 +874,7 @@ int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, co
   p.num_experts = E;
   p.expert_counts = expert_counts;
   p.w_rows_per_expert = I;
-  p.feat_tiles = (I + 64 * ctas - 1) / (64 * ctas);
-  const size_t need = split_workspace_bytes(rows, H, I);
-  const bool may_split = need > 0 && workspace != nullptr && workspace_bytes >= need && aligned16(workspace) &&
-                         split_expected(rows, E, tok, ctas, S, p.feat_tiles, p.k_blocks);
+  p.feat_tiles = wide ? I / (fpc * ctas) : ft_normal;
   if (may_split) {
     p.tail_split = kSplitMax;
     p.ws_counters = static_cast<int*>(workspace);
@@ -854,8 +882,9 @@ int ek_moe_gate_up_packed(const void* x_perm, const void* w1, const void* w3, co
   }
   const int grid = std::max(1, S / ctas) * ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = pr ? launch_packed_tok<kEpiSwiGLUT, true>(tok, ta, tb, tx, p, grid, s)
-          : launch_packed_tok<kEpiSwiGLUT, false>(tok, ta, tb, tx, p, grid, s);
+  rc = wide ? launch_packed_wide<kEpiSwiGLUT>(tok, ta, tb, tx, p, grid, s)
+       : pr  ? launch_packed_tok<kEpiSwiGLUT, true>(tok, ta, tb, tx, p, grid, s)
+             : launch_packed_tok<kEpiSwiGLUT, false>(tok, ta, tb, tx, p, grid, s);
   if (rc || !may_split) return rc;
   const int n = rows * I;
   split_swiglu_kernel<<<std::max(1, std::min((n + 255) / 256, 148 * 4)), 256, 0, s>>>(

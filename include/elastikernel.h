@@ -281,7 +281,11 @@ int ek_moe_down(const void* act, const void* w2, const int* block_expert, const 
  * 128-row (or 256-row with pair = 1, a 2-SM CTA pair) side and the expert's
  * tokens the N side, in tiles of tok_tile tokens (16/32/64/128/256). Weight
  * tiles stream from HBM once per token tile, which keeps small token counts
- * HBM-efficient. tok_tile = 0 and pair = -1 choose automatically.
+ * HBM-efficient. tok_tile = 0 and pair = -1 choose automatically. For the
+ * gate/up GEMM pair = 2 asks for wide pair tiles (256 weight rows per CTA,
+ * two accumulators sharing the token rows; token tiles 128 / 256, I % 256 ==
+ * 0, no K-split; bit-identical results), never chosen automatically: in bf16
+ * they measured slightly slower at the Mixtral shapes.
  * Results equal the block-padded variants' (within fp32 summation order).
  * E <= 256.
  *

@@ -167,6 +167,33 @@ def test_packed_token_tiles(cuda_dev, tok, pair):
     assert og.max_rel_err(out, om.moe_ref(x, logits, w1, w2, w3, k)) <= TOL
 
 
+@pytest.mark.parametrize("tok", [128, 256])
+@pytest.mark.parametrize("planes", [False, True])
+def test_packed_wide_gate_up(cuda_dev, tok, planes):
+    """Wide CTA-pair gate/up tiles (256 weight rows per CTA, two accumulators):
+    bit-identical to the 128-row pair tiles (same per-element K order), and
+    the layer against the oracle; w1 / w3 as two tensors or as the two planes
+    of one (one 3-D box per stage)."""
+    from elastikernel_b200 import _ops
+
+    T, H, I, E, k = 700, 256, 512, 8, 2
+    x, logits, w1, w2, w3 = _moe_inputs(T, H, I, E, seed=tok + planes)
+    d = [t.to(cuda_dev) for t in (x, logits, w1, w2, w3)]
+    if planes:
+        w13 = torch.stack([d[2], d[4]])
+        d[2], d[4] = w13[0], w13[1]
+    ids, wts = _ops.moe_route(d[1], k)
+    perm = _ops.moe_permute(ids, E, x=d[0], block_m=1)
+    act_w = _ops.moe_gate_up_packed(perm, d[2], d[4], tok_tile=tok, pair=2, ksplit=False)
+    act_n = _ops.moe_gate_up_packed(perm, d[2], d[4], tok_tile=tok, pair=1, ksplit=False)
+    y = _ops.moe_down_packed(perm, act_w, d[3], wts, tok_tile=tok, pair=1)
+    out = _ops.moe_combine(y, T, k)
+    torch.cuda.synchronize()
+    n = int(perm["num_rows_padded"].item())
+    assert torch.equal(act_w[:n], act_n[:n])
+    assert og.max_rel_err(out, om.moe_ref(x, logits, w1, w2, w3, k)) <= TOL
+
+
 @pytest.mark.parametrize("T", [1, 16, 128])
 def test_fused_moe_mixtral_shapes(cuda_dev, T):
     """Mixtral expert shapes (H=4096, I=14336, E=8, top-2) at small token counts."""
