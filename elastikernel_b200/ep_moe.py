@@ -401,16 +401,20 @@ class ExpertParallelMoE:
         self._a2a(out, inp, None, None)
         return out
 
-    def _exchange_group(self, send, g: int, rows_g: int):
-        """All-to-all of group g's block of the send layout (equal splits)."""
+    def _exchange_group(self, send, g: int, rows_g: int, groups: int):
+        """All-to-all of group g's block of the send layout (equal splits).
+        The exchange keys name the group count and the block's rows, so
+        layers of other shapes on the same exchanger get buffers of their own."""
         sl = slice(g * rows_g, (g + 1) * rows_g)
         x_send, xs_send, ids_send, w_send = send
         xb = x_send[sl]
+        tag = (groups, rows_g, g)
         if self.fp8:  # byte view: the exchange does not need to know the float8 type
-            x_recv = (self._xchg(xb.view(torch.uint8), ("x", g)).view(xb.dtype), self._xchg(xs_send[sl], ("xs", g)))
+            x_recv = (self._xchg(xb.view(torch.uint8), ("x",) + tag).view(xb.dtype),
+                      self._xchg(xs_send[sl], ("xs",) + tag))
         else:
-            x_recv = self._xchg(xb, ("x", g))
-        return x_recv, self._xchg(ids_send[sl], ("ids", g)), self._xchg(w_send[sl], ("w", g))
+            x_recv = self._xchg(xb, ("x",) + tag)
+        return x_recv, self._xchg(ids_send[sl], ("ids",) + tag), self._xchg(w_send[sl], ("w",) + tag)
 
     def _group_weights(self, a: int, b: int):
         """The weights of local experts [a, b): views, e4m3 codes with their
@@ -459,7 +463,7 @@ class ExpertParallelMoE:
         with on(comm):
             recvs = []
             for g in range(groups):
-                recv = self._exchange_group(send, g, rows_g)
+                recv = self._exchange_group(send, g, rows_g, groups)
                 ev = None
                 if piped:
                     ev = torch.cuda.Event()
@@ -489,11 +493,11 @@ class ExpertParallelMoE:
                     comm.wait_event(ev_y)
                     y.record_stream(comm)  # made on the compute stream, sent from here
                 if use_p2p:  # every group's results land in one buffer, group after group
-                    self.p2p.all_to_all(y, ("y", groups), part=g, parts=groups)
+                    self.p2p.all_to_all(y, ("y", groups, rows_g), part=g, parts=groups)
                 else:
                     self._a2a(y_back[g * rows_g:(g + 1) * rows_g], y, None, None)
             if use_p2p:
-                y_back = self.p2p.buffer_view(("y", groups), y0.dtype, shape)
+                y_back = self.p2p.buffer_view(("y", groups, rows_g), y0.dtype, shape)
         if piped:
             cur.wait_stream(comm)
             y_back.record_stream(cur)  # made on the comm stream, read here
