@@ -617,11 +617,8 @@ def moe_bench(dev, steps: int, hbm_gbs: float, peak_bf16_tflops: float, cpu: boo
         logits = torch.randn((T, E), device=dev, generator=g)
         for label, stream, sms in (("full", torch.cuda.current_stream(dev), 148), ("half", half_stream, half_sms)):
             with torch.cuda.stream(stream):
-                # ~0.2 s of untimed layers first: after the full-device layers the
-                # power-capped SM clock takes ~0.1 s to recover on the partition
-                # (T=4096 on 72 SMs ran 4.9 ms per layer for its first ~30 layers
-                # after the full-device ones, 3.55 ms on a fresh partition)
-                settle(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k), None, ms=200.0)
+                for _ in range(2):
+                    _ops.fused_moe(x, logits, w1, w2, w3, k)
                 r = time_on_stream(lambda: _ops.fused_moe(x, logits, w1, w2, w3, k), stream,
                                    reps=max(3, steps // 2), warmup=2)
                 # the same layer replayed from a CUDA graph (no host work between its launches)
