@@ -899,7 +899,8 @@ def summarize(line: dict) -> dict:
         sm["moe_ep"] = {"n_gpus": ep["n_gpus"], "ms": ep["ms_per_layer"], "tokens_per_s": ep["tokens_per_s"],
                         "pct_fp8_peak_scaled": ep["pct_fp8_peak_scaled"], "gemm_sms": ep["gemm_partition_sms"],
                         "ep_max_rel_err": [ep["ep_max_rel_err"], ep.get("ep_max_rel_err_act_e4m3")],
-                        "expert_groups": ep["expert_groups"], "ms_ungrouped": ep.get("ms_per_layer_ungrouped"),
+                        "expert_groups": ep["expert_groups"], "exchange": ep.get("exchange", "")[:40],
+                        "ms_ungrouped": ep.get("ms_per_layer_ungrouped"),
                         "phases_ms_ungrouped": ep["phases_ms_ungrouped"],
                         "a2a_gbs": [ep["all_to_all"].get("dispatch_gbs_per_rank"),
                                     ep["all_to_all"].get("combine_gbs_per_rank")]}
