@@ -443,7 +443,7 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
         from elastikernel_b200.p2p_exchange import P2PAllToAll
 
         stream_a2a = StreamAllToAll()
-        p2p = P2PAllToAll()
+        p2p = P2PAllToAll(device_epochs=True)  # device-side epochs: the layer can be graph-replayed
     moe = ExpertParallelMoE(E, k, qw=qw, ops=CudaEPOps(num_sms=gemm_sms), capacity="auto", stream_a2a=stream_a2a,
                             p2p=p2p)
     # Expert groups (N > 1): each rank's experts in 2 groups; a group's
@@ -484,6 +484,46 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
         exchange = f"NCCL (copy-engine exchange unavailable: {str(err)[:160]})"
         ms, out = time_layer(groups)
     ms_ungrouped = time_layer(1)[0] if groups > 1 else ms
+    # The same layer captured once in a CUDA graph and replayed (no host work
+    # between its launches; the copy-engine exchanges keep their epochs on the
+    # device). This is the layer time reported; the eager time stays beside it.
+    # At N > 1 only the grouped copy-engine layer is captured (no NCCL call in
+    # a graph).
+    ms_graph, graph_match, graph_note = None, None, None
+    if world == 1 or (groups > 1 and moe.p2p is not None):
+        from elastikernel_b200.graph import Captured
+
+        cap = None
+        try:
+            with torch.cuda.stream(main):
+                cap = Captured(lambda: moe(x, logits, groups=groups, compute_stream=gemm_stream,
+                                           comm_stream=comm_stream), main)
+        except RuntimeError as err:  # the eager time stands
+            graph_note = f"capture failed: {str(err)[:160]}"
+            torch.cuda.synchronize()
+        ok = max_over_ranks(float(cap is None), world) == 0.0  # every rank captured
+        if ok:
+            with torch.cuda.stream(main):
+                for _ in range(2):
+                    cap()
+                torch.cuda.synchronize()
+                barrier(world)
+                reps = max(3, steps // 10)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(main)
+                for _ in range(reps):
+                    yg = cap()
+                e.record(main)
+                torch.cuda.synchronize()
+            ms_graph = max_over_ranks(s.elapsed_time(e) / reps, world)
+            graph_match = bool(max_over_ranks(float(not torch.equal(yg, out)), world) == 0.0)
+            del yg
+        del cap
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_eager = ms
+    if ms_graph is not None:
+        ms = ms_graph
     # phase split of one ungrouped layer (device time between phase events on
     # the experts' partition stream; NCCL inside the same timeline)
     barrier(world)
@@ -518,6 +558,9 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
             "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms, "comm_partition_sms": comm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
             "expert_groups": groups, "exchange": exchange, "ms_per_layer_ungrouped": round(ms_ungrouped, 3),
+            "ms_per_layer_eager": round(ms_eager, 3), "timing": ("the layer replayed from a CUDA graph"
+                                                                if ms_graph is not None else "eager launches"),
+            "graph_equals_eager": graph_match, **({"graph_note": graph_note} if graph_note else {}),
             "placement": ("experts in the 116-SM green context, exchanges on the 32-SM one, overlapped group by "
                           "group" if groups > 1 else "routing, exchanges and the experts' 116-CTA GEMMs in turn on "
                           "a full-device stream"),
@@ -900,7 +943,7 @@ def summarize(line: dict) -> dict:
                         "pct_fp8_peak_scaled": ep["pct_fp8_peak_scaled"], "gemm_sms": ep["gemm_partition_sms"],
                         "ep_max_rel_err": [ep["ep_max_rel_err"], ep.get("ep_max_rel_err_act_e4m3")],
                         "expert_groups": ep["expert_groups"], "exchange": ep.get("exchange", "")[:40],
-                        "ms_ungrouped": ep.get("ms_per_layer_ungrouped"),
+                        "ms_ungrouped": ep.get("ms_per_layer_ungrouped"), "ms_eager": ep.get("ms_per_layer_eager"),
                         "phases_ms_ungrouped": ep["phases_ms_ungrouped"],
                         "a2a_gbs": [ep["all_to_all"].get("dispatch_gbs_per_rank"),
                                     ep["all_to_all"].get("combine_gbs_per_rank")]}

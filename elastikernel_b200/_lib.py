@@ -93,6 +93,8 @@ _SIGNATURES = {
     "ek_p2p_copy": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
     "ek_p2p_signal": (_c_int, [ctypes.POINTER(_c_vp), _c_int, _c_int, _c_vp]),
     "ek_p2p_wait": (_c_int, [_c_vp, _c_int, _c_int, _c_vp]),
+    "ek_p2p_signal_dev": (_c_int, [ctypes.POINTER(_c_vp), _c_int, _c_vp, _c_vp]),
+    "ek_p2p_wait_dev": (_c_int, [_c_vp, _c_int, _c_vp, _c_vp]),
     "ek_moe_route_permute": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
                                       _c_vp, _c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "ek_moe_gate_up": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,

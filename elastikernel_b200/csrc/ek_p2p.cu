@@ -52,6 +52,40 @@ __global__ void p2p_wait_kernel(const int* flags, int n, int value) {
   __threadfence();
 }
 
+// Device-side epochs (for layers replayed from a CUDA graph, where a value
+// baked into a kernel parameter would repeat): the signal kernel increments
+// this rank's counter for the exchange and stores the new value into the
+// peers' flags; the wait kernel, next on the same stream, reads the counter
+// and polls for that value. Every rank makes the same calls, so the counters
+// move in lockstep.
+__global__ void p2p_signal_dev_kernel(PeerFlags f, int n, int* counter) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  const int e = *counter + 1;
+  *counter = e;
+  for (int i = 0; i < n; ++i)
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f.flag[i]), "r"(e) : "memory");
+}
+
+__global__ void p2p_wait_dev_kernel(const int* flags, int n, const int* counter) {
+  const int value = *reinterpret_cast<const volatile int*>(counter);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
+      if (v - value >= 0) break;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(&g_ek_status, kStatusWaitTimeout);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  __threadfence();
+}
+
 int read_status(int clear, int* v) {
   int rc = check_cuda(cudaMemcpyFromSymbol(v, g_ek_status, sizeof(int)), "read status");
   if (rc) return rc;
@@ -133,6 +167,29 @@ int ek_p2p_signal(void* const* flags, int n, int value, void* stream) {
   }
   p2p_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, n, value);
   return check_cuda(cudaGetLastError(), "p2p signal launch");
+}
+
+int ek_p2p_signal_dev(void* const* flags, int n, int* counter, void* stream) {
+  clear_error();
+  if (n < 0 || n > kMaxPeers || (n > 0 && !flags) || !counter)
+    return set_error(EK_ERR_INVALID, "p2p_signal_dev: 0..%d flags and a counter", kMaxPeers);
+  PeerFlags f{};
+  for (int i = 0; i < n; ++i) {
+    if (!flags[i] || (reinterpret_cast<uintptr_t>(flags[i]) & 3u))
+      return set_error(EK_ERR_INVALID, "p2p_signal_dev: flag %d is null or misaligned", i);
+    f.flag[i] = static_cast<int*>(flags[i]);
+  }
+  p2p_signal_dev_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, n, counter);
+  return check_cuda(cudaGetLastError(), "p2p signal launch");
+}
+
+int ek_p2p_wait_dev(const int* flags, int n, const int* counter, void* stream) {
+  clear_error();
+  if (n < 0 || n > kMaxPeers || (n > 0 && !flags) || !counter)
+    return set_error(EK_ERR_INVALID, "p2p_wait_dev: 0..%d flags and a counter", kMaxPeers);
+  if (n == 0) return EK_OK;
+  p2p_wait_dev_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(flags, n, counter);
+  return check_cuda(cudaGetLastError(), "p2p wait launch");
 }
 
 int ek_p2p_wait(const int* flags, int n, int value, void* stream) {

@@ -453,12 +453,17 @@ class ExpertParallelMoE:
         # yet, so they get every SM the caller's stream has)
         send, slot_row, Cg = self._dispatch_groups(x, gate_logits, groups)
         rows_g = self.world * Cg
+        # Cross-stream uses are recorded on the allocator (record_stream) in
+        # eager mode. Under CUDA-graph capture they are not needed: every
+        # tensor outlives its last use inside the captured layer, which ends
+        # joined back on the caller's stream.
+        track = piped and not torch.cuda.is_current_stream_capturing()
         if piped:
             cur = torch.cuda.current_stream(x.device)
             comm.wait_stream(cur)
             compute.wait_stream(cur)
             for t in send:
-                if t is not None:
+                if t is not None and track:
                     t.record_stream(comm)  # made on the caller's stream, sent from the comm stream
         with on(comm):
             recvs = []
@@ -476,7 +481,8 @@ class ExpertParallelMoE:
                     compute.wait_event(ev)
                     xr, ids_r, w_r = recv
                     for t in (xr if isinstance(xr, tuple) else (xr,)) + (ids_r, w_r):
-                        t.record_stream(compute)  # made on the comm stream, read here
+                        if track:
+                            t.record_stream(compute)  # made on the comm stream, read here
                 y = self._group_experts(recv, g * eg, (g + 1) * eg)
                 ev_y = None
                 if piped:
@@ -491,7 +497,8 @@ class ExpertParallelMoE:
             for g, (y, ev_y) in enumerate(ys):
                 if piped:
                     comm.wait_event(ev_y)
-                    y.record_stream(comm)  # made on the compute stream, sent from here
+                    if track:
+                        y.record_stream(comm)  # made on the compute stream, sent from here
                 if use_p2p:  # every group's results land in one buffer, group after group
                     self.p2p.all_to_all(y, ("y", groups, rows_g), part=g, parts=groups)
                 else:
@@ -500,7 +507,8 @@ class ExpertParallelMoE:
                 y_back = self.p2p.buffer_view(("y", groups, rows_g), y0.dtype, shape)
         if piped:
             cur.wait_stream(comm)
-            y_back.record_stream(cur)  # made on the comm stream, read here
+            if track:
+                y_back.record_stream(cur)  # made on the comm stream, read here
         # each token's k rows summed on the caller's stream, every SM again
         return self.ops.combine_rows(y_back, slot_row, T, self.topk)
 

@@ -39,12 +39,23 @@ _ALIGN = 256
 class P2PAllToAll:
     """Copy-engine all-to-all among the ranks of `group` (one GPU each, with
     peer access over NVLink). Construction is cheap; every method that maps
-    memory is collective."""
+    memory is collective.
 
-    def __init__(self, group=None):
+    device_epochs=True: the epochs live in device counters (one per key and
+    part) that the signal kernel increments, and every key has one buffer,
+    so a layer built on these exchanges can be captured in a CUDA graph and
+    replayed (a host-side epoch would be frozen into the graph). One buffer
+    is enough for the expert-parallel layer: a rank copies into a peer's
+    buffer for the next layer only after that peer has signalled the next
+    layer's dispatch, which it does after it has finished the previous one.
+    Every rank must use the same mode."""
+
+    def __init__(self, group=None, device_epochs: bool = False):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.device_epochs = bool(device_epochs)
+        self._nbuf = 1 if self.device_epochs else 2
         self._keys = {}
         self._opened = {}  # (peer, handle bytes) -> mapped base address
         self._closed = False
@@ -53,10 +64,12 @@ class P2PAllToAll:
         """Allocate this rank's arena for `key` (two buffers of `parts` parts of
         nbytes) and map every peer's."""
         lib = _lib.lib()
-        flag_bytes = 2 * parts * self.world * 4
+        nb = self._nbuf
+        # header: flags [buffer][part][peer], then (device epochs) a counter per part
+        flag_bytes = nb * parts * self.world * 4 + (parts * 4 if self.device_epochs else 0)
         data_off = -(-flag_bytes // _ALIGN) * _ALIGN
         buf_bytes = -(-nbytes // _ALIGN) * _ALIGN
-        arena = torch.zeros(data_off + 2 * parts * buf_bytes, dtype=torch.uint8, device=device)
+        arena = torch.zeros(data_off + nb * parts * buf_bytes, dtype=torch.uint8, device=device)
         base = ctypes.c_ulonglong()
         size = ctypes.c_size_t()
         _lib.check(lib.ek_p2p_mem_base(ctypes.c_void_p(arena.data_ptr()), ctypes.byref(base), ctypes.byref(size)),
@@ -108,12 +121,14 @@ class P2PAllToAll:
                                f"bytes, got {parts} x {nbytes}")
         if not 0 <= part < parts:
             raise RuntimeError("p2p all_to_all: part out of range")
+        if not self.device_epochs and torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("capturing p2p exchanges in a CUDA graph needs P2PAllToAll(device_epochs=True)")
         lib = _lib.lib()
         stream = ctypes.c_void_p(torch.cuda.current_stream(inp.device).cuda_stream)
         if part == 0:
             slot["epoch"] += 1
         e = slot["epoch"]
-        b = e % 2
+        b = e % self._nbuf
         blk = nbytes // self.world
         dbuf = slot["data_off"] + (b * parts + part) * slot["buf_bytes"]
         fbase = (b * parts + part) * self.world
@@ -124,10 +139,15 @@ class P2PAllToAll:
                                        ctypes.c_void_p(src + p * blk), blk, stream), "ek_p2p_copy")
         flags = (ctypes.c_void_p * self.world)(*[slot["peers"][p] + (fbase + self.rank) * 4
                                                  for p in range(self.world)])
-        _lib.check(lib.ek_p2p_signal(flags, self.world, e, stream), "ek_p2p_signal")
         arena = slot["arena"]
-        _lib.check(lib.ek_p2p_wait(ctypes.c_void_p(arena.data_ptr() + fbase * 4), self.world, e, stream),
-                   "ek_p2p_wait")
+        my_flags = ctypes.c_void_p(arena.data_ptr() + fbase * 4)
+        if self.device_epochs:
+            counter = ctypes.c_void_p(arena.data_ptr() + (parts * self.world + part) * 4)
+            _lib.check(lib.ek_p2p_signal_dev(flags, self.world, counter, stream), "ek_p2p_signal_dev")
+            _lib.check(lib.ek_p2p_wait_dev(my_flags, self.world, counter, stream), "ek_p2p_wait_dev")
+        else:
+            _lib.check(lib.ek_p2p_signal(flags, self.world, e, stream), "ek_p2p_signal")
+            _lib.check(lib.ek_p2p_wait(my_flags, self.world, e, stream), "ek_p2p_wait")
         return arena[dbuf:dbuf + nbytes].view(inp.dtype).view(inp.shape)
 
     def buffer_view(self, key, dtype, shape) -> torch.Tensor:
@@ -137,7 +157,7 @@ class P2PAllToAll:
         slot = self._keys[key]
         if slot["parts"] > 1 and slot["nbytes"] % _ALIGN:
             raise RuntimeError("buffer_view: parts are not contiguous (nbytes not a multiple of 256)")
-        b = slot["epoch"] % 2
+        b = slot["epoch"] % self._nbuf
         dbuf = slot["data_off"] + b * slot["parts"] * slot["buf_bytes"]
         n = slot["parts"] * slot["nbytes"]
         return slot["arena"][dbuf:dbuf + n].view(dtype).view(shape)

@@ -411,6 +411,13 @@ int ek_p2p_ipc_close(void* ptr);
 int ek_p2p_copy(void* dst, const void* src, size_t bytes, void* stream);
 int ek_p2p_signal(void* const* flags, int n, int value, void* stream);
 int ek_p2p_wait(const int* flags, int n, int value, void* stream);
+/* Device-side epochs, for exchanges replayed from a CUDA graph:
+ * ek_p2p_signal_dev increments the local int *counter and stores the new
+ * value into the n flags; ek_p2p_wait_dev (next on the same stream) waits
+ * until each of the n local flags holds a value >= *counter (bounded as
+ * ek_p2p_wait). */
+int ek_p2p_signal_dev(void* const* flags, int n, int* counter, void* stream);
+int ek_p2p_wait_dev(const int* flags, int n, const int* counter, void* stream);
 
 /* Top-k combine: out[t] = sum_{j<k} y[t*k + j] (fp32 sum in j order), bf16 out. */
 int ek_moe_combine(const void* y, void* out, int T, int topk, int H, void* stream);

@@ -273,6 +273,28 @@ def _worker(rank, world, port, q):
         if st:
             raise AssertionError(f"device status {st} after the copy-engine exchanges")
         px.close()
+        # device-side epochs: the grouped layer captured in a CUDA graph and
+        # replayed gives the eager layer's output, replay after replay
+        from elastikernel_b200.graph import Captured
+
+        pxd = P2PAllToAll(device_epochs=True)
+        moe_d = ExpertParallelMoE(E, K_TOP, qw=qw, capacity="auto", ops=CudaEPOps(num_sms=p_sms), p2p=pxd)
+        side = torch.cuda.Stream(dev)
+        with torch.cuda.stream(side):
+            eager = moe_d(xc, lc, groups=2, compute_stream=p_comp, comm_stream=p_comm)
+            cap = Captured(lambda: moe_d(xc, lc, groups=2, compute_stream=p_comp, comm_stream=p_comm), side)
+            for _ in range(3):
+                yg = cap()
+                side.synchronize()
+                if not torch.equal(yg, eager):
+                    raise AssertionError("graph-replayed EP layer differs from the eager one")
+        err_fp8 = max(err_fp8, max_rel_err(yg, refc.float().cpu().numpy()))
+        del cap
+        torch.cuda.synchronize()
+        st = _lib_status(dev)
+        if st:
+            raise AssertionError(f"device status {st} after the graph-replayed exchanges")
+        pxd.close()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
