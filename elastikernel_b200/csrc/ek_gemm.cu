@@ -140,6 +140,31 @@ Candidate evaluate_csplit(int M, int N, int K, int dtype, int bn, int cs, int ma
   return c;
 }
 
+// The same with CTA-pair tiles (256 x bn, gemm_csplit_pair_kernel): csp
+// pairs per cluster, each SM doing half of each 256-row MMA and loading half
+// of the B tile.
+Candidate evaluate_csplit_pair(int M, int N, int K, int dtype, int bn, int csp, int max_clusters) {
+  Machine mc;
+  Candidate c{1, bn, 1, 0, 0, 1e30, 0};
+  const int es = elem_bytes(dtype);
+  const int bk = 128 / es;
+  const int tiles = ((M + 255) / 256) * ((N + bn - 1) / bn);
+  const int kb = (K + bk - 1) / bk;
+  if (max_clusters <= 0 || tiles > max_clusters || kb / csp < 2) return c;
+  const double flops_clk = dtype == EK_DTYPE_E4M3 ? mc.f8_flops_clk : mc.f16_flops_clk;
+  const double mma_clk = 128.0 * bn * bk * 2.0 / flops_clk;
+  const double feed_clk = (128.0 + double(bn) / 2) * 128.0 / mc.feed_bytes_clk;
+  const double t_kb_us = std::max(mma_clk, feed_clk) / (mc.clk_ghz * 1e3);
+  const int slice_kb = (kb + csp - 1) / csp;
+  const double red_us = mc.csplit_fixed_us + 128.0 * bn * 4.0 / (mc.dsmem_gbs_per_sm * 1e3);
+  const double grid = double(tiles) * 2 * csp;
+  const double unique = (double(M) * K + double(K) * N) * es + double(M) * N * 2;
+  const double t_hbm = unique / (std::min(mc.hbm_gbs, grid * mc.hbm_per_sm_gbs) * 1e3);
+  c.est_us = std::max(slice_kb * t_kb_us + mc.csplit_fill_us, t_hbm) + red_us + mc.launch_us;
+  c.eff = double(kb) / (double(slice_kb) * csp);
+  return c;
+}
+
 // Clusters of cs CTAs (cs = 2, 4, 8) of the cluster-split kernel that the
 // current device holds at once, when num_sms is its full SM count; 0 when the
 // query is not possible (no device) or num_sms is a partition. Queried once
@@ -248,16 +273,27 @@ static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layo
   }
   // The cluster split (fewer tiles than SMs): taken when its estimate beats
   // the persistent schedule's by 2 %, or when force_split < 0 asks for it.
+  // force_split < 0 pins -force_split K slices; force_bn picks single CTAs (> 0)
+  // or CTA pairs (< 0) as for the persistent schedule.
   int best_cs = 0;
-  if (force_split <= 0 && force_bn >= 0) {
+  if (force_split <= 0) {
     for (int cs : {2, 4, 8}) {
       if (force_split < 0 && cs != -force_split) continue;
       for (int bn : {256, 128}) {
-        if (force_bn > 0 && bn != force_bn) continue;
-        Candidate c = evaluate_csplit(M, N, K, dtype, bn, cs, csplit_max_clusters(S, cs));
-        if (c.est_us < best.est_us * 0.98 || (force_split < 0 && best_cs == 0 && c.est_us < 1e29)) {
-          best = c;
-          best_cs = cs;
+        if (force_bn >= 0 && (force_bn == 0 || bn == force_bn)) {
+          Candidate c = evaluate_csplit(M, N, K, dtype, bn, cs, csplit_max_clusters(S, cs));
+          if (c.est_us < best.est_us * 0.98 || (force_split < 0 && best_cs == 0 && c.est_us < 1e29)) {
+            best = c;
+            best_cs = cs;
+          }
+        }
+        // pairs: a cluster of 2 * cs CTAs (at most 8)
+        if (cs <= 4 && force_bn <= 0 && (force_bn == 0 || bn == -force_bn)) {
+          Candidate c = evaluate_csplit_pair(M, N, K, dtype, bn, cs, csplit_max_clusters(S, 2 * cs));
+          if (c.est_us < best.est_us * 0.98 || (force_split < 0 && best_cs == 0 && c.est_us < 1e29)) {
+            best = c;
+            best_cs = cs;
+          }
         }
       }
     }
@@ -267,18 +303,19 @@ static int plan_dense_uncached(int M, int N, int K, int S, int dtype, int b_layo
   const int es = elem_bytes(dtype);
   ek_gemm_plan p{};
   if (best_cs > 0) {
-    p.bm = 128;
+    const int cc = best.pair ? 2 : 1;
+    p.bm = 128 * cc;
     p.bn = best.bn;
     p.bk = 128 / es;
-    p.cta_pair = 0;
-    p.tiles_m = (M + 127) / 128;
+    p.cta_pair = best.pair;
+    p.tiles_m = (M + p.bm - 1) / p.bm;
     p.tiles_n = (N + best.bn - 1) / best.bn;
     p.k_blocks = (K + p.bk - 1) / p.bk;
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.tail_split = 1;
     p.num_dp_tiles = p.num_tiles;
     p.num_units = p.num_tiles * best_cs;
-    p.grid = p.num_units;
+    p.grid = p.num_units * cc;
     p.num_sms = S;
     p.waves = 1;
     p.wave_efficiency = best.eff;
@@ -350,13 +387,20 @@ template <class Cfg>
 int launch_csplit(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& prm, int grid, int cs,
                   cudaStream_t stream) {
   constexpr int smem = CsplitLayout<Cfg>::SMEM_BYTES;
+  const int cluster = Cfg::kPair ? 2 * cs : cs;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return set_error(EK_ERR_CUDA, "device index out of range");
   if (!attr_done[dev]) {
-    int rc = check_cuda(cudaFuncSetAttribute(gemm_csplit_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                        "cudaFuncSetAttribute(cluster split)");
+    int rc = 0;
+    if constexpr (Cfg::kPair)
+      rc = check_cuda(cudaFuncSetAttribute(gemm_csplit_pair_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           smem),
+                      "cudaFuncSetAttribute(cluster split, pairs)");
+    else
+      rc = check_cuda(cudaFuncSetAttribute(gemm_csplit_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                      "cudaFuncSetAttribute(cluster split)");
     if (rc) return rc;
     attr_done[dev] = true;
   }
@@ -367,12 +411,16 @@ int launch_csplit(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.x = cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, gemm_csplit_kernel<Cfg>, ta, tb, prm), "cluster-split gemm launch");
+  if constexpr (Cfg::kPair)
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_csplit_pair_kernel<Cfg>, ta, tb, prm),
+                      "cluster-split pair gemm launch");
+  else
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_csplit_kernel<Cfg>, ta, tb, prm), "cluster-split gemm launch");
 }
 
 template <int kElem, bool kBMN, int kEpi>
@@ -380,6 +428,16 @@ int launch_mode(int pair, int bn, const CUtensorMap& ta, const CUtensorMap& tb, 
                 cudaStream_t stream, int cs = 0) {
   if (cs > 1) {
     if (cs != 2 && cs != 4 && cs != 8) return set_error(EK_ERR_INVALID, "cluster split of %d CTAs", cs);
+    if (pair) {
+      if (cs > 4) return set_error(EK_ERR_INVALID, "cluster split of %d CTA pairs", cs);
+      switch (bn) {
+        case 128:
+          return launch_csplit<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense, true>>(ta, tb, prm, grid, cs, stream);
+        case 256:
+          return launch_csplit<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense, true>>(ta, tb, prm, grid, cs, stream);
+      }
+      return set_error(EK_ERR_UNSUPPORTED, "cluster split with pairs and bn=%d not built", bn);
+    }
     switch (bn) {
       case 128: return launch_csplit<GemmCfg<128, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, cs, stream);
       case 256: return launch_csplit<GemmCfg<256, kElem, kBMN, kEpi, kSchedDense>>(ta, tb, prm, grid, cs, stream);

@@ -123,18 +123,22 @@ typedef struct ek_gemm_plan {
   double wave_efficiency;  /* useful K-steps / (grid * K-steps of busiest CTA)   */
   double est_us;           /* model estimate of the kernel time                  */
   size_t workspace_bytes;  /* scratch the schedule needs (split partials)        */
-  int cluster_split;       /* > 1: K split over a thread-block cluster of this  */
-                           /* many CTAs per 128 x bn tile, reduced through      */
-                           /* distributed shared memory (no workspace); grid =  */
-                           /* num_tiles * cluster_split; 0 = persistent schedule */
+  int cluster_split;       /* > 1: K split into this many slices per tile, one  */
+                           /* CTA (or, with cta_pair, one CTA pair) per slice,  */
+                           /* the slices of a tile forming one thread-block     */
+                           /* cluster and reduced through distributed shared    */
+                           /* memory (no workspace); grid = num_units * (1 or 2) */
+                           /* = num_tiles * cluster_split * (1 or 2);           */
+                           /* 0 = persistent schedule                           */
 } ek_gemm_plan;
 
 /* Plan a GEMM C[M,N] = A[M,K] * B on num_sms SMs (num_sms > 0 required here).
  * force_bn pins the tile: > 0 one CTA per 128 x force_bn tile (64/128/192/256),
  * < 0 a CTA pair per 256 x -force_bn tile (128/256), 0 = choose.
  * force_split > 0 pins the tail split of the persistent schedule, < 0 the
- * cluster split (-force_split = 2, 4 or 8 CTAs per tile; bn 128 or 256),
- * 0 = choose. The cluster split is offered on a device's full SM count only
+ * cluster split into -force_split K slices (2, 4 or 8 single CTAs, or with
+ * force_bn < 0 2 or 4 CTA pairs; bn 128 or 256), 0 = choose. The cluster
+ * split is offered on a device's full SM count only
  * (cluster placement inside a green-context partition is not known) and
  * when every cluster fits on the device at once. */
 int ek_gemm_plan_make(int M, int N, int K, int num_sms, int dtype, int b_layout, int force_bn, int force_split,

@@ -51,6 +51,26 @@ def test_cluster_split_forced(cuda_dev, cs, bn, layout):
     assert err <= TOL, f"cs={cs} bn={bn} {layout}: {err:.3e}"
 
 
+@pytest.mark.parametrize("csp", [2, 4])
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+def test_cluster_split_pairs_forced(cuda_dev, csp, bn, layout):
+    """CTA-pair tiles (256 x bn, 2-SM MMA) split over csp pairs of one
+    cluster; ragged M, N and K."""
+    from elastikernel_b200 import _ops
+
+    M, N, K = 500, 520, 2000
+    S = _full_sms(cuda_dev)
+    a, b, da, db = _inputs(M, N, K, torch.bfloat16, layout, cuda_dev, seed=csp * 7 + bn)
+    p = _ops.plan(M, N, K, S, torch.bfloat16, layout, -bn, -csp)
+    assert p["cluster_split"] == csp and p["cta_pair"] == 1 and p["bm"] == 256 and p["bn"] == bn
+    assert p["grid"] == p["num_tiles"] * csp * 2 and p["workspace_bytes"] == 0
+    c = _ops.gemm(da, db, num_sms=S, b_layout=layout, force_bn=-bn, force_split=-csp)
+    torch.cuda.synchronize()
+    err = max_rel_err(c, gemm_ref(a, b, layout))
+    assert err <= TOL, f"pairs csp={csp} bn={bn} {layout}: {err:.3e}"
+
+
 @pytest.mark.parametrize("M", [1, 77, 128, 256, 512])
 def test_small_m_default_plan(cuda_dev, M):
     """The M-sweep shapes N = K = 4096 at small M: the planner's choice (a
@@ -81,8 +101,8 @@ def test_cluster_split_fp16(cuda_dev):
     assert max_rel_err(c, gemm_ref(a, b, "nk")) <= TOL
 
 
-@pytest.mark.parametrize("cs", [2, 8])
-def test_cluster_split_fp8_scaled(cuda_dev, cs):
+@pytest.mark.parametrize("cs,bn", [(2, 256), (8, 256), (2, -256)])
+def test_cluster_split_fp8_scaled(cuda_dev, cs, bn):
     """e4m3 operands with per-row / per-channel scales applied after the
     cluster's reduction."""
     from elastikernel_b200 import _ops
@@ -95,7 +115,7 @@ def test_cluster_split_fp8_scaled(cuda_dev, cs):
     aq, a_s = _ops.quant_e4m3(a.to(cuda_dev))
     wq, w_s = _ops.quant_e4m3(w.to(cuda_dev))
     ref = gemm_fp8_ref(aq.cpu(), wq.cpu(), a_s.cpu(), w_s.cpu())
-    c = _ops.gemm_fp8(aq, wq, a_s, w_s, num_sms=S, force_bn=256, force_split=-cs)
+    c = _ops.gemm_fp8(aq, wq, a_s, w_s, num_sms=S, force_bn=bn, force_split=-cs)
     torch.cuda.synchronize()
     assert max_rel_err(c, ref) <= TOL_FP8
 
