@@ -553,7 +553,7 @@ def moe_ep_bench(dev, world: int, steps: int, peak_bf16_tflops: float, groups: i
     tf = flop / (ms * 1e-3) / 1e12
     peak_fp8 = 2.0 * peak_bf16_tflops
     return {"config": "DeepSeek-V3-shaped: E=256 top-8 H=7168 I=2048, e4m3 128x128 block scales, 4096 tokens/rank, "
-                      f"{eg} experts/rank, e4m3 dispatch via NCCL all-to-all",
+                      f"{eg} experts/rank, e4m3 dispatch and bf16 combine by all-to-all (path in 'exchange')",
             "n_gpus": world, "ms_per_layer": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1),
             "tflops_per_gpu": round(tf, 1), "gemm_partition_sms": gemm_sms, "comm_partition_sms": comm_sms,
             "pct_fp8_peak_scaled": round(100 * tf / (peak_fp8 * gemm_sms / 148), 1),
