@@ -849,7 +849,13 @@ def main() -> None:
     if "moe" in legs:
         extras["moe"] = moe_bench(dev, args.steps, hbm, peak_tf, cpu=(rank == 0 and world == 1 and "cpu" in legs))
     if "moe_ep" in legs:
-        extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
+        # An error in this leg is reported in its field; the GEMM line above
+        # it still prints (every rank takes the same collective steps unless
+        # the error is one rank's alone, which the process group's timeout ends).
+        try:
+            extras["moe_ep"] = moe_ep_bench(dev, world, args.steps, peak_tf)
+        except Exception as err:  # noqa: BLE001
+            extras["moe_ep"] = {"n_gpus": world, "error": f"{type(err).__name__}: {str(err)[:300]}"}
     if "triton" in legs and rank == 0 and world == 1 and args.triton_sms.strip():
         extras["triton_reference"] = triton_reference(dev, [int(x) for x in args.triton_sms.split(",")])
     if "cpu" in legs and rank == 0 and world == 1:
@@ -938,7 +944,9 @@ def summarize(line: dict) -> dict:
             sm["moe_cpu"] = {str(r["T"]): [r.get("vectorised_tokens_per_s"), r.get("loop_tokens_per_s")]
                              for r in moe["cpu"]["results"]}
     ep = line.get("moe_ep")
-    if ep:
+    if ep and "error" in ep:
+        sm["moe_ep"] = {"n_gpus": ep["n_gpus"], "error": ep["error"][:160]}
+    elif ep:
         sm["moe_ep"] = {"n_gpus": ep["n_gpus"], "ms": ep["ms_per_layer"], "tokens_per_s": ep["tokens_per_s"],
                         "pct_fp8_peak_scaled": ep["pct_fp8_peak_scaled"], "gemm_sms": ep["gemm_partition_sms"],
                         "ep_max_rel_err": [ep["ep_max_rel_err"], ep.get("ep_max_rel_err_act_e4m3")],

@@ -63,3 +63,16 @@ def test_summary_is_compact_and_complete():
     assert len(text) < 2600, len(text)
     assert set(s["partitions"]) == {"16", "32", "64", "96", "132", "148"}
     assert s["moe_ep"]["ep_max_rel_err"] == [0.011, 0.004] and "moe_cpu" in s and "fp8" in s and "m_sweep" in s
+
+
+def test_summary_reports_an_ep_leg_error():
+    """An expert-parallel leg that raised leaves an error field; the summary
+    carries it instead of failing on the missing measurements."""
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    line = {"value": 1400.0, "roofline": {"frac": 0.85}, "e2e": {"value": 99.0}, "clocks": {"sm_mhz": 1965.0},
+            "moe_ep": {"n_gpus": 8, "error": "RuntimeError: " + "x" * 400}}
+    s = bench.summarize(line)
+    assert s["moe_ep"]["n_gpus"] == 8 and s["moe_ep"]["error"].startswith("RuntimeError")
+    assert len(s["moe_ep"]["error"]) <= 160
